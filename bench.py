@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""Benchmark of the decode-step hot path.
+
+Workload: one decode token through a stack of 26 Gemma-2-2B-shape layers
+(hidden 2304, 8 Q / 4 KV heads, head_dim 256, FFN 2304->9216->2304, GeGLU)
+at batch 1 with a KV context of 4096, f16 weights N(0, 0.02), KV cache and
+input N(0, 1), seeded. A step = one token through all 26 layers (QKV with
+fused RMSNorm + KV write, split-KV flash-decode, o_proj + residual, fused
+gate/up GeGLU, down_proj + residual), replayed from one CUDA graph. The
+weights and caches of the stack (4.5 GB) are far larger than the 126 MB L2,
+so every step streams them from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+At N > 1 (torchrun, one process per GPU) every rank runs its own replica
+(the config-2 decode path at batch 1 does not shard);
+`value` is the tokens/s of all ranks together, timed as the max over ranks.
+Rank 0 prints one JSON line.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS = 26
+CTX = 4096
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", FALLBACK_BF16_TFLOPS)), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def metric_name():
+    return "Gemma-2-2B-shape decode tok/s (26-layer stack, batch 1, ctx 4096)"
+
+
+def config_dict(parallelism):
+    return {"workload": "config2: Gemma-2-2B-shape decode layer x%d, batch 1, KV ctx %d, f16" % (LAYERS, CTX),
+            "layers": LAYERS, "hidden": 2304, "q_heads": 8, "kv_heads": 4, "head_dim": 256, "ffn": 9216,
+            "global_batch": 1, "seq_len": CTX, "activation": "gelu_tanh (GeGLU)",
+            "l2": "inputs larger than L2 (weights + KV of the stack stream from HBM every step)",
+            "parallelism": parallelism}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.path = os.path.join("/tmp", "pc_clocks_%d_%d.csv" % (os.getpid(), device_index))
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port) — the reported baseline and the reference arm
+# ---------------------------------------------------------------------------
+
+def host_layer(seed=1234):
+    """One layer's weights / caches / input on the host in the oracle's layout."""
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(seed)
+    H, Nq, Nkv, Hd, F = 2304, 8, 4, 256, 9216
+
+    def w(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+
+    d = dict(x=rng.standard_normal((H,), dtype=np.float32).astype(np.float16),
+             w_attn_norm=(rng.standard_normal(H) * 0.1).astype(np.float32),
+             w_mlp_norm=(rng.standard_normal(H) * 0.1).astype(np.float32),
+             w_qkv=w((Nq + 2 * Nkv) * Hd, H), w_o=w(H, Nq * Hd), w_gate=w(F, H), w_up=w(F, H), w_down=w(H, F),
+             k_cache=rng.standard_normal((Nkv, CTX, Hd), dtype=np.float32).astype(np.float16),
+             v_cache=rng.standard_normal((Nkv, CTX, Hd), dtype=np.float32).astype(np.float16))
+    return d, oracle
+
+
+def time_cpu_layer(reps_min=1, budget_s=15.0, threads=None):
+    """Seconds per layer of the oracle decode layer on the host cores."""
+    d, oracle = host_layer()
+    if threads:
+        oracle.set_threads(threads)
+    cores = oracle.threads()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < reps_min or (time.perf_counter() < t_end and len(times) < 50):
+        t0 = time.perf_counter()
+        oracle.decode_layer(d["x"], "f16", d["w_attn_norm"], d["w_mlp_norm"], d["w_qkv"], d["w_o"], d["w_gate"],
+                            d["w_up"], d["w_down"], d["k_cache"], d["v_cache"], 8, 4, 256, CTX - 1)
+        times.append(time.perf_counter() - t0)
+    times.sort()
+    return times[len(times) // 2], cores, len(times)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    d, oracle = host_layer()
+    oracle.set_threads(os.cpu_count() or 1)
+    cores = oracle.threads()
+
+    def step():
+        oracle.decode_layer(d["x"], "f16", d["w_attn_norm"], d["w_mlp_norm"], d["w_qkv"], d["w_o"], d["w_gate"],
+                            d["w_up"], d["w_down"], d["k_cache"], d["v_cache"], 8, 4, 256, CTX - 1)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    tok_s = 1.0 / (dt * LAYERS)
+    sample = "each step: one of the %d layers (ctx %d) on the host; tok/s = 1 / (%d x layer time)" % (LAYERS, CTX,
+                                                                                                     LAYERS)
+    line = {"impl": "reference", "metric": metric_name(), "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1000.0,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV cache and input)",
+            "config": config_dict("cpu, %d threads" % cores),
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference = the C++ restatement of the reference's Metal kernels (oracle/); the Swift/Metal "
+                    "original cannot run on Linux"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    import popcorn_b200 as pc
+    from popcorn_b200 import _native as N
+    from popcorn_b200.decode import DecodeStack, LayerShape
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    shape = LayerShape(max_ctx=CTX, dtype="f16")
+    lib = pc.KernelLibrary(local)
+    stack = DecodeStack(lib, shape, LAYERS, seed=1234 + rank, device=local)
+    stream = torch.cuda.Stream(device=local)
+    pos = CTX - 1
+    hbm_gbs, _, peak_kind = peaks()
+
+    with torch.cuda.stream(stream):
+        stack.set_position(pos)
+        stack.x.normal_()
+        enc = stack.encoder(stream)
+        # eager run once (validates launches), then capture one step
+        stack.encode_step(enc)
+        torch.cuda.synchronize()
+        n0 = enc.dispatch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            stack.encode_step(enc)
+        launches_per_step = enc.dispatch_count - n0
+        torch.cuda.synchronize()
+
+        # ---- device-timed region: inputs resident in HBM ----
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        clocks = ClockSampler(local)
+        clocks.start()
+        time.sleep(0.3)
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        barrier()
+        t_start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = t_start.elapsed_time(t_end) / args.steps
+
+        # ---- end to end through the C ABI with host buffers ----
+        H = shape.H
+        host_in = torch.empty(H, dtype=torch.float16).pin_memory()
+        host_in.normal_()
+        host_pos = torch.tensor([pos, pos + 1], dtype=torch.int32).pin_memory()
+        host_out = torch.empty(H, dtype=torch.float16).pin_memory()
+        L = N.lib()
+        sptr = torch.cuda.current_stream().cuda_stream
+
+        def e2e_step():
+            L.pc_memcpy_htod_async(stack.x.data_ptr(), host_in.data_ptr(), H * 2, sptr)
+            L.pc_memcpy_htod_async(stack.pos_state.data_ptr(), host_pos.data_ptr(), 8, sptr)
+            graph.replay()
+            L.pc_memcpy_dtoh_async(host_out.data_ptr(), stack.out.data_ptr(), H * 2, sptr)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e_start.elapsed_time(e_end) / args.steps
+        clk = clocks.stop()
+        barrier()
+
+        # ---- per-kernel durations (eager steps, CUDA events via the dispatch hook) ----
+        events = {}
+        pending = []
+
+        def hook(name, phase, _stream):
+            if phase == 0:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                pending.append((name, ev))
+            else:
+                name0, ev0 = pending.pop()
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                events.setdefault(name0, []).append((ev0, ev))
+
+        enc.set_dispatch_hook(hook)
+        for _ in range(args.profile_steps):
+            stack.encode_step(enc)
+        torch.cuda.synchronize()
+        enc.set_dispatch_hook(None)
+        kern_ms = {n: sum(a.elapsed_time(b) for a, b in v) / len(v) for n, v in events.items()}
+        kern_n = {n: len(v) // args.profile_steps for n, v in events.items()}
+
+    # max over ranks of the timed step
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    s = shape
+    F, Hd = s.F, s.Hd
+    per_launch_bytes = {
+        "qkv_matvec_f16": (s.Nq + 2 * s.Nkv) * Hd * s.H * 2 + s.H * 2 + 2 * s.Nkv * Hd * 2 + s.Nq * Hd * 2,
+        "flash_decoding_partial_f16": s.kv_bytes(CTX) + s.Nq * Hd * 2,
+        "matvec_residual_f16": None,  # o_proj and down_proj share the name; split below
+        "geglu_matvec_f16": 2 * F * s.H * 2 + s.H * 2 + F * 2,
+    }
+    kernels = {}
+    for n, t in kern_ms.items():
+        b = per_launch_bytes.get(n)
+        if n == "matvec_residual_f16":
+            # average of o_proj (2304x2048) and down (2304x9216) launches
+            b = ((s.H * s.Nq * Hd + s.H * F) * 2) / 2
+        entry = {"ms": t, "launches_per_step": kern_n[n]}
+        if b:
+            entry["gbs"] = b / (t * 1e-3) / 1e9
+            entry["frac_of_measured_hbm"] = entry["gbs"] / hbm_gbs
+        kernels[n] = entry
+    dom = "geglu_matvec_f16"
+    dom_gbs = kernels.get(dom, {}).get("gbs")
+    fd = kernels.get("flash_decoding_partial_f16", {})
+
+    tok_s = world * 1000.0 / ms
+    e2e_tok_s = world * 1000.0 / e2e_ms
+    bytes_step = stack.algorithmic_bytes_per_step(CTX)
+    line = {
+        "metric": metric_name(), "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV cache and input)",
+        "config": config_dict("replicas" if world > 1 else "single GPU"),
+        "step_hbm_gbs": bytes_step / (ms * 1e-3) / 1e9,
+        "step_frac_of_measured_hbm": bytes_step / (ms * 1e-3) / 1e9 / hbm_gbs,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": dom_gbs, "peak": hbm_gbs, "unit": "GB/s",
+                     "frac": (dom_gbs / hbm_gbs) if dom_gbs else None, "peak_kind": peak_kind,
+                     "traffic": None,
+                     "algorithmic_bytes_per_launch": per_launch_bytes[dom]},
+        "flash_decode": {"kernel": "flash_decoding_partial_f16", "achieved_gbs": fd.get("gbs"),
+                         "frac_of_measured_hbm": fd.get("frac_of_measured_hbm"),
+                         "bytes_per_launch": per_launch_bytes["flash_decoding_partial_f16"]},
+        "kernels": kernels,
+        "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": H * 2 + 8, "d2h_bytes_per_step": H * 2,
+                "path": "pc_memcpy_htod_async (pinned host) -> graph of C-ABI kernels -> pc_memcpy_dtoh_async"},
+        "gpu_launches": launches_per_step * args.steps,
+        "launches_per_step": launches_per_step,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        t_layer, cores, reps = time_cpu_layer()
+        line["cpu_baseline"] = {"value": 1.0 / (t_layer * LAYERS), "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": "%d run(s) of one layer (ctx %d) of the oracle on the host, median; "
+                                          "tok/s = 1 / (%d x layer time)" % (reps, CTX, LAYERS)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,284 @@
+/*
+ * popcorn_cuda.h — C ABI of the B200 (sm_100a) decode-step kernel library.
+ *
+ * This is the drop-in boundary for finnvoor/Popcorn's decode path. A Swift
+ * module (module.modulemap over this header) re-backs Popcorn's public types
+ * with these calls; every entry point below names the reference interface
+ * it replaces (paths are inside the finnvoor/Popcorn source tree).
+ *
+ * Conventions
+ *  - Every function that can fail returns an int status: 0 (PC_OK) or one
+ *    of the negative PopcornError.Code values (Sources/Popcorn/
+ *    PopcornError.swift:23-42). The message of the last failure on the
+ *    calling thread is pc_last_error_message().
+ *  - Validation happens when a kernel object is created, before anything is
+ *    launched, as the reference's throwing initialisers do.
+ *  - The library never frees or retains caller memory. Tensors are plain
+ *    descriptors over caller-owned device pointers, bound at offset 0 with
+ *    contiguous row-major layout (Sources/Popcorn/Tensor.swift:5-22).
+ *  - Scratch memory always comes from the caller's allocator callbacks.
+ *  - Streams are cudaStream_t passed as void*; the library enqueues on the
+ *    caller's stream and never synchronises it (the caller owns submission,
+ *    as the Metal caller owns the command buffer).
+ */
+#ifndef POPCORN_CUDA_H
+#define POPCORN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PC_API __attribute__((visibility("default")))
+#define PC_MAX_RANK 8
+
+/* PopcornError.Code, Sources/Popcorn/PopcornError.swift:23-42. */
+typedef enum pc_status {
+    PC_OK = 0,
+    PC_ERR_CONSTANT_ALLOCATION_FAILED = -1001,
+    PC_ERR_TENSOR_ALLOCATION_FAILED = -1003,
+    PC_ERR_KERNEL_FUNCTION_NOT_FOUND = -1006,
+    PC_ERR_TENSOR_SHAPE_MISMATCH = -1007,
+    PC_ERR_TENSOR_INVALID_RANK = -1008,
+    PC_ERR_TENSOR_INVALID_AXIS = -1009,
+    PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION = -1010,
+    PC_ERR_WORKSPACE_EXHAUSTED = -1012,
+    PC_ERR_GPU_OUT_OF_MEMORY = -1013,
+    PC_ERR_GPU_TIMEOUT = -1014,
+    PC_ERR_GPU_PAGE_FAULT = -1015,
+    PC_ERR_GPU_INVALID_RESOURCE = -1016,
+    PC_ERR_GPU_DEVICE_REMOVED = -1017,
+    PC_ERR_GPU_ACCESS_REVOKED = -1018,
+    PC_ERR_GPU_INTERNAL = -1019
+} pc_status;
+
+/* Tensor.DataType, Sources/Popcorn/Tensor.swift:135-148 (same order). */
+typedef enum pc_dtype {
+    PC_U8 = 0, PC_U16 = 1, PC_U32 = 2, PC_U64 = 3,
+    PC_I8 = 4, PC_I16 = 5, PC_I32 = 6, PC_I64 = 7,
+    PC_F32 = 8, PC_F16 = 9, PC_BF16 = 10
+} pc_dtype;
+
+/* Tensor {buffer, shape, dataType}, Sources/Popcorn/Tensor.swift:5-22. */
+typedef struct pc_tensor {
+    void* data;      /* device pointer, bound at offset 0 */
+    int32_t dtype;   /* pc_dtype */
+    int32_t rank;    /* 0..PC_MAX_RANK */
+    int64_t shape[PC_MAX_RANK];
+} pc_tensor;
+
+/* Tensor.Access, Sources/Popcorn/Tensor.swift:182-199. */
+typedef enum pc_access { PC_ACCESS_READ = 1, PC_ACCESS_WRITE = 2, PC_ACCESS_READ_WRITE = 3 } pc_access;
+
+/* AttentionMask, Sources/Popcorn/Kernels/AttentionMask.swift:17-41. */
+typedef enum pc_mask_kind {
+    PC_MASK_CAUSAL = 0,
+    PC_MASK_CAUSAL_SLIDING_WINDOW = 1,
+    PC_MASK_BIDIRECTIONAL = 2
+} pc_mask_kind;
+typedef struct pc_attention_mask {
+    int32_t kind;    /* pc_mask_kind */
+    int32_t window;  /* sliding-window length; -1 when unused */
+} pc_attention_mask;
+
+/* ---- errors, sizes ------------------------------------------------------ */
+
+/* Message of the last failing call on this thread (PopcornError
+ * .errorDescription, PopcornError.swift:44-58). Never NULL. */
+PC_API const char* pc_last_error_message(void);
+/* Tensor.DataType.stride, Tensor.swift:152-159; 0 for an unknown dtype. */
+PC_API int pc_dtype_stride(int32_t dtype);
+/* ScratchSpec.byteCount = max(1, prod(shape) * stride), ScratchSpec.swift:23-25. */
+PC_API int64_t pc_scratch_spec_byte_count(const int64_t* shape, int32_t rank, int32_t dtype);
+/* Library version (major*10000 + minor*100 + patch). */
+PC_API int pc_version(void);
+
+/* ---- device memory (MTLDevice.makeBuffer counterpart for C callers) ----- */
+
+PC_API int pc_device_count(int* count);
+PC_API int pc_buffer_alloc(int device, size_t bytes, void** ptr);
+PC_API int pc_buffer_free(void* ptr);
+PC_API int pc_memcpy_htod_async(void* dst, const void* src, size_t bytes, void* stream);
+PC_API int pc_memcpy_dtoh_async(void* dst, const void* src, size_t bytes, void* stream);
+PC_API int pc_stream_synchronize(void* stream);
+/* Reads and clears the device-side error word of `device` (bit 0: a bounded
+ * wait inside a kernel gave up). 0 when clean. Synchronises the device. */
+PC_API int pc_device_error_check(int device, uint32_t* flags);
+
+/* ---- KernelLibrary (Sources/Popcorn/KernelLibrary.swift:4-41) ----------- */
+
+typedef struct pc_library pc_library;
+/* KernelLibrary(device:), KernelLibrary.swift:7-14. */
+PC_API int pc_library_create(int device, pc_library** out);
+PC_API void pc_library_destroy(pc_library* library);
+/* KernelLibrary.device, KernelLibrary.swift:18. */
+PC_API int pc_library_device(const pc_library* library, int* device);
+/* KernelLibrary.pipelineState(for:), KernelLibrary.swift:20-41: the same
+ * name always yields the same handle (cache identity); unknown names fail
+ * with PC_ERR_KERNEL_FUNCTION_NOT_FOUND (-1006). Thread-safe. */
+PC_API int pc_library_lookup(pc_library* library, const char* function_name, const void** handle);
+PC_API int pc_library_function_count(const pc_library* library);
+PC_API const char* pc_library_function_name(const pc_library* library, int index);
+
+/* ---- scratch protocol (Sources/Popcorn/KernelResources.swift:5-36) ------ */
+
+/* KernelScratchAllocator.borrowTemporaryBuffer(length:) / release. borrow
+ * returns 0 and a device pointer of at least `length` bytes, and sets
+ * *was_reused when the buffer may hold earlier writes in the same encoder
+ * (KernelTemporaryBuffer.wasReused, KernelResources.swift:14-20). A
+ * non-zero return aborts the encode with that status. release may be NULL;
+ * it runs when the composite kernel finishes encoding, before the GPU has
+ * run it — stream order protects reuse by later work on the same stream. */
+typedef struct pc_scratch_allocator {
+    void* ctx;
+    int (*borrow)(void* ctx, size_t length, void** ptr, int* was_reused);
+    void (*release)(void* ctx, void* ptr);
+} pc_scratch_allocator;
+
+/* ---- KernelCommandEncoder (Sources/Popcorn/KernelCommandEncoder.swift) --- */
+
+typedef struct pc_encoder pc_encoder;
+typedef struct pc_kernel pc_kernel;
+
+/* Phase of a dispatch hook call: Metal4DispatchPhase, KernelCommandEncoder.swift:243-246. */
+typedef enum pc_dispatch_phase { PC_WILL_DISPATCH = 0, PC_DID_DISPATCH = 1 } pc_dispatch_phase;
+typedef void (*pc_dispatch_hook)(void* ctx, const char* function_name, int phase, void* stream);
+
+/* KernelCommandEncoder(compute:library:scratch:), KernelCommandEncoder.swift:8-16.
+ * `stream` is a cudaStream_t (NULL = legacy default stream). `scratch` is
+ * copied; it may be NULL when only non-composite kernels are encoded. */
+PC_API int pc_encoder_create(pc_library* library, void* stream, const pc_scratch_allocator* scratch,
+                             pc_encoder** out);
+PC_API void pc_encoder_destroy(pc_encoder* encoder);
+/* encode(_:), KernelCommandEncoder.swift:39-47. */
+PC_API int pc_encoder_encode(pc_encoder* encoder, const pc_kernel* kernel);
+/* barrier(), KernelCommandEncoder.swift:71-85: clears the access map. On one
+ * CUDA stream launches are already ordered, so no GPU work is enqueued. */
+PC_API int pc_encoder_barrier(pc_encoder* encoder);
+/* Barriers inserted so far (explicit + hazard-driven, :155-168). */
+PC_API int64_t pc_encoder_barrier_count(const pc_encoder* encoder);
+/* Kernel launches enqueued so far. */
+PC_API int64_t pc_encoder_dispatch_count(const pc_encoder* encoder);
+/* metal4DispatchHook, KernelCommandEncoder.swift:29-37,237-239. */
+PC_API int pc_encoder_set_dispatch_hook(pc_encoder* encoder, pc_dispatch_hook hook, void* ctx);
+PC_API int pc_encoder_stream(const pc_encoder* encoder, void** stream);
+
+/* ---- kernel objects (Sources/Popcorn/Kernel.swift:15-70) ----------------- */
+
+PC_API void pc_kernel_destroy(pc_kernel* kernel);
+/* Operation name ("FlashAttention", "KVCacheWrite", ...). */
+PC_API const char* pc_kernel_name(const pc_kernel* kernel);
+/* Kernel.tensors, Kernel.swift:17-19: the user-visible bindings. */
+PC_API int pc_kernel_binding_count(const pc_kernel* kernel);
+PC_API int pc_kernel_binding(const pc_kernel* kernel, int index, pc_tensor* tensor, int* access);
+/* Function names this kernel will launch, ';'-separated (route visible). */
+PC_API const char* pc_kernel_function_names(const pc_kernel* kernel);
+
+/* FlashAttention.Path, FlashAttention.swift:94-98 + route(sq:hd:supportsMPP:)
+ * :109-113. On B200 the tensor-core prefill kernel plays the MPP role. */
+typedef enum pc_attention_path { PC_PATH_PLAIN = 0, PC_PATH_TENSOR = 1, PC_PATH_DECODING = 2 } pc_attention_path;
+PC_API int pc_flash_attention_route(int64_t query_len, int64_t head_dim, int32_t dtype);
+
+/* Kernels.FlashAttention(q:k:v:into:scale:mask:), FlashAttention.swift:51-90.
+ * q [B,Nq,Sq,Hd], k/v [B,Nkv,Sk,Hd], out [B,Nq,Sq,Hd]. Sq == 1 routes to
+ * split-KV FlashDecoding (FlashDecoding.swift:6-90), which borrows its
+ * partial (m, l, O) scratch from the encoder's allocator. */
+PC_API int pc_kernel_flash_attention(const pc_tensor* q, const pc_tensor* k, const pc_tensor* v,
+                                     const pc_tensor* out, float scale, pc_attention_mask mask,
+                                     pc_kernel** kernel);
+/* Explicit-dimension form, FlashAttention.swift:13-49. */
+PC_API int pc_kernel_flash_attention_dims(const pc_tensor* q, const pc_tensor* k, const pc_tensor* v,
+                                          const pc_tensor* out, int64_t batch, int64_t query_heads,
+                                          int64_t kv_heads, int64_t query_len, int64_t key_len,
+                                          int64_t head_dim, float scale, pc_attention_mask mask,
+                                          pc_kernel** kernel);
+/* Extension (no reference counterpart; the reference shares Sk across the
+ * batch, FlashDecoding.metal:55-58): decode attention over a KV cache
+ * [B,Nkv,Smax,Hd] with per-sequence key counts seq_lens (int32 [B] on the
+ * device, 0 <= len <= Smax). Equals FlashDecoding run per sequence on the
+ * compact slice [1,Nkv,len,Hd] with the query at position len-1. A
+ * sequence with len 0 yields zeros. */
+PC_API int pc_kernel_flash_decoding_ragged(const pc_tensor* q, const pc_tensor* k_cache,
+                                           const pc_tensor* v_cache, const pc_tensor* seq_lens,
+                                           const pc_tensor* out, float scale, pc_attention_mask mask,
+                                           pc_kernel** kernel);
+
+/* Kernels.KVCacheWrite(source:cache:offset:), KVCacheWrite.swift:38-49.
+ * source [B,Nkv,Snew,Hd] into cache [B,Nkv,Smax,Hd] at `offset`.
+ * Dtypes (source, cache): f32/f32, bf16/bf16, f32/bf16 (reference), f16/f16
+ * (extension). Bit-exact copy, or RNE for f32 -> bf16. */
+PC_API int pc_kernel_kv_cache_write(const pc_tensor* source, const pc_tensor* cache, int64_t offset,
+                                    pc_kernel** kernel);
+/* Explicit-dimension form, KVCacheWrite.swift:8-36. */
+PC_API int pc_kernel_kv_cache_write_dims(const pc_tensor* source, const pc_tensor* cache, int64_t batch,
+                                         int64_t kv_heads, int64_t new_len, int64_t max_len,
+                                         int64_t head_dim, int64_t offset, pc_kernel** kernel);
+
+/* Kernels.RMSNorm(_:weight:into:axis:eps:addOneToWeight:), RMSNorm.swift:39-70.
+ * weight may be NULL; when present it is f32 [H] (RMSNorm.metal:44-46). */
+PC_API int pc_kernel_rmsnorm(const pc_tensor* x, const pc_tensor* weight, const pc_tensor* out, int32_t axis,
+                             float eps, int32_t add_one_to_weight, pc_kernel** kernel);
+/* Explicit-dimension form, RMSNorm.swift:10-37. */
+PC_API int pc_kernel_rmsnorm_dims(const pc_tensor* x, const pc_tensor* weight, const pc_tensor* out,
+                                  int64_t row_count, int64_t hidden_size, float eps,
+                                  int32_t add_one_to_weight, pc_kernel** kernel);
+
+/* Kernels.Matmul(_:_:into:transposeB:), Matmul.swift:68-93. a [M,K],
+ * b [N,K] (transposeB) or [K,N], c [M,N]. M == 1 routes to the matvec
+ * (Matmul.swift:22-32). */
+PC_API int pc_kernel_matmul(const pc_tensor* a, const pc_tensor* b, const pc_tensor* c, int32_t transpose_b,
+                            pc_kernel** kernel);
+/* Explicit-dimension form, Matmul.swift:9-66. */
+PC_API int pc_kernel_matmul_dims(const pc_tensor* a, const pc_tensor* b, const pc_tensor* c, int64_t m,
+                                 int64_t k, int64_t n, int32_t transpose_b, pc_kernel** kernel);
+
+/* Kernels.GeluTanh(_:into:), GeluTanh.swift:8-26. */
+PC_API int pc_kernel_gelu_tanh(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel);
+/* Kernels.Mul(_:_:into:), Mul.swift. */
+PC_API int pc_kernel_mul(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel);
+/* Kernels.Add(_:_:into:), Add.swift. */
+PC_API int pc_kernel_add(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel);
+/* Extension: SiLU, silu(g) = g / (1 + exp(-g)) (no reference kernel). */
+PC_API int pc_kernel_silu(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel);
+
+/* ---- fused decode ops (extensions; each equals a reference op sequence) -- */
+
+/* out = Matmul(RMSNorm(x, norm_weight, eps, add_one), w, transposeB) for
+ * x [1,K]: the RMSNorm output is rounded to x's dtype before the product,
+ * as the unfused pair stores it (RMSNorm.metal:36, Matvec.metal:92). */
+PC_API int pc_kernel_rmsnorm_matmul(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                    int32_t add_one_to_weight, const pc_tensor* w, const pc_tensor* out,
+                                    pc_kernel** kernel);
+/* Gated MLP up half: out = act(W_gate xn) * (W_up xn), xn = RMSNorm(x) when
+ * norm_weight is given (else xn = x), with each intermediate rounded to the
+ * activation dtype as GeluTanh/Mul store them (Gemma4TextInference.swift:
+ * 424-429). act: 0 = GeluTanh (GeGLU), 1 = SiLU (SwiGLU). x [1,K],
+ * w_gate/w_up [F,K], out [1,F]. */
+typedef enum pc_activation { PC_ACT_GELU_TANH = 0, PC_ACT_SILU = 1 } pc_activation;
+PC_API int pc_kernel_gated_mlp(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                               int32_t add_one_to_weight, const pc_tensor* w_gate, const pc_tensor* w_up,
+                               int32_t activation, const pc_tensor* out, pc_kernel** kernel);
+/* out = residual + Matmul(a, w, transposeB) for a [1,K]: the product is
+ * rounded to the output dtype before the add, as Matmul then Add store it
+ * (Gemma4TextInference.swift:401-404, 431-434). */
+PC_API int pc_kernel_matmul_residual(const pc_tensor* a, const pc_tensor* w, const pc_tensor* residual,
+                                     const pc_tensor* out, pc_kernel** kernel);
+/* QKV projection of one decode token with the KV-cache write fused:
+ * qkv = Matmul(RMSNorm(x), w_qkv) for w_qkv [(Nq+2Nkv)*Hd, K]; the q part
+ * goes to q_out [1,Nq,1,Hd]; the k and v parts are written to the caches
+ * [1,Nkv,Smax,Hd] at position `offset`, exactly as KVCacheWrite would
+ * store them (KVCacheWrite.metal:17-26). The position is `offset`, or, when
+ * `position` (int32 [1] on the device) is given, the value it holds when the
+ * kernel runs — so one captured CUDA graph can serve every decode step. */
+PC_API int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                    int32_t add_one_to_weight, const pc_tensor* w_qkv, const pc_tensor* q_out,
+                                    const pc_tensor* k_cache, const pc_tensor* v_cache, int64_t offset,
+                                    const pc_tensor* position, pc_kernel** kernel);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPCORN_CUDA_H */

@@ -1,0 +1,116 @@
+"""ctypes binding of ``libpopcorn_cuda.so`` (the C ABI in include/popcorn_cuda.h).
+
+The library is the product; this module only declares its signatures. It
+fails loudly when the library has not been built: there is no fallback.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libpopcorn_cuda.so")
+HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "popcorn_cuda.h")
+
+PC_MAX_RANK = 8
+
+
+class pc_tensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * PC_MAX_RANK)]
+
+
+class pc_attention_mask(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("window", ctypes.c_int32)]
+
+
+BORROW_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
+                             ctypes.POINTER(ctypes.c_int))
+RELEASE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_void_p)
+HOOK_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p)
+
+
+class pc_scratch_allocator(ctypes.Structure):
+    _fields_ = [("ctx", ctypes.c_void_p), ("borrow", BORROW_FN), ("release", RELEASE_FN)]
+
+
+_lib = None
+
+
+def lib():
+    """Loads the CUDA library once; raises ImportError if it is missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError("popcorn_b200: %s is missing; build it with `python -c \"import __graft_entry__ as g; "
+                              "g.build()\"` (nvcc, sm_100a)" % LIB_PATH)
+        L = ctypes.CDLL(LIB_PATH)
+        _declare(L)
+        _lib = L
+    return _lib
+
+
+def _declare(L):
+    P, I, I32, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+    T = ctypes.POINTER(pc_tensor)
+    PP = ctypes.POINTER(ctypes.c_void_p)
+    M = pc_attention_mask
+    sig = {
+        "pc_last_error_message": ([], ctypes.c_char_p),
+        "pc_dtype_stride": ([I32], I),
+        "pc_scratch_spec_byte_count": ([ctypes.POINTER(I64), I32, I32], I64),
+        "pc_version": ([], I),
+        "pc_device_count": ([ctypes.POINTER(I)], I),
+        "pc_buffer_alloc": ([I, ctypes.c_size_t, PP], I),
+        "pc_buffer_free": ([P], I),
+        "pc_memcpy_htod_async": ([P, P, ctypes.c_size_t, P], I),
+        "pc_memcpy_dtoh_async": ([P, P, ctypes.c_size_t, P], I),
+        "pc_stream_synchronize": ([P], I),
+        "pc_device_error_check": ([I, ctypes.POINTER(ctypes.c_uint32)], I),
+        "pc_library_create": ([I, PP], I),
+        "pc_library_destroy": ([P], None),
+        "pc_library_device": ([P, ctypes.POINTER(I)], I),
+        "pc_library_lookup": ([P, ctypes.c_char_p, PP], I),
+        "pc_library_function_count": ([P], I),
+        "pc_library_function_name": ([P, I], ctypes.c_char_p),
+        "pc_encoder_create": ([P, P, ctypes.POINTER(pc_scratch_allocator), PP], I),
+        "pc_encoder_destroy": ([P], None),
+        "pc_encoder_encode": ([P, P], I),
+        "pc_encoder_barrier": ([P], I),
+        "pc_encoder_barrier_count": ([P], I64),
+        "pc_encoder_dispatch_count": ([P], I64),
+        "pc_encoder_set_dispatch_hook": ([P, HOOK_FN, P], I),
+        "pc_encoder_stream": ([P, PP], I),
+        "pc_kernel_destroy": ([P], None),
+        "pc_kernel_name": ([P], ctypes.c_char_p),
+        "pc_kernel_binding_count": ([P], I),
+        "pc_kernel_binding": ([P, I, T, ctypes.POINTER(I)], I),
+        "pc_kernel_function_names": ([P], ctypes.c_char_p),
+        "pc_flash_attention_route": ([I64, I64, I32], I),
+        "pc_kernel_flash_attention": ([T, T, T, T, F, M, PP], I),
+        "pc_kernel_flash_attention_dims": ([T, T, T, T, I64, I64, I64, I64, I64, I64, F, M, PP], I),
+        "pc_kernel_flash_decoding_ragged": ([T, T, T, T, T, F, M, PP], I),
+        "pc_kernel_kv_cache_write": ([T, T, I64, PP], I),
+        "pc_kernel_kv_cache_write_dims": ([T, T, I64, I64, I64, I64, I64, I64, PP], I),
+        "pc_kernel_rmsnorm": ([T, T, T, I32, F, I32, PP], I),
+        "pc_kernel_rmsnorm_dims": ([T, T, T, I64, I64, F, I32, PP], I),
+        "pc_kernel_matmul": ([T, T, T, I32, PP], I),
+        "pc_kernel_matmul_dims": ([T, T, T, I64, I64, I64, I32, PP], I),
+        "pc_kernel_gelu_tanh": ([T, T, PP], I),
+        "pc_kernel_mul": ([T, T, T, PP], I),
+        "pc_kernel_add": ([T, T, T, PP], I),
+        "pc_kernel_silu": ([T, T, PP], I),
+        "pc_kernel_rmsnorm_matmul": ([T, T, F, I32, T, T, PP], I),
+        "pc_kernel_gated_mlp": ([T, T, F, I32, T, T, I32, T, PP], I),
+        "pc_kernel_matmul_residual": ([T, T, T, T, PP], I),
+        "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def header_symbols():
+    """Names of every function include/popcorn_cuda.h declares (PC_API)."""
+    import re
+    text = open(HEADER_PATH).read()
+    return sorted(set(re.findall(r"PC_API\s+[^;(]*?\b(pc_\w+)\s*\(", text)))

@@ -1,0 +1,719 @@
+// flash_decoding.cu — split-KV GQA decode attention (Sq = 1) for sm_100a.
+//
+// Semantics (FlashDecoding.metal:29-231): per (b, hq) the query at position
+// len-1 attends to keys [0, len) of KV head hkv = hq*Nkv/Nq (:56); q is
+// pre-scaled (:66); softmax uses natural exp (computed here as exp2 of
+// log2e-scaled scores, the same function); the key range is split into
+// partitions whose unnormalised (m, l, O) are merged by a log-sum-exp combine
+// (:182-231). Sliding-window masks keep keys with posQ - j < window (:97-99).
+//
+// B200 design.
+//  * One CTA per (b, KV head, head group, split): the G query heads that
+//    share a KV head are served from ONE read of their K/V rows (the
+//    reference re-reads K/V once per query head).
+//  * K and V tiles of 32 keys stream HBM -> shared memory with the Blackwell
+//    bulk-copy engine (cp.async.bulk, 1-D, no multicast) into a 2-4 stage
+//    ring tracked by mbarriers; one elected thread issues the copies, so
+//    the SM's warps only compute while up to 96 KB per CTA is in flight.
+//  * Each warp scores 8 keys per tile: lanes hold Hd/32 contiguous head
+//    dims (one 16-byte shared load per key row at Hd 256, conflict-free),
+//    then a transpose-reduction folds the 8 x G partial dots across the warp
+//    in 9G shuffles instead of 40G.
+//  * The split count is chosen so the grid fills every SM; a second small
+//    kernel merges the splits (skipped when one split covers the keys).
+//  * Every mbarrier wait is bounded; a wait that gives up sets a device
+//    error word (pc_device_error_check) and the CTA drains its copies and
+//    leaves.
+#include <algorithm>
+
+#include "common.cuh"
+#include "dtype.cuh"
+#include "launch.hpp"
+#include "popcorn.hpp"
+
+namespace popcorn {
+
+__device__ unsigned int g_fd_error_word;
+
+namespace launch {
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = 4;
+constexpr int kTileKeys = 32;  // 8 keys per warp per tile
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---- mbarrier / bulk-copy primitives -------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: ~20k suspended tries of <= 0.1 ms each.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < 20000; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_fd_error_word, 1u);
+    return false;
+}
+
+// ---- lane slice loads ----------------------------------------------------------
+
+// E consecutive elements of a row (in shared memory) -> floats.
+template <class KV, int E>
+__device__ __forceinline__ void load_slice(const char* p, float* f) {
+    if constexpr (Elem<KV>::bytes == 2) {
+        if constexpr (E == 2) {
+            float2 a = unpack2<KV>(*reinterpret_cast<const uint32_t*>(p));
+            f[0] = a.x; f[1] = a.y;
+        } else if constexpr (E == 4) {
+            uint2 v = *reinterpret_cast<const uint2*>(p);
+            float2 a = unpack2<KV>(v.x), b = unpack2<KV>(v.y);
+            f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+        } else {
+#pragma unroll
+            for (int c = 0; c < E / 8; ++c) unpack8<KV>(reinterpret_cast<const uint4*>(p)[c], f + 8 * c);
+        }
+    } else {
+        if constexpr (E == 2) {
+            float2 a = *reinterpret_cast<const float2*>(p);
+            f[0] = a.x; f[1] = a.y;
+        } else {
+#pragma unroll
+            for (int c = 0; c < E / 4; ++c) {
+                float4 a = reinterpret_cast<const float4*>(p)[c];
+                f[4 * c] = a.x; f[4 * c + 1] = a.y; f[4 * c + 2] = a.z; f[4 * c + 3] = a.w;
+            }
+        }
+    }
+}
+
+template <class KV, int HD>
+struct FDShape {
+    static constexpr int E = HD / 32;
+    static constexpr int kRowBytes = HD * Elem<KV>::bytes;
+    static constexpr int kTileBytes = kTileKeys * kRowBytes;  // one of K or V
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kStages = (2 * kStageBytes > 200 * 1024) ? 1 : std::max(2, std::min(4, 98304 / kStageBytes));
+};
+
+template <int G, int HD>
+constexpr int merge_bytes() {
+    return kWarps * G * (HD + 2) * 4;
+}
+
+template <class KV, int HD, int G>
+constexpr size_t fd_smem_bytes() {
+    using S = FDShape<KV, HD>;
+    size_t ring = size_t(S::kStages) * S::kStageBytes;
+    size_t merge = size_t(merge_bytes<G, HD>());
+    return ring > merge ? ring : merge;
+}
+
+struct FDArgs {
+    FlashDecode p;
+    int splits;
+    int64_t chunk;
+    int G;        // query heads per CTA
+    int hgroups;  // head groups per KV head
+    float* po;
+    float* pm;
+    float* pl;
+};
+
+// Key range [jb, je) of this CTA's split for sequence length len.
+__device__ __forceinline__ void split_range(const FDArgs& a, int64_t len, int split, int64_t& jb, int64_t& je) {
+    jb = int64_t(split) * a.chunk;
+    je = jb + a.chunk;
+    if (je > len) je = len;
+    if (a.p.mask_kind == 1 && a.p.window > 0) {
+        int64_t lo = len - a.p.window;  // keys with posQ - j < window
+        if (jb < lo) jb = lo;
+    }
+}
+
+// Writes this CTA's (m, l, O) for heads hq0..hq0+G-1, or the normalised
+// output when the plan has a single split.
+template <int G, int HD>
+__device__ __forceinline__ void write_result(const FDArgs& a, int64_t b, int64_t hq0, int split, const float* mm,
+                                             const float* ll, const float* oo, int tid) {
+    const FlashDecode& p = a.p;
+    for (int idx = tid; idx < G * HD; idx += kThreads) {
+        int g = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * G + g]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                float mw = mm[w * G + g];
+                float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+                L += f * ll[w * G + g];
+                O += f * oo[(w * G + g) * HD + d];
+            }
+        }
+        int64_t hq = hq0 + g;
+        if (a.splits == 1) {
+            float r = L > 0.f ? O * (1.0f / L) : 0.f;
+            int64_t o = (b * p.Nq + hq) * HD + d;
+            if (p.out_dtype == PC_F32) Elem<TF32>::store(p.out, o, r);
+            else if (p.out_dtype == PC_BF16) Elem<TBF16>::store(p.out, o, r);
+            else Elem<TF16>::store(p.out, o, r);
+        } else {
+            int64_t slot = (b * p.Nq + hq) * a.splits + split;
+            a.po[slot * HD + d] = O;
+            if (d == 0) {
+                a.pm[slot] = M;
+                a.pl[slot] = L;
+            }
+        }
+    }
+}
+
+template <class KV, int HD, int G>
+__global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
+    using S = FDShape<KV, HD>;
+    constexpr int E = S::E;
+    constexpr int NST = S::kStages;
+    extern __shared__ __align__(128) char smem[];
+    __shared__ __align__(8) uint64_t bars[4];
+
+    pdl_launch_dependents();
+    const FlashDecode& p = a.p;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.x;
+    const int64_t hkv = blockIdx.y / a.hgroups;
+    const int hg = blockIdx.y % a.hgroups;
+    const int64_t b = blockIdx.z;
+    const int64_t gtot = p.Nq / p.Nkv;
+    const int64_t hq0 = hkv * gtot + int64_t(hg) * G;
+
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) mbar_init(smem_addr(&bars[s]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    pdl_wait();  // q, the cache and seq_lens may come from the previous kernel
+
+    const int64_t len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
+    int64_t jb, je;
+    split_range(a, len, split, jb, je);
+
+    float* mm = reinterpret_cast<float*>(smem);
+    float* ll = mm + kWarps * G;
+    float* oo = ll + kWarps * G;
+
+    if (jb >= je) {  // no keys for this split (FlashDecoding.metal:78-87)
+        if (tid < kWarps * G) {
+            mm[tid] = -INFINITY;
+            ll[tid] = 0.f;
+        }
+        for (int i = tid; i < kWarps * G * HD; i += kThreads) oo[i] = 0.f;
+        __syncthreads();
+        write_result<G, HD>(a, b, hq0, split, mm, ll, oo, tid);
+        return;
+    }
+
+    const int64_t head_off = (b * p.Nkv + hkv) * p.S * HD;  // elements
+    const char* kbase = static_cast<const char*>(p.k) + head_off * Elem<KV>::bytes;
+    const char* vbase = static_cast<const char*>(p.v) + head_off * Elem<KV>::bytes;
+    const int ntiles = int((je - jb + kTileKeys - 1) / kTileKeys);
+
+    auto issue = [&](int t) {
+        int s = t % NST;
+        int64_t j0 = jb + int64_t(t) * kTileKeys;
+        int64_t nk = je - j0 < kTileKeys ? je - j0 : kTileKeys;
+        uint32_t bytes = uint32_t(nk) * S::kRowBytes;
+        uint32_t bar = smem_addr(&bars[s]);
+        mbar_expect_tx(bar, 2 * bytes);
+        char* st = smem + size_t(s) * S::kStageBytes;
+        bulk_g2s(smem_addr(st), kbase + j0 * S::kRowBytes, bytes, bar);
+        bulk_g2s(smem_addr(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
+    };
+    if (tid == 0)
+        for (int t = 0; t < NST && t < ntiles; ++t) issue(t);
+
+    // Query slices (pre-scaled, in log2 units) for the G heads.
+    float q[G][E];
+    const float qs = p.scale * kLog2e;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        int64_t qb = ((b * p.Nq) + hq0 + g) * HD + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) q[g][e] = Elem<KV>::load(p.q, qb + e) * qs;
+    }
+
+    float m[G], l[G], o[G][E];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[g][e] = 0.f;
+    }
+
+    bool bad = false;
+    for (int t = 0; t < ntiles; ++t) {
+        const int s = t % NST;
+        const uint32_t parity = uint32_t(t / NST) & 1u;
+        if (!mbar_wait(smem_addr(&bars[s]), parity)) bad = true;
+        bad = __syncthreads_or(bad);
+        if (bad) break;
+
+        const int64_t j0 = jb + int64_t(t) * kTileKeys;
+        const int nk = int(je - j0 < kTileKeys ? je - j0 : kTileKeys);
+        const int kw0 = warp * 8;  // this warp's first key in the tile
+        const char* ktile = smem + size_t(s) * S::kStageBytes;
+        const char* vtile = ktile + S::kTileBytes;
+
+        if (kw0 < nk) {
+            // Partial dots: vals[i*G + g] for the warp's 8 keys.
+            float vals[8 * G];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float kf[E];
+                if (kw0 + i < nk) {
+                    load_slice<KV, E>(ktile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, kf);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) kf[e] = 0.f;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc = fmaf(q[g][e], kf[e], acc);
+                    vals[i * G + g] = acc;
+                }
+            }
+            // Transpose-reduction: after the xor-16/8/4 steps lane L holds
+            // the partial sums of key (L >> 2) & 7; xor-2/1 finish them.
+            {
+                const bool hi = lane & 16;
+#pragma unroll
+                for (int i = 0; i < 4 * G; ++i) {
+                    float lo_v = vals[i], hi_v = vals[i + 4 * G];
+                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+            }
+            {
+                const bool hi = lane & 8;
+#pragma unroll
+                for (int i = 0; i < 2 * G; ++i) {
+                    float lo_v = vals[i], hi_v = vals[i + 2 * G];
+                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+            }
+            {
+                const bool hi = lane & 4;
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    float lo_v = vals[i], hi_v = vals[i + G];
+                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                }
+            }
+            const int my_key = (lane >> 2) & 7;
+            const bool valid = kw0 + my_key < nk;
+            float pr[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float sv = vals[g];
+                sv += __shfl_xor_sync(0xffffffffu, sv, 2);
+                sv += __shfl_xor_sync(0xffffffffu, sv, 1);
+                float mx = valid ? sv : -INFINITY;
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                float mnew = fmaxf(m[g], mx);
+                float so = exp2f(m[g] - mnew);  // 0 while m is -inf
+                float pv = valid ? exp2f(sv - mnew) : 0.f;
+                float ps = pv;
+                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[g] = l[g] * so + ps;
+                m[g] = mnew;
+#pragma unroll
+                for (int e = 0; e < E; ++e) o[g][e] *= so;
+                pr[g] = pv;
+            }
+            // O += p_i * V_i over the warp's keys.
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float pi[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) pi[g] = __shfl_sync(0xffffffffu, pr[g], i * 4);
+                if (kw0 + i < nk) {
+                    float vf[E];
+                    load_slice<KV, E>(vtile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, vf);
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+#pragma unroll
+                        for (int e = 0; e < E; ++e) o[g][e] = fmaf(pi[g], vf[e], o[g][e]);
+                }
+            }
+        }
+        __syncthreads();  // every warp is done with stage s
+        if (tid == 0 && t + NST < ntiles) issue(t + NST);
+    }
+
+    if (bad) {
+        // Drain the copies still in flight (bounded) before the CTA leaves:
+        // for every stage, wait for the last tile that was issued into it.
+        if (tid == 0) {
+            for (int st = 0; st < NST; ++st) {
+                int last = -1;
+                for (int t = st; t < ntiles; t += NST) last = t;
+                if (last >= 0) mbar_wait(smem_addr(&bars[st]), uint32_t(last / NST) & 1u);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+
+    // Merge the four warps' softmax states.
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            mm[warp * G + g] = m[g];
+            ll[warp * G + g] = l[g];
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < E; ++e) oo[(warp * G + g) * HD + lane * E + e] = o[g][e];
+    __syncthreads();
+    write_result<G, HD>(a, b, hq0, split, mm, ll, oo, tid);
+}
+
+// Generic kernel (any Hd <= 512, any alignment, q dtype may differ from
+// K/V): one query head per CTA, plain loads, one key per warp step.
+template <class QT, class KV>
+__global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
+    constexpr int MAXE = 16;
+    __shared__ float mm[kWarps], ll[kWarps];
+    extern __shared__ float oo[];  // [kWarps][Hd]
+    pdl_launch_dependents();
+    pdl_wait();
+    const FlashDecode& p = a.p;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.x;
+    const int64_t hq = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    const int64_t Hd = p.Hd;
+    const int64_t hkv = hq * p.Nkv / p.Nq;
+    const int64_t len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
+    int64_t jb, je;
+    split_range(a, len, split, jb, je);
+    float q[MAXE], o[MAXE];
+    const float qs = p.scale * kLog2e;
+    for (int i = 0; i < MAXE; ++i) {
+        int64_t d = lane + 32 * i;
+        q[i] = d < Hd ? Elem<QT>::load(p.q, (b * p.Nq + hq) * Hd + d) * qs : 0.f;
+        o[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    const int64_t kv0 = (b * p.Nkv + hkv) * p.S;
+    for (int64_t j = jb + warp; j < je; j += kWarps) {
+        float acc = 0.f;
+        for (int i = 0; i < MAXE; ++i) {
+            int64_t d = lane + 32 * i;
+            if (d < Hd) acc = fmaf(q[i], Elem<KV>::load(p.k, (kv0 + j) * Hd + d), acc);
+        }
+        float sv = warp_sum(acc);
+        float mnew = fmaxf(m, sv);
+        float so = exp2f(m - mnew);
+        float pv = exp2f(sv - mnew);
+        l = l * so + pv;
+        m = mnew;
+        for (int i = 0; i < MAXE; ++i) {
+            int64_t d = lane + 32 * i;
+            float vv = d < Hd ? Elem<KV>::load(p.v, (kv0 + j) * Hd + d) : 0.f;
+            o[i] = fmaf(pv, vv, o[i] * so);
+        }
+    }
+    if (lane == 0) {
+        mm[warp] = m;
+        ll[warp] = l;
+    }
+    for (int i = 0; i < MAXE; ++i) {
+        int64_t d = lane + 32 * i;
+        if (d < Hd) oo[warp * Hd + d] = o[i];
+    }
+    __syncthreads();
+    for (int64_t d = tid; d < Hd; d += kThreads) {
+        float M = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < kWarps; ++w) {
+                float f = mm[w] == -INFINITY ? 0.f : exp2f(mm[w] - M);
+                L += f * ll[w];
+                O += f * oo[w * Hd + d];
+            }
+        }
+        if (a.splits == 1) {
+            float r = L > 0.f ? O * (1.0f / L) : 0.f;
+            int64_t oi = (b * p.Nq + hq) * Hd + d;
+            if (p.out_dtype == PC_F32) Elem<TF32>::store(p.out, oi, r);
+            else if (p.out_dtype == PC_BF16) Elem<TBF16>::store(p.out, oi, r);
+            else Elem<TF16>::store(p.out, oi, r);
+        } else {
+            int64_t slot = (b * p.Nq + hq) * a.splits + split;
+            a.po[slot * Hd + d] = O;
+            if (d == 0) {
+                a.pm[slot] = M;
+                a.pl[slot] = L;
+            }
+        }
+    }
+}
+
+// Log-sum-exp combine of the splits (FlashDecoding.metal:182-231).
+template <class OT>
+__global__ void __launch_bounds__(kThreads) fd_combine_kernel(const float* po, const float* pm, const float* pl,
+                                                              void* out, int64_t Nq, int64_t Hd, int splits) {
+    extern __shared__ float wts[];  // [splits]
+    __shared__ float red[kWarps];
+    __shared__ float s_M, s_L;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t bh = int64_t(blockIdx.y) * Nq + blockIdx.x;
+    const float* m = pm + bh * splits;
+    const float* l = pl + bh * splits;
+    float mx = -INFINITY;
+    for (int s = tid; s < splits; s += kThreads) mx = fmaxf(mx, m[s]);
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float v = red[0];
+        for (int w = 1; w < kWarps; ++w) v = fmaxf(v, red[w]);
+        s_M = v;
+    }
+    __syncthreads();
+    const float M = s_M;
+    float lsum = 0.f;
+    for (int s = tid; s < splits; s += kThreads) {
+        float f = (M == -INFINITY || m[s] == -INFINITY) ? 0.f : exp2f(m[s] - M);
+        wts[s] = f;
+        lsum += f * l[s];
+    }
+    lsum = warp_sum(lsum);
+    __syncthreads();
+    if (lane == 0) red[warp] = lsum;
+    __syncthreads();
+    if (tid == 0) {
+        float v = 0.f;
+        for (int w = 0; w < kWarps; ++w) v += red[w];
+        s_L = v;
+    }
+    __syncthreads();
+    const float L = s_L;
+    const float inv_l = L > 0.f ? 1.0f / L : 0.f;
+    const float* o = po + bh * splits * Hd;
+    for (int64_t d = tid; d < Hd; d += kThreads) {
+        float acc = 0.f;
+        for (int s = 0; s < splits; ++s) acc = fmaf(wts[s], o[int64_t(s) * Hd + d], acc);
+        Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+    }
+}
+
+bool fast_path(const FlashDecode& p) {
+    bool hd_ok = p.Hd == 64 || p.Hd == 128 || p.Hd == 256 || p.Hd == 512;
+    return hd_ok && p.q_dtype == p.kv_dtype && aligned16(p.k) && aligned16(p.v);
+}
+
+int heads_per_cta(const FlashDecode& p) {
+    int64_t g = p.Nq / p.Nkv;
+    int64_t cap = 32 / (p.Hd / 32);  // G * Hd/32 <= 32
+    for (int c : {8, 4, 2})
+        if (c <= cap && g % c == 0) return c;
+    return 1;
+}
+
+template <class KV, int HD, int G>
+cudaError_t run_fast(const FDArgs& a, dim3 grid, cudaStream_t s) {
+    auto kern = fd_partial_kernel<KV, HD, G>;
+    constexpr size_t smem = fd_smem_bytes<KV, HD, G>();
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = allow_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    return launch_k(kern, grid, dim3(kThreads), smem, s, a);
+}
+
+// Register budget: q and O slices take 2*G*Hd/32 floats per lane; keep
+// G*Hd/32 <= 32 (the plan never asks for more).
+template <class KV, int HD>
+cudaError_t run_fast_g(const FDArgs& a, dim3 grid, cudaStream_t s) {
+    switch (a.G) {
+    case 1: return run_fast<KV, HD, 1>(a, grid, s);
+    case 2: return run_fast<KV, HD, 2>(a, grid, s);
+    case 4:
+        if constexpr (HD <= 256) return run_fast<KV, HD, 4>(a, grid, s);
+        break;
+    case 8:
+        if constexpr (HD <= 128) return run_fast<KV, HD, 8>(a, grid, s);
+        break;
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <class KV>
+cudaError_t run_fast_hd(const FDArgs& a, dim3 grid, cudaStream_t s) {
+    switch (a.p.Hd) {
+    case 64: return run_fast_g<KV, 64>(a, grid, s);
+    case 128: return run_fast_g<KV, 128>(a, grid, s);
+    case 256: return run_fast_g<KV, 256>(a, grid, s);
+    case 512: return run_fast_g<KV, 512>(a, grid, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <class QT>
+cudaError_t run_generic_q(const FDArgs& a, dim3 grid, cudaStream_t s) {
+    size_t smem = size_t(kWarps) * a.p.Hd * 4;
+    switch (a.p.kv_dtype) {
+    case PC_F32: return launch_k(fd_generic_kernel<QT, TF32>, grid, dim3(kThreads), smem, s, a);
+    case PC_F16: return launch_k(fd_generic_kernel<QT, TF16>, grid, dim3(kThreads), smem, s, a);
+    case PC_BF16: return launch_k(fd_generic_kernel<QT, TBF16>, grid, dim3(kThreads), smem, s, a);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+FlashDecodePlan flash_decode_plan(const FlashDecode& p, int sm_count) {
+    FlashDecodePlan plan{};
+    plan.fast = fast_path(p);
+    plan.heads_per_cta = plan.fast ? heads_per_cta(p) : 1;
+    int64_t hgroups = (p.Nq / p.Nkv) / plan.heads_per_cta;
+    int64_t base = p.B * p.Nkv * hgroups;
+    int64_t target = int64_t(sm_count) * 2;
+    int64_t max_tiles = (p.S + kTileKeys - 1) / kTileKeys;
+    if (max_tiles < 1) max_tiles = 1;
+    int64_t splits = (target + base - 1) / base;
+    if (splits < 1) splits = 1;
+    if (splits > max_tiles) splits = max_tiles;
+    if (splits > 1024) splits = 1024;
+    int64_t tiles_per_split = (max_tiles + splits - 1) / splits;
+    plan.chunk = tiles_per_split * kTileKeys;
+    plan.splits = int((p.S + plan.chunk - 1) / plan.chunk);
+    if (plan.splits < 1) plan.splits = 1;
+    plan.scratch_o = size_t(p.B * p.Nq) * plan.splits * p.Hd * 4;
+    plan.scratch_ml = size_t(p.B * p.Nq) * plan.splits * 4;
+    return plan;
+}
+
+cudaError_t flash_decode(const FlashDecode& p, const FlashDecodePlan& plan, float* po, float* pm, float* pl,
+                         cudaStream_t s) {
+    FDArgs a{p, plan.splits, plan.chunk, plan.heads_per_cta, int((p.Nq / p.Nkv) / plan.heads_per_cta), po, pm, pl};
+    cudaError_t err;
+    if (plan.fast) {
+        dim3 grid(unsigned(plan.splits), unsigned(p.Nkv * a.hgroups), unsigned(p.B));
+        switch (p.kv_dtype) {
+        case PC_BF16: err = run_fast_hd<TBF16>(a, grid, s); break;
+        case PC_F16: err = run_fast_hd<TF16>(a, grid, s); break;
+        case PC_F32: err = run_fast_hd<TF32>(a, grid, s); break;
+        default: return cudaErrorInvalidValue;
+        }
+    } else {
+        dim3 grid(unsigned(plan.splits), unsigned(p.Nq), unsigned(p.B));
+        switch (p.q_dtype) {
+        case PC_F32: err = run_generic_q<TF32>(a, grid, s); break;
+        case PC_F16: err = run_generic_q<TF16>(a, grid, s); break;
+        case PC_BF16: err = run_generic_q<TBF16>(a, grid, s); break;
+        default: return cudaErrorInvalidValue;
+        }
+    }
+    return err;
+}
+
+cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& plan, const float* po, const float* pm,
+                                 const float* pl, cudaStream_t s) {
+    if (plan.splits <= 1) return cudaSuccess;
+    dim3 grid(unsigned(p.Nq), unsigned(p.B));
+    size_t smem = size_t(plan.splits) * 4;
+    switch (p.out_dtype) {
+    case PC_F32: return launch_k(fd_combine_kernel<TF32>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
+    case PC_F16: return launch_k(fd_combine_kernel<TF16>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
+    case PC_BF16: return launch_k(fd_combine_kernel<TBF16>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
+    }
+    return cudaErrorInvalidValue;
+}
+
+uint32_t read_and_clear_fd_errors() {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fd_error_word, sizeof(v)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) cudaMemcpyToSymbol(g_fd_error_word, &zero, sizeof(zero));
+    return v;
+}
+
+namespace {
+RegisterFunctions reg_fd({
+    {"flash_decoding_partial_bf16", reinterpret_cast<const void*>(fd_partial_kernel<TBF16, 256, 2>)},
+    {"flash_decoding_partial_f16", reinterpret_cast<const void*>(fd_partial_kernel<TF16, 256, 2>)},
+    {"flash_decoding_partial_f32", reinterpret_cast<const void*>(fd_partial_kernel<TF32, 256, 2>)},
+    {"flash_decoding_partial_generic", reinterpret_cast<const void*>(fd_generic_kernel<TF32, TF32>)},
+    {"flash_decoding_reduce_bf16", reinterpret_cast<const void*>(fd_combine_kernel<TBF16>)},
+    {"flash_decoding_reduce_f16", reinterpret_cast<const void*>(fd_combine_kernel<TF16>)},
+    {"flash_decoding_reduce_f32", reinterpret_cast<const void*>(fd_combine_kernel<TF32>)},
+});
+}  // namespace
+
+}  // namespace launch
+}  // namespace popcorn
+
+extern "C" int pc_device_error_check(int device, uint32_t* flags) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return PC_ERR_GPU_DEVICE_REMOVED;
+    }
+    cudaDeviceSynchronize();
+    *flags = popcorn::launch::read_and_clear_fd_errors();
+    cudaSetDevice(prev);
+    return PC_OK;
+}

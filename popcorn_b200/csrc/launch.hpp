@@ -1,0 +1,152 @@
+// launch.hpp — parameter blocks and launchers of the sm_100a kernels.
+//
+// Each launcher enqueues on `stream`, never synchronises and returns the
+// CUDA launch status. Shapes have been validated by the kernel objects
+// (ops.cu) before any launcher runs.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace popcorn {
+namespace launch {
+
+struct DeviceInfo {
+    int device;
+    int sm_count;
+};
+DeviceInfo device_info(int device);
+
+// KVCacheWrite.metal:7-59 semantics. When pos_dev != nullptr the offset is
+// read from device memory (*pos_dev) at run time.
+struct KVWrite {
+    const void* src;
+    int src_dtype;
+    void* cache;
+    int cache_dtype;
+    int64_t B, Nkv, Snew, Smax, Hd, offset;
+    const int32_t* pos_dev;
+};
+cudaError_t kv_cache_write(const KVWrite& p, cudaStream_t stream);
+
+// RMSNorm.metal:7-42 semantics; weight is f32 [H] or null.
+struct RMSNorm {
+    const void* x;
+    int x_dtype;
+    const float* weight;
+    void* out;
+    int out_dtype;
+    int64_t rows, H;
+    float eps;
+    int add_one;
+};
+cudaError_t rmsnorm(const RMSNorm& p, cudaStream_t stream);
+
+// Row-vector times weight matrix with optional fused prologue/epilogue.
+//   y[n] = sum_k xin[k] * W[n,k]     (W [N,K] row-major, linear-layer layout)
+// Prologue: xin = round(RMSNorm(x)) when norm_weight != null or has_norm.
+// Epilogue kind:
+//   kStore     out[n] = y[n]
+//   kResidual  out[n] = round(round(y[n]) + residual[n])
+//   kGated     out[n] = round(round(act(round(y_gate[n]))) * round(y_up[n]))
+//   kQKV       rows [0, q_rows) -> q_out; the next kv_rows -> k_cache at
+//              pos; the last kv_rows -> v_cache at pos
+enum class Epilogue : int { kStore = 0, kResidual = 1, kGated = 2, kQKV = 3 };
+struct Gemv {
+    const void* x;
+    int x_dtype;
+    const void* w;   // gate for kGated
+    const void* w2;  // up for kGated
+    int w_dtype;
+    void* out;
+    int out_dtype;
+    int64_t K, N;
+    bool has_norm;
+    const float* norm_weight;  // may be null with has_norm (no weight)
+    float eps;
+    int add_one;
+    Epilogue epilogue;
+    const void* residual;  // kResidual, out dtype
+    int activation;        // kGated: 0 gelu_tanh, 1 silu
+    // kQKV
+    void* k_cache;
+    void* v_cache;
+    int64_t q_rows, kv_rows, Hd, Smax, offset;
+    const int32_t* pos_dev;
+};
+cudaError_t gemv(const Gemv& p, cudaStream_t stream);
+
+// General C = A * B (or A * B^T), fp32 accumulation (Matmul.metal:7-27).
+struct Matmul {
+    const void* a;
+    int a_dtype;
+    const void* b;
+    int b_dtype;
+    void* c;
+    int c_dtype;
+    int64_t M, K, N;
+    int transpose_b;
+};
+cudaError_t matmul(const Matmul& p, cudaStream_t stream);
+// True when the tcgen05 tensor-core GEMM serves this problem.
+bool matmul_uses_tensor_cores(const Matmul& p);
+
+// Elementwise: GeluTanh / SiLU (unary) and Mul / Add (binary).
+enum class Unary : int { kGeluTanh = 0, kSilu = 1 };
+enum class Binary : int { kMul = 0, kAdd = 1 };
+cudaError_t unary(Unary op, const void* x, int x_dtype, void* out, int out_dtype, int64_t count,
+                  cudaStream_t stream);
+cudaError_t binary(Binary op, const void* a, const void* b, void* out, int dtype, int64_t count,
+                   cudaStream_t stream);
+
+// Split-KV decode attention (FlashDecoding.metal:29-231 semantics).
+struct FlashDecode {
+    const void* q;  // [B, Nq, 1, Hd]
+    int q_dtype;
+    const void* k;  // [B, Nkv, S, Hd]
+    const void* v;
+    int kv_dtype;
+    void* out;  // [B, Nq, 1, Hd]
+    int out_dtype;
+    int64_t B, Nq, Nkv, S, Hd;
+    const int32_t* seq_lens;  // [B] on device, or null: every sequence has S keys
+    float scale;
+    int mask_kind;
+    int32_t window;
+};
+struct FlashDecodePlan {
+    int splits;
+    int64_t chunk;        // keys per split
+    int heads_per_cta;    // query heads sharing one K/V read
+    bool fast;            // bulk-copy pipelined kernel (else generic)
+    size_t scratch_o;     // bytes of partial O
+    size_t scratch_ml;    // bytes of partial m (and of l)
+};
+FlashDecodePlan flash_decode_plan(const FlashDecode& p, int sm_count);
+// Partial pass. partial_o [B,Nq,splits,Hd] f32, partial_m / partial_l
+// [B,Nq,splits] f32 (log2 units). With one split it writes the output.
+cudaError_t flash_decode(const FlashDecode& p, const FlashDecodePlan& plan, float* partial_o, float* partial_m,
+                         float* partial_l, cudaStream_t stream);
+// Log-sum-exp combine of the splits into the output (no-op for one split).
+cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& plan, const float* partial_o,
+                                 const float* partial_m, const float* partial_l, cudaStream_t stream);
+
+// Prefill attention (FlashAttention.metal:31-162 semantics), Sq >= 1.
+struct FlashAttention {
+    const void* q;  // [B, Nq, Sq, Hd]
+    int q_dtype;
+    const void* k;  // [B, Nkv, Sk, Hd]
+    const void* v;
+    int kv_dtype;
+    void* out;
+    int out_dtype;
+    int64_t B, Nq, Nkv, Sq, Sk, Hd;
+    float scale;
+    int mask_kind;
+    int32_t window;
+};
+cudaError_t flash_attention(const FlashAttention& p, cudaStream_t stream);
+bool flash_attention_uses_tensor_cores(const FlashAttention& p);
+
+}  // namespace launch
+}  // namespace popcorn

@@ -1,0 +1,821 @@
+// ops.cu — the kernel value objects (validation + routing) and the kernel
+// half of the C ABI. Each class restates one reference op's initialiser
+// checks and routing; the arithmetic lives in the launchers (launch.hpp).
+#include <memory>
+#include <sstream>
+
+#include "launch.hpp"
+#include "popcorn.hpp"
+
+namespace popcorn {
+void set_last_error(const std::string& m);
+KernelCommandEncoder& encoder_impl(pc_encoder* e);
+
+namespace {
+
+std::string dims_string(const std::vector<int64_t>& v) {
+    std::ostringstream os;
+    os << "[";
+    for (size_t i = 0; i < v.size(); ++i) os << (i ? ", " : "") << v[i];
+    os << "]";
+    return os.str();
+}
+
+void require_rank(const Tensor& t, int rank) {
+    if (t.rank() != rank)
+        fail(PC_ERR_TENSOR_INVALID_RANK, "Expected rank " + std::to_string(rank) + ", got " + std::to_string(t.rank()) + ".");
+}
+
+void require_elements(const Tensor& t, int64_t n, const char* what) {
+    if (t.element_count() < n)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(what) + " holds " + std::to_string(t.element_count()) +
+                                               " elements; the dimensions need " + std::to_string(n) + ".");
+}
+
+bool is_float(int dt) { return dt == PC_F32 || dt == PC_F16 || dt == PC_BF16; }
+
+const char* dt_tag(int dt) { return dt == PC_F32 ? "f32" : dt == PC_F16 ? "f16" : dt == PC_BF16 ? "bf16" : "x"; }
+
+// ---------------------------------------------------------------------------
+// Kernels.FlashAttention + _FlashDecoding (FlashAttention.swift:13-139,
+// FlashDecoding.swift:6-90)
+// ---------------------------------------------------------------------------
+class FlashAttentionKernel : public Kernel {
+public:
+    FlashAttentionKernel(Tensor q, Tensor k, Tensor v, Tensor out, const Tensor* seq_lens, int64_t B, int64_t Nq,
+                         int64_t Nkv, int64_t Sq, int64_t Sk, int64_t Hd, float scale, pc_attention_mask mask)
+        : q_(q), k_(k), v_(v), out_(out), B_(B), Nq_(Nq), Nkv_(Nkv), Sq_(Sq), Sk_(Sk), Hd_(Hd), scale_(scale),
+          mask_(mask) {
+        if (seq_lens) {
+            lens_ = *seq_lens;
+            has_lens_ = true;
+        }
+        // FlashAttention.swift:27-36.
+        if (Nkv <= 0 || Nq <= 0 || Nq % Nkv != 0)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention query heads must be divisible by KV heads; got " +
+                                                   std::to_string(Nq) + " and " + std::to_string(Nkv) + ".");
+        if (Hd > 512)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention head dim must be <= 512 (kernel limit); got " +
+                                                   std::to_string(Hd) + ".");
+        if (Hd <= 0 || B <= 0 || Sq <= 0)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention needs batch, query length and head dim >= 1.");
+        if (!has_lens_ && Sk <= 0)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention needs at least one key (keyLen >= 1).");
+        if (mask.kind < 0 || mask.kind > 2)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "unknown attention mask kind " + std::to_string(mask.kind) + ".");
+        if (mask.kind == PC_MASK_CAUSAL_SLIDING_WINDOW && mask.window < 1)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "sliding-window length must be >= 1.");
+        // _FDPartial / _FlashAttentionPlain dtype checks (FlashDecoding.swift:119-125, 199-205;
+        // FlashAttention.swift:181-190), widened to f16 (extension).
+        if (!is_float(q.dtype()) || !is_float(k.dtype()) || k.dtype() != v.dtype() || !is_float(out.dtype()))
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+                 "Unsupported FlashAttention data type combination: " + dtype_name(q.dtype()) + ", " +
+                     dtype_name(k.dtype()) + ", " + dtype_name(v.dtype()) + ", " + dtype_name(out.dtype()) + ".");
+        if (Sq == 1 && q.dtype() != k.dtype())
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Unsupported FlashDecoding Q/K/V data type: " +
+                                                               dtype_name(q.dtype()) + " with K/V " +
+                                                               dtype_name(k.dtype()) + ".");
+        require_elements(q, B * Nq * Sq * Hd, "FlashAttention q");
+        require_elements(k, B * Nkv * Sk * Hd, "FlashAttention k");
+        require_elements(v, B * Nkv * Sk * Hd, "FlashAttention v");
+        require_elements(out, B * Nq * Sq * Hd, "FlashAttention out");
+        if (has_lens_) {
+            if (lens_.dtype() != PC_I32)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "seq_lens must be i32; got " + dtype_name(lens_.dtype()) + ".");
+            require_elements(lens_, B, "seq_lens");
+        }
+        path_ = pc_flash_attention_route(Sq, Hd, q.dtype());
+        if (path_ == PC_PATH_DECODING) {
+            function_names_ = std::string("flash_decoding_partial_") + dt_tag(k.dtype()) + ";flash_decoding_reduce_" +
+                              dt_tag(out.dtype());
+        } else {
+            launch::FlashAttention fa = fa_params();
+            path_ = launch::flash_attention_uses_tensor_cores(fa) ? PC_PATH_TENSOR : PC_PATH_PLAIN;
+            function_names_ = path_ == PC_PATH_TENSOR ? "flash_attention_tc_bf16" : "flash_attention";
+        }
+    }
+
+    const char* name() const override { return "FlashAttention"; }
+
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> b = {{q_, PC_ACCESS_READ}, {k_, PC_ACCESS_READ}, {v_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
+        if (has_lens_) b.push_back({lens_, PC_ACCESS_READ});
+        return b;
+    }
+
+    launch::FlashAttention fa_params() const {
+        return launch::FlashAttention{q_.data(), q_.dtype(), k_.data(), v_.data(), k_.dtype(), out_.data(), out_.dtype(),
+                                      B_, Nq_, Nkv_, Sq_, Sk_, Hd_, scale_, mask_.kind, mask_.window};
+    }
+
+    void encode(KernelCommandEncoder& enc) const override {
+        if (path_ != PC_PATH_DECODING) {
+            launch::FlashAttention p = fa_params();
+            enc.dispatch(path_ == PC_PATH_TENSOR ? "flash_attention_tc_bf16" : "flash_attention", tensors(),
+                         [p](cudaStream_t s) { return launch::flash_attention(p, s); });
+            return;
+        }
+        launch::FlashDecode p{q_.data(), q_.dtype(), k_.data(), v_.data(), k_.dtype(), out_.data(), out_.dtype(),
+                              B_, Nq_, Nkv_, Sk_, Hd_, has_lens_ ? static_cast<const int32_t*>(lens_.data()) : nullptr,
+                              scale_, mask_.kind, mask_.window};
+        launch::FlashDecodePlan plan = launch::flash_decode_plan(p, enc.sm_count());
+        // FlashDecoding.swift:55-59: partial O [B,Nq,P,Hd], m and l [B,Nq,P], f32.
+        std::vector<ScratchSpec> specs = {{{B_, Nq_, plan.splits, Hd_}, PC_F32},
+                                          {{B_, Nq_, plan.splits}, PC_F32},
+                                          {{B_, Nq_, plan.splits}, PC_F32}};
+        std::string partial_name = std::string("flash_decoding_partial_") + dt_tag(k_.dtype());
+        std::string reduce_name = std::string("flash_decoding_reduce_") + dt_tag(out_.dtype());
+        std::vector<Binding> reads = {{q_, PC_ACCESS_READ}, {k_, PC_ACCESS_READ}, {v_, PC_ACCESS_READ}};
+        if (has_lens_) reads.push_back({lens_, PC_ACCESS_READ});
+        enc.with_temporaries(specs, [&](const std::vector<Tensor>& t) {
+            float* po = static_cast<float*>(t[0].data());
+            float* pm = static_cast<float*>(t[1].data());
+            float* pl = static_cast<float*>(t[2].data());
+            std::vector<Binding> partial_b = reads;
+            partial_b.push_back({t[0], PC_ACCESS_WRITE});
+            partial_b.push_back({t[1], PC_ACCESS_WRITE});
+            partial_b.push_back({t[2], PC_ACCESS_WRITE});
+            std::vector<Binding> reduce_b = {{t[0], PC_ACCESS_READ}, {t[1], PC_ACCESS_READ}, {t[2], PC_ACCESS_READ},
+                                             {out_, PC_ACCESS_WRITE}};
+            if (plan.splits == 1) {
+                // One split covers every key: the partial pass normalises
+                // and writes the output itself.
+                partial_b.push_back({out_, PC_ACCESS_WRITE});
+            }
+            enc.dispatch(partial_name, partial_b, [p, plan, po, pm, pl](cudaStream_t s) {
+                return launch::flash_decode(p, plan, po, pm, pl, s);
+            });
+            if (plan.splits > 1)
+                enc.dispatch(reduce_name, reduce_b, [p, plan, po, pm, pl](cudaStream_t s) {
+                    return launch::flash_decode_combine(p, plan, po, pm, pl, s);
+                });
+        });
+    }
+
+private:
+    Tensor q_, k_, v_, out_, lens_;
+    bool has_lens_ = false;
+    int64_t B_, Nq_, Nkv_, Sq_, Sk_, Hd_;
+    float scale_;
+    pc_attention_mask mask_;
+    int path_ = PC_PATH_DECODING;
+};
+
+// ---------------------------------------------------------------------------
+// Kernels.KVCacheWrite (KVCacheWrite.swift:5-72)
+// ---------------------------------------------------------------------------
+class KVCacheWriteKernel : public Kernel {
+public:
+    KVCacheWriteKernel(Tensor src, Tensor cache, int64_t B, int64_t Nkv, int64_t Snew, int64_t Smax, int64_t Hd,
+                       int64_t offset)
+        : src_(src), cache_(cache), p_{} {
+        int s = src.dtype(), c = cache.dtype();
+        // KVCacheWrite.swift:20-25 plus the f16 extension.
+        if (s == PC_F32 && c == PC_F32) function_names_ = "kv_cache_write";
+        else if (s == PC_BF16 && c == PC_BF16) function_names_ = "kv_cache_write_bf16";
+        else if (s == PC_F32 && c == PC_BF16) function_names_ = "kv_cache_write_f32_to_bf16";
+        else if (s == PC_F16 && c == PC_F16) function_names_ = "kv_cache_write_f16";
+        else
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Unsupported KV cache data type combination: " +
+                                                               dtype_name(s) + ", " + dtype_name(c) + ".");
+        if (offset < 0 || offset + Snew > Smax || B < 0 || Nkv < 0 || Snew < 0 || Hd < 0)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache write range " + std::to_string(offset) + "..<" +
+                                                   std::to_string(offset + Snew) + " exceeds cache length " +
+                                                   std::to_string(Smax) + ".");
+        require_elements(src, B * Nkv * Snew * Hd, "KVCacheWrite source");
+        require_elements(cache, B * Nkv * Smax * Hd, "KVCacheWrite cache");
+        p_ = launch::KVWrite{src.data(), s, cache.data(), c, B, Nkv, Snew, Smax, Hd, offset, nullptr};
+    }
+    const char* name() const override { return "KVCacheWrite"; }
+    std::vector<Binding> tensors() const override { return {{src_, PC_ACCESS_READ}, {cache_, PC_ACCESS_WRITE}}; }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::KVWrite p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::kv_cache_write(p, s); });
+    }
+
+private:
+    Tensor src_, cache_;
+    launch::KVWrite p_;
+};
+
+// ---------------------------------------------------------------------------
+// Kernels.RMSNorm (RMSNorm.swift:7-96)
+// ---------------------------------------------------------------------------
+class RMSNormKernel : public Kernel {
+public:
+    RMSNormKernel(Tensor x, const Tensor* w, Tensor out, int64_t rows, int64_t H, float eps, bool add_one)
+        : x_(x), out_(out) {
+        int dt = x.dtype();
+        if (dt == PC_F32) function_names_ = "rmsnorm";
+        else if (dt == PC_F16) function_names_ = "rmsnorm_f16";
+        else if (dt == PC_BF16) function_names_ = "rmsnorm_bf16";
+        else fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Unsupported RMSNorm data type: " + dtype_name(dt) + ".");
+        // RMSNorm.metal:44-46: the output has x's type, the weight is f32.
+        if (out.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm output must be " + dtype_name(dt) + "; got " +
+                                                               dtype_name(out.dtype()) + ".");
+        if (w) {
+            w_ = *w;
+            has_w_ = true;
+            if (w->dtype() != PC_F32)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32; got " +
+                                                                   dtype_name(w->dtype()) + ".");
+            require_elements(*w, H, "RMSNorm weight");
+        }
+        if (H <= 0 || rows < 0) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RMSNorm hidden size must be >= 1.");
+        require_elements(x, rows * H, "RMSNorm x");
+        require_elements(out, rows * H, "RMSNorm out");
+        p_ = launch::RMSNorm{x.data(), dt, has_w_ ? static_cast<const float*>(w->data()) : nullptr, out.data(),
+                             out.dtype(), rows, H, eps, add_one ? 1 : 0};
+    }
+    const char* name() const override { return "RMSNorm"; }
+    std::vector<Binding> tensors() const override {
+        // With no weight the reference binds x in the weight slot (RMSNorm.swift:13).
+        return {{x_, PC_ACCESS_READ}, {has_w_ ? w_ : x_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::RMSNorm p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::rmsnorm(p, s); });
+    }
+
+private:
+    Tensor x_, w_, out_;
+    bool has_w_ = false;
+    launch::RMSNorm p_{};
+};
+
+// Dtype combinations the matvec serves: Matmul.swift:362-374
+// (fff, f.bf.f, bf.bf.f, bf.bf.bf) plus the f16 forms (MPPMatvec's
+// f16.f16.f16, f16.f16.f32) and f32.f16.f32 (Matvec.metal:130).
+bool matvec_dtypes_ok(int x, int w, int o) {
+    if (x == PC_F32 && w == PC_F32 && o == PC_F32) return true;
+    if (w != PC_BF16 && w != PC_F16) return false;
+    return (x == PC_F32 || x == w) && (o == PC_F32 || o == w);
+}
+
+// ---------------------------------------------------------------------------
+// Kernels.Matmul (Matmul.swift:9-93, 233-277)
+// ---------------------------------------------------------------------------
+class MatmulKernel : public Kernel {
+public:
+    MatmulKernel(Tensor a, Tensor b, Tensor c, int64_t m, int64_t k, int64_t n, bool transpose_b)
+        : a_(a), b_(b), c_(c), m_(m), k_(k), n_(n), tb_(transpose_b) {
+        int ad = a.dtype(), bd = b.dtype(), cd = c.dtype();
+        if (m < 0 || k < 0 || n < 0) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul dimensions must be >= 0.");
+        require_elements(a, m * k, "Matmul A");
+        require_elements(b, k * n, "Matmul B");
+        require_elements(c, m * n, "Matmul C");
+        gemv_ = (m == 1 && transpose_b && matvec_dtypes_ok(ad, bd, cd));
+        if (gemv_) {
+            function_names_ = std::string("matvec_nk_") + dt_tag(ad) + "_" + dt_tag(bd) + "_" + dt_tag(cd);
+            return;
+        }
+        // Matmul.swift:198-231 (naive / MPP combinations) plus f16.
+        bool ok = (ad == PC_F32 && bd == PC_F32 && cd == PC_F32) ||
+                  (ad == PC_F32 && (bd == PC_F16 || bd == PC_BF16) && cd == PC_F32) ||
+                  ((ad == PC_BF16 || ad == PC_F16) && bd == ad && (cd == PC_F32 || cd == ad));
+        if (!ok)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Unsupported matmul data type combination: " +
+                                                               dtype_name(ad) + ", " + dtype_name(bd) + ", " +
+                                                               dtype_name(cd) + ".");
+        launch::Matmul p = params();
+        function_names_ = launch::matmul_uses_tensor_cores(p) ? "matmul_tc_bf16_tb" : "matmul";
+    }
+    launch::Matmul params() const {
+        return launch::Matmul{a_.data(), a_.dtype(), b_.data(), b_.dtype(), c_.data(), c_.dtype(), m_, k_, n_, tb_ ? 1 : 0};
+    }
+    const char* name() const override { return "Matmul"; }
+    std::vector<Binding> tensors() const override {
+        return {{a_, PC_ACCESS_READ}, {b_, PC_ACCESS_READ}, {c_, PC_ACCESS_WRITE}};
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        if (m_ == 0 || n_ == 0) return;
+        if (gemv_) {
+            launch::Gemv g{};
+            g.x = a_.data(); g.x_dtype = a_.dtype(); g.w = b_.data(); g.w_dtype = b_.dtype();
+            g.out = c_.data(); g.out_dtype = c_.dtype(); g.K = k_; g.N = n_;
+            g.epilogue = launch::Epilogue::kStore;
+            enc.dispatch(function_names_, tensors(), [g](cudaStream_t s) { return launch::gemv(g, s); });
+            return;
+        }
+        launch::Matmul p = params();
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::matmul(p, s); });
+    }
+
+private:
+    Tensor a_, b_, c_;
+    int64_t m_, k_, n_;
+    bool tb_;
+    bool gemv_ = false;
+};
+
+// ---------------------------------------------------------------------------
+// Elementwise: GeluTanh, SiLU, Mul, Add (GeluTanh.swift, Mul.swift, Add.swift)
+// ---------------------------------------------------------------------------
+class UnaryKernel : public Kernel {
+public:
+    UnaryKernel(launch::Unary op, Tensor x, Tensor out) : op_(op), x_(x), out_(out) {
+        const char* base = op == launch::Unary::kGeluTanh ? "gelu_tanh" : "silu";
+        const char* opname = op == launch::Unary::kGeluTanh ? "GeluTanh" : "SiLU";
+        if (!x.same_shape(out))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(opname) + " output shape must match input; got " +
+                                                   out.shape_string() + ", expected " + x.shape_string() + ".");
+        if (!is_float(x.dtype()) || out.dtype() != x.dtype())
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, std::string("Unsupported ") + opname + " data type: " +
+                                                               dtype_name(x.dtype()) + ".");
+        function_names_ = x.dtype() == PC_F32 ? std::string(base) : std::string(base) + "_" + dt_tag(x.dtype());
+        name_ = opname;
+    }
+    const char* name() const override { return name_; }
+    std::vector<Binding> tensors() const override { return {{x_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}}; }
+    void encode(KernelCommandEncoder& enc) const override {
+        auto op = op_;
+        const void* x = x_.data();
+        void* o = out_.data();
+        int dt = x_.dtype();
+        int64_t n = x_.element_count();
+        if (n == 0) return;
+        enc.dispatch(function_names_, tensors(), [=](cudaStream_t s) { return launch::unary(op, x, dt, o, dt, n, s); });
+    }
+
+private:
+    launch::Unary op_;
+    Tensor x_, out_;
+    const char* name_;
+};
+
+class BinaryKernel : public Kernel {
+public:
+    BinaryKernel(launch::Binary op, Tensor a, Tensor b, Tensor out) : op_(op), a_(a), b_(b), out_(out) {
+        const char* base = op == launch::Binary::kMul ? "mul" : "add";
+        name_ = op == launch::Binary::kMul ? "Mul" : "Add";
+        if (!a.same_shape(b) || !a.same_shape(out))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(name_) + " shapes must match; got " + a.shape_string() +
+                                                   ", " + b.shape_string() + ", " + out.shape_string() + ".");
+        if (!is_float(a.dtype()) || b.dtype() != a.dtype() || out.dtype() != a.dtype())
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, std::string("Unsupported ") + name_ + " data type: " +
+                                                               dtype_name(a.dtype()) + ".");
+        function_names_ = a.dtype() == PC_F32 ? std::string(base) : std::string(base) + "_" + dt_tag(a.dtype());
+    }
+    const char* name() const override { return name_; }
+    std::vector<Binding> tensors() const override {
+        return {{a_, PC_ACCESS_READ}, {b_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        auto op = op_;
+        const void* a = a_.data();
+        const void* b = b_.data();
+        void* o = out_.data();
+        int dt = a_.dtype();
+        int64_t n = a_.element_count();
+        if (n == 0) return;
+        enc.dispatch(function_names_, tensors(), [=](cudaStream_t s) { return launch::binary(op, a, b, o, dt, n, s); });
+    }
+
+private:
+    launch::Binary op_;
+    Tensor a_, b_, out_;
+    const char* name_;
+};
+
+// ---------------------------------------------------------------------------
+// Fused decode ops (extensions)
+// ---------------------------------------------------------------------------
+void check_norm_weight(const Tensor* w, int64_t K) {
+    if (!w) return;
+    if (w->dtype() != PC_F32)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32; got " + dtype_name(w->dtype()) + ".");
+    require_elements(*w, K, "RMSNorm weight");
+}
+
+void check_row_vector(const Tensor& x, int64_t K, const char* what) {
+    if (x.element_count() != K)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(what) + " must hold one row of " + std::to_string(K) +
+                                               " elements; got " + x.shape_string() + ".");
+}
+
+class FusedGemvKernel : public Kernel {
+public:
+    FusedGemvKernel(const char* name, std::vector<Binding> bindings, launch::Gemv g, std::string fn)
+        : name_(name), bindings_(std::move(bindings)), g_(g) {
+        function_names_ = std::move(fn);
+    }
+    const char* name() const override { return name_; }
+    std::vector<Binding> tensors() const override { return bindings_; }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::Gemv g = g_;
+        enc.dispatch(function_names_, bindings_, [g](cudaStream_t s) { return launch::gemv(g, s); });
+    }
+
+private:
+    const char* name_;
+    std::vector<Binding> bindings_;
+    launch::Gemv g_;
+};
+
+std::unique_ptr<Kernel> make_rmsnorm_matmul(const Tensor& x, const Tensor* nw, float eps, bool add_one, const Tensor& w,
+                                            const Tensor& out) {
+    require_rank(w, 2);
+    int64_t N = w[0], K = w[1];
+    check_row_vector(x, K, "RMSNorm+Matmul x");
+    check_row_vector(out, N, "RMSNorm+Matmul out");
+    check_norm_weight(nw, K);
+    if (!is_float(x.dtype()) || w.dtype() != x.dtype() || out.dtype() != x.dtype() || x.dtype() == PC_F32)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm+Matmul needs x, w and out all f16 or all bf16.");
+    launch::Gemv g{};
+    g.x = x.data(); g.x_dtype = x.dtype(); g.w = w.data(); g.w_dtype = w.dtype(); g.out = out.data();
+    g.out_dtype = out.dtype(); g.K = K; g.N = N; g.has_norm = true;
+    g.norm_weight = nw ? static_cast<const float*>(nw->data()) : nullptr; g.eps = eps; g.add_one = add_one;
+    g.epilogue = launch::Epilogue::kStore;
+    std::vector<Binding> b = {{x, PC_ACCESS_READ}, {w, PC_ACCESS_READ}, {out, PC_ACCESS_WRITE}};
+    if (nw) b.push_back({*nw, PC_ACCESS_READ});
+    return std::make_unique<FusedGemvKernel>("RMSNormMatmul", b, g, std::string("rmsnorm_matvec_") + dt_tag(x.dtype()));
+}
+
+std::unique_ptr<Kernel> make_gated_mlp(const Tensor& x, const Tensor* nw, float eps, bool add_one, const Tensor& wg,
+                                       const Tensor& wu, int act, const Tensor& out) {
+    require_rank(wg, 2);
+    require_rank(wu, 2);
+    if (wg.dims() != wu.dims())
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "gate and up weights must have the same shape; got " + wg.shape_string() +
+                                               " and " + wu.shape_string() + ".");
+    int64_t F = wg[0], K = wg[1];
+    check_row_vector(x, K, "GatedMLP x");
+    check_row_vector(out, F, "GatedMLP out");
+    check_norm_weight(nw, K);
+    if (act != PC_ACT_GELU_TANH && act != PC_ACT_SILU)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "unknown activation " + std::to_string(act) + ".");
+    int dt = x.dtype();
+    if ((dt != PC_F16 && dt != PC_BF16) || wg.dtype() != dt || wu.dtype() != dt || out.dtype() != dt)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "GatedMLP needs x, weights and out all f16 or all bf16.");
+    launch::Gemv g{};
+    g.x = x.data(); g.x_dtype = dt; g.w = wg.data(); g.w2 = wu.data(); g.w_dtype = dt; g.out = out.data();
+    g.out_dtype = dt; g.K = K; g.N = F; g.has_norm = nw != nullptr;
+    g.norm_weight = nw ? static_cast<const float*>(nw->data()) : nullptr; g.eps = eps; g.add_one = add_one;
+    g.epilogue = launch::Epilogue::kGated; g.activation = act;
+    std::vector<Binding> b = {{x, PC_ACCESS_READ}, {wg, PC_ACCESS_READ}, {wu, PC_ACCESS_READ}, {out, PC_ACCESS_WRITE}};
+    if (nw) b.push_back({*nw, PC_ACCESS_READ});
+    return std::make_unique<FusedGemvKernel>("GatedMLP", b, g,
+                                             std::string(act == PC_ACT_SILU ? "swiglu_matvec_" : "geglu_matvec_") + dt_tag(dt));
+}
+
+std::unique_ptr<Kernel> make_matmul_residual(const Tensor& a, const Tensor& w, const Tensor& res, const Tensor& out) {
+    require_rank(w, 2);
+    int64_t N = w[0], K = w[1];
+    check_row_vector(a, K, "Matmul+Add a");
+    check_row_vector(res, N, "Matmul+Add residual");
+    check_row_vector(out, N, "Matmul+Add out");
+    int dt = a.dtype();
+    if ((dt != PC_F16 && dt != PC_BF16) || w.dtype() != dt || res.dtype() != dt || out.dtype() != dt)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Matmul+Add needs all tensors f16 or all bf16.");
+    launch::Gemv g{};
+    g.x = a.data(); g.x_dtype = dt; g.w = w.data(); g.w_dtype = dt; g.out = out.data(); g.out_dtype = dt;
+    g.K = K; g.N = N; g.epilogue = launch::Epilogue::kResidual; g.residual = res.data();
+    std::vector<Binding> b = {{a, PC_ACCESS_READ}, {w, PC_ACCESS_READ}, {res, PC_ACCESS_READ}, {out, PC_ACCESS_WRITE}};
+    return std::make_unique<FusedGemvKernel>("MatmulResidual", b, g, std::string("matvec_residual_") + dt_tag(dt));
+}
+
+std::unique_ptr<Kernel> make_qkv(const Tensor& x, const Tensor* nw, float eps, bool add_one, const Tensor& wqkv,
+                                 const Tensor& q_out, const Tensor& kc, const Tensor& vc, int64_t offset,
+                                 const Tensor* pos) {
+    require_rank(wqkv, 2);
+    require_rank(kc, 4);
+    require_rank(q_out, 4);
+    if (!kc.same_shape(vc))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "K and V caches must have the same shape; got " + kc.shape_string() + " and " +
+                                               vc.shape_string() + ".");
+    int64_t K = wqkv[1];
+    int64_t Nkv = kc[1], Smax = kc[2], Hd = kc[3];
+    int64_t Nq = q_out[1];
+    if (kc[0] != 1 || q_out[0] != 1 || q_out[2] != 1 || q_out[3] != Hd)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKV projection is for batch 1, one token: q_out [1,Nq,1,Hd], caches [1,Nkv,Smax,Hd].");
+    if (wqkv[0] != (Nq + 2 * Nkv) * Hd)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "w_qkv must have (Nq + 2*Nkv)*Hd = " + std::to_string((Nq + 2 * Nkv) * Hd) +
+                                               " rows; got " + std::to_string(wqkv[0]) + ".");
+    check_row_vector(x, K, "QKV x");
+    check_norm_weight(nw, K);
+    if (!pos && (offset < 0 || offset >= Smax))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache write range " + std::to_string(offset) + "..<" +
+                                               std::to_string(offset + 1) + " exceeds cache length " + std::to_string(Smax) + ".");
+    if (pos && (pos->dtype() != PC_I32 || pos->element_count() < 1))
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "position must be an i32 tensor with one element.");
+    int dt = x.dtype();
+    if ((dt != PC_F16 && dt != PC_BF16) || wqkv.dtype() != dt || q_out.dtype() != dt || kc.dtype() != dt || vc.dtype() != dt)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "QKV projection needs all tensors f16 or all bf16.");
+    launch::Gemv g{};
+    g.x = x.data(); g.x_dtype = dt; g.w = wqkv.data(); g.w_dtype = dt; g.out = q_out.data(); g.out_dtype = dt;
+    g.K = K; g.N = wqkv[0]; g.has_norm = true; g.norm_weight = nw ? static_cast<const float*>(nw->data()) : nullptr;
+    g.eps = eps; g.add_one = add_one; g.epilogue = launch::Epilogue::kQKV;
+    g.k_cache = kc.data(); g.v_cache = vc.data(); g.q_rows = Nq * Hd; g.kv_rows = Nkv * Hd; g.Hd = Hd; g.Smax = Smax;
+    g.offset = offset; g.pos_dev = pos ? static_cast<const int32_t*>(pos->data()) : nullptr;
+    std::vector<Binding> b = {{x, PC_ACCESS_READ}, {wqkv, PC_ACCESS_READ}, {q_out, PC_ACCESS_WRITE},
+                              {kc, PC_ACCESS_WRITE}, {vc, PC_ACCESS_WRITE}};
+    if (nw) b.push_back({*nw, PC_ACCESS_READ});
+    if (pos) b.push_back({*pos, PC_ACCESS_READ});
+    return std::make_unique<FusedGemvKernel>("QKVProjection", b, g, std::string("qkv_matvec_") + dt_tag(dt));
+}
+
+}  // namespace
+}  // namespace popcorn
+
+using namespace popcorn;
+
+struct pc_kernel {
+    std::unique_ptr<Kernel> impl;
+    std::vector<Binding> bindings;
+};
+
+namespace {
+int wrap(std::unique_ptr<Kernel> k, pc_kernel** out) {
+    auto* pk = new pc_kernel{std::move(k), {}};
+    pk->bindings = pk->impl->tensors();
+    *out = pk;
+    return PC_OK;
+}
+}  // namespace
+
+#define PC_GUARD_BEGIN                       \
+    try {                                    \
+        if (kernel) *kernel = nullptr;
+#define PC_GUARD_END                         \
+    }                                        \
+    catch (const PopcornError& e) {          \
+        set_last_error(e.message);           \
+        return e.code;                       \
+    }                                        \
+    catch (const std::exception& e) {        \
+        set_last_error(e.what());            \
+        return PC_ERR_GPU_INTERNAL;          \
+    }
+
+extern "C" {
+
+void pc_kernel_destroy(pc_kernel* kernel) { delete kernel; }
+
+const char* pc_kernel_name(const pc_kernel* kernel) { return kernel ? kernel->impl->name() : ""; }
+
+int pc_kernel_binding_count(const pc_kernel* kernel) { return kernel ? int(kernel->bindings.size()) : 0; }
+
+int pc_kernel_binding(const pc_kernel* kernel, int index, pc_tensor* tensor, int* access) {
+    if (!kernel || index < 0 || size_t(index) >= kernel->bindings.size()) {
+        set_last_error("binding index out of range.");
+        return PC_ERR_TENSOR_SHAPE_MISMATCH;
+    }
+    if (tensor) *tensor = kernel->bindings[size_t(index)].tensor.d;
+    if (access) *access = kernel->bindings[size_t(index)].access;
+    return PC_OK;
+}
+
+const char* pc_kernel_function_names(const pc_kernel* kernel) {
+    return kernel ? kernel->impl->function_names().c_str() : "";
+}
+
+// FlashAttention.route, FlashAttention.swift:109-113. Sq == 1 -> decoding;
+// Sq >= 32 with a 16-bit dtype and hd in the tensor-core kernel's set ->
+// tensor; otherwise plain. (The final decision for "tensor" also checks
+// shapes in the launcher; pc_kernel_function_names shows the result.)
+int pc_flash_attention_route(int64_t query_len, int64_t head_dim, int32_t dtype) {
+    if (query_len == 1) return PC_PATH_DECODING;
+    if (query_len >= 32 && head_dim <= 512 && (dtype == PC_BF16 || dtype == PC_F16)) return PC_PATH_TENSOR;
+    return PC_PATH_PLAIN;
+}
+
+int pc_encoder_encode(pc_encoder* encoder, const pc_kernel* k) {
+    try {
+        if (!encoder || !k) fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, "encoder or kernel is null.");
+        encoder_impl(encoder).encode(*k->impl);
+    } catch (const PopcornError& e) {
+        set_last_error(e.message);
+        return e.code;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return PC_ERR_GPU_INTERNAL;
+    }
+    return PC_OK;
+}
+
+int pc_kernel_flash_attention_dims(const pc_tensor* q, const pc_tensor* k, const pc_tensor* v, const pc_tensor* out,
+                                   int64_t batch, int64_t query_heads, int64_t kv_heads, int64_t query_len,
+                                   int64_t key_len, int64_t head_dim, float scale, pc_attention_mask mask,
+                                   pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<FlashAttentionKernel>(tensor_arg(q, "q"), tensor_arg(k, "k"), tensor_arg(v, "v"),
+                                                       tensor_arg(out, "out"), nullptr, batch, query_heads, kv_heads,
+                                                       query_len, key_len, head_dim, scale, mask),
+                kernel);
+    PC_GUARD_END
+}
+
+// FlashAttention.swift:51-90.
+int pc_kernel_flash_attention(const pc_tensor* q, const pc_tensor* k, const pc_tensor* v, const pc_tensor* out,
+                              float scale, pc_attention_mask mask, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor tq = tensor_arg(q, "q"), tk = tensor_arg(k, "k"), tv = tensor_arg(v, "v"), to = tensor_arg(out, "out");
+    require_rank(tq, 4);
+    require_rank(tk, 4);
+    require_rank(tv, 4);
+    int64_t B = tq[0], Nq = tq[1], Sq = tq[2], Hd = tq[3], Nkv = tk[1], Sk = tk[2];
+    if (tk[0] != B || tk[3] != Hd)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention K shape must match Q batch/headDim; q " + tq.shape_string() +
+                                               ", k " + tk.shape_string() + ".");
+    if (!tv.same_shape(tk))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention V shape must match K; v " + tv.shape_string() + ", k " +
+                                               tk.shape_string() + ".");
+    std::vector<int64_t> expected = {B, Nq, Sq, Hd};
+    if (to.dims() != expected)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashAttention output shape must be " + dims_string(expected) + "; got " +
+                                               to.shape_string() + ".");
+    return wrap(std::make_unique<FlashAttentionKernel>(tq, tk, tv, to, nullptr, B, Nq, Nkv, Sq, Sk, Hd, scale, mask),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_flash_decoding_ragged(const pc_tensor* q, const pc_tensor* k_cache, const pc_tensor* v_cache,
+                                    const pc_tensor* seq_lens, const pc_tensor* out, float scale,
+                                    pc_attention_mask mask, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor tq = tensor_arg(q, "q"), tk = tensor_arg(k_cache, "k_cache"), tv = tensor_arg(v_cache, "v_cache"),
+           tl = tensor_arg(seq_lens, "seq_lens"), to = tensor_arg(out, "out");
+    require_rank(tq, 4);
+    require_rank(tk, 4);
+    int64_t B = tq[0], Nq = tq[1], Sq = tq[2], Hd = tq[3], Nkv = tk[1], Smax = tk[2];
+    if (Sq != 1) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "ragged FlashDecoding takes one query token per sequence.");
+    if (tk[0] != B || tk[3] != Hd || !tv.same_shape(tk))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "K/V caches must be [B,Nkv,Smax,Hd] matching q; q " + tq.shape_string() +
+                                               ", k " + tk.shape_string() + ", v " + tv.shape_string() + ".");
+    if (to.dims() != tq.dims())
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "FlashDecoding output shape must be " + tq.shape_string() + "; got " +
+                                               to.shape_string() + ".");
+    if (Smax < 1) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache length must be >= 1.");
+    return wrap(std::make_unique<FlashAttentionKernel>(tq, tk, tv, to, &tl, B, Nq, Nkv, 1, Smax, Hd, scale, mask), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_kv_cache_write_dims(const pc_tensor* source, const pc_tensor* cache, int64_t batch, int64_t kv_heads,
+                                  int64_t new_len, int64_t max_len, int64_t head_dim, int64_t offset,
+                                  pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<KVCacheWriteKernel>(tensor_arg(source, "source"), tensor_arg(cache, "cache"), batch,
+                                                     kv_heads, new_len, max_len, head_dim, offset),
+                kernel);
+    PC_GUARD_END
+}
+
+// KVCacheWrite.swift:38-49.
+int pc_kernel_kv_cache_write(const pc_tensor* source, const pc_tensor* cache, int64_t offset, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor s = tensor_arg(source, "source"), c = tensor_arg(cache, "cache");
+    require_rank(s, 4);
+    require_rank(c, 4);
+    if (c[0] != s[0] || c[1] != s[1] || c[3] != s[3])
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache shape must match source batch/heads/headDim; source " +
+                                               s.shape_string() + ", cache " + c.shape_string() + ".");
+    return wrap(std::make_unique<KVCacheWriteKernel>(s, c, s[0], s[1], s[2], c[2], s[3], offset), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_rmsnorm_dims(const pc_tensor* x, const pc_tensor* weight, const pc_tensor* out, int64_t row_count,
+                           int64_t hidden_size, float eps, int32_t add_one_to_weight, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor w;
+    if (weight) w = tensor_arg(weight, "weight");
+    return wrap(std::make_unique<RMSNormKernel>(tensor_arg(x, "x"), weight ? &w : nullptr, tensor_arg(out, "out"),
+                                                row_count, hidden_size, eps, add_one_to_weight != 0),
+                kernel);
+    PC_GUARD_END
+}
+
+// RMSNorm.swift:39-70.
+int pc_kernel_rmsnorm(const pc_tensor* x, const pc_tensor* weight, const pc_tensor* out, int32_t axis, float eps,
+                      int32_t add_one_to_weight, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor tx = tensor_arg(x, "x"), to = tensor_arg(out, "out");
+    int rank = tx.rank();
+    int norm_axis = axis < 0 ? rank + axis : axis;
+    if (rank <= 0 || norm_axis != rank - 1)
+        fail(PC_ERR_TENSOR_INVALID_AXIS, "Axis " + std::to_string(axis) + " is invalid for a tensor of rank " +
+                                             std::to_string(rank) + ".");
+    if (!tx.same_shape(to))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RMSNorm output shape must match input; got " + to.shape_string() +
+                                               ", expected " + tx.shape_string() + ".");
+    int64_t H = tx[norm_axis];
+    int64_t rows = H > 0 ? tx.element_count() / H : 0;
+    Tensor w;
+    if (weight) {
+        w = tensor_arg(weight, "weight");
+        bool ok = (w.rank() == 1 && w[0] == H) || w.same_shape(tx);
+        if (!ok)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RMSNorm weight shape must be [" + std::to_string(H) + "] or " +
+                                                   tx.shape_string() + "; got " + w.shape_string() + ".");
+    }
+    return wrap(std::make_unique<RMSNormKernel>(tx, weight ? &w : nullptr, to, rows, H, eps, add_one_to_weight != 0),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_matmul_dims(const pc_tensor* a, const pc_tensor* b, const pc_tensor* c, int64_t m, int64_t k, int64_t n,
+                          int32_t transpose_b, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<MatmulKernel>(tensor_arg(a, "a"), tensor_arg(b, "b"), tensor_arg(c, "c"), m, k, n,
+                                               transpose_b != 0),
+                kernel);
+    PC_GUARD_END
+}
+
+// Matmul.swift:68-93.
+int pc_kernel_matmul(const pc_tensor* a, const pc_tensor* b, const pc_tensor* c, int32_t transpose_b, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor ta = tensor_arg(a, "a"), tb = tensor_arg(b, "b"), tc = tensor_arg(c, "c");
+    require_rank(ta, 2);
+    require_rank(tb, 2);
+    require_rank(tc, 2);
+    int64_t m = ta[0], k = ta[1];
+    int64_t n = transpose_b ? tb[0] : tb[1];
+    std::vector<int64_t> eb = transpose_b ? std::vector<int64_t>{n, k} : std::vector<int64_t>{k, n};
+    std::vector<int64_t> ec = {m, n};
+    if (tb.dims() != eb)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul RHS shape mismatch: expected " + dims_string(eb) + ", got " +
+                                               tb.shape_string() + ".");
+    if (tc.dims() != ec)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul output shape mismatch: expected " + dims_string(ec) + ", got " +
+                                               tc.shape_string() + ".");
+    return wrap(std::make_unique<MatmulKernel>(ta, tb, tc, m, k, n, transpose_b != 0), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_gelu_tanh(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<UnaryKernel>(launch::Unary::kGeluTanh, tensor_arg(x, "x"), tensor_arg(out, "out")), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_silu(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<UnaryKernel>(launch::Unary::kSilu, tensor_arg(x, "x"), tensor_arg(out, "out")), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_mul(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<BinaryKernel>(launch::Binary::kMul, tensor_arg(a, "a"), tensor_arg(b, "b"),
+                                               tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_add(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<BinaryKernel>(launch::Binary::kAdd, tensor_arg(a, "a"), tensor_arg(b, "b"),
+                                               tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_rmsnorm_matmul(const pc_tensor* x, const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                             const pc_tensor* w, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(make_rmsnorm_matmul(tensor_arg(x, "x"), norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
+                                    tensor_arg(w, "w"), tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_gated_mlp(const pc_tensor* x, const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                        const pc_tensor* w_gate, const pc_tensor* w_up, int32_t activation, const pc_tensor* out,
+                        pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(make_gated_mlp(tensor_arg(x, "x"), norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
+                               tensor_arg(w_gate, "w_gate"), tensor_arg(w_up, "w_up"), activation,
+                               tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_matmul_residual(const pc_tensor* a, const pc_tensor* w, const pc_tensor* residual, const pc_tensor* out,
+                              pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(make_matmul_residual(tensor_arg(a, "a"), tensor_arg(w, "w"), tensor_arg(residual, "residual"),
+                                     tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                             const pc_tensor* w_qkv, const pc_tensor* q_out, const pc_tensor* k_cache,
+                             const pc_tensor* v_cache, int64_t offset, const pc_tensor* position, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw, pos;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    if (position) pos = tensor_arg(position, "position");
+    return wrap(make_qkv(tensor_arg(x, "x"), norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
+                         tensor_arg(w_qkv, "w_qkv"), tensor_arg(q_out, "q_out"), tensor_arg(k_cache, "k_cache"),
+                         tensor_arg(v_cache, "v_cache"), offset, position ? &pos : nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+}  // extern "C"

@@ -1,0 +1,157 @@
+"""Decode-layer composition over the C ABI (the hot path the benchmark runs).
+
+The layer follows the reference's decode-layer template
+(Examples/GemmaCLI/Sources/GemmaCLI/Gemma4TextInference.swift:312-436),
+restricted to BASELINE's layer list (RMSNorm, QKV matvec, KV-cache write,
+GQA flash-decode, o_proj, gated MLP) plus the two residual adds:
+
+    xn   = RMSNorm(x) ; q,k,v = W_qkv xn ; KVCacheWrite(k, v at pos)
+    attn = FlashDecoding(q, caches[:pos+1])
+    h    = x + W_o attn
+    act  = act(W_gate RMSNorm(h)) * (W_up RMSNorm(h))
+    out  = h + W_down act
+
+It is encoded as five fused kernels per layer (six launches when the
+decode attention splits its keys), each equal to the reference op sequence
+with the same rounding points:
+
+    QKVProjection (RMSNorm + matvec + KV write)  -> FlashDecodingRagged
+    -> MatmulResidual (o_proj + Add) -> GatedMLP (RMSNorm + gate/up + act*up)
+    -> MatmulResidual (down_proj + Add)
+
+The position lives in device memory, so one captured CUDA graph serves
+every decode step.
+"""
+from .api import AttentionMask, FixedScratch, KernelCommandEncoder, Kernels
+
+
+class LayerShape:
+    """Gemma-2-2B-shape layer."""
+
+    def __init__(self, hidden=2304, q_heads=8, kv_heads=4, head_dim=256, ffn=9216, max_ctx=4096, dtype="f16",
+                 eps=1e-6, attn_scale=1.0 / 16, activation=0):
+        self.H, self.Nq, self.Nkv, self.Hd, self.F = hidden, q_heads, kv_heads, head_dim, ffn
+        self.Smax = max_ctx
+        self.dtype = dtype
+        self.eps = eps
+        self.scale = attn_scale
+        self.activation = activation  # 0 GeGLU (gelu_tanh), 1 SwiGLU (silu)
+
+    @property
+    def weight_params(self):
+        H, Nq, Nkv, Hd, F = self.H, self.Nq, self.Nkv, self.Hd, self.F
+        return (Nq + 2 * Nkv) * Hd * H + H * Nq * Hd + 2 * F * H + H * F
+
+    @property
+    def elem(self):
+        return 4 if self.dtype == "f32" else 2
+
+    def kv_bytes(self, ctx):
+        return 2 * self.Nkv * ctx * self.Hd * self.elem
+
+    def bytes_per_token(self, ctx):
+        """Algorithmic HBM bytes of one layer at context ctx: every weight
+        once, K and V of ctx keys once."""
+        return self.weight_params * self.elem + self.kv_bytes(ctx)
+
+
+def _torch_dtype(dt):
+    import torch
+    return {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dt]
+
+
+class DecodeLayerWeights:
+    """Random-init weights N(0, 0.02) and a pre-filled KV cache N(0, 1)."""
+
+    def __init__(self, shape, generator, device="cuda"):
+        import torch
+        s = shape
+        tdt = _torch_dtype(s.dtype)
+
+        def randn(*sz, std=1.0):
+            return (torch.randn(*sz, generator=generator, device=device, dtype=torch.float32) * std).to(tdt)
+
+        self.attn_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
+        self.mlp_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
+        self.w_qkv = randn((s.Nq + 2 * s.Nkv) * s.Hd, s.H, std=0.02)
+        self.w_o = randn(s.H, s.Nq * s.Hd, std=0.02)
+        self.w_gate = randn(s.F, s.H, std=0.02)
+        self.w_up = randn(s.F, s.H, std=0.02)
+        self.w_down = randn(s.H, s.F, std=0.02)
+        self.k_cache = randn(1, s.Nkv, s.Smax, s.Hd)
+        self.v_cache = randn(1, s.Nkv, s.Smax, s.Hd)
+
+
+class DecodeStack:
+    """A stack of decode layers with its activations, position and scratch.
+
+    encode_step() enqueues one token through every layer on the encoder's
+    stream; `x` holds the token's hidden state on entry and the stack's
+    output on exit (it ping-pongs through two buffers).
+    """
+
+    def __init__(self, library, shape, n_layers, seed=0, device=0):
+        import torch
+        self.shape = shape
+        self.library = library
+        self.device = device
+        g = torch.Generator(device="cuda:%d" % device)
+        g.manual_seed(seed)
+        self.layers = [DecodeLayerWeights(shape, g) for _ in range(n_layers)]
+        s = shape
+        tdt = _torch_dtype(s.dtype)
+        dev = "cuda:%d" % device
+        self.x = torch.zeros(1, s.H, dtype=tdt, device=dev)
+        self.x2 = torch.zeros(1, s.H, dtype=tdt, device=dev)
+        self.h = torch.zeros(1, s.H, dtype=tdt, device=dev)
+        self.q = torch.zeros(1, s.Nq, 1, s.Hd, dtype=tdt, device=dev)
+        self.attn = torch.zeros(1, s.Nq, 1, s.Hd, dtype=tdt, device=dev)
+        self.act = torch.zeros(1, s.F, dtype=tdt, device=dev)
+        # device-resident position state: [pos, pos + 1]
+        self.pos_state = torch.zeros(2, dtype=torch.int32, device=dev)
+        # scratch for the decode attention partials (reused by every layer)
+        self.scratch = FixedScratch(64 << 20, device)
+        self._kernels = None
+
+    def kernels(self):
+        """The validated kernel objects of one step (built once)."""
+        if self._kernels is not None:
+            return self._kernels
+        s = self.shape
+        pos = self.pos_state[0:1]
+        lens = self.pos_state[1:2]
+        ks = []
+        cur, nxt = self.x, self.x2
+        for i, w in enumerate(self.layers):
+            ks.append(Kernels.QKVProjection(cur, w.attn_norm, w.w_qkv, self.q, w.k_cache, w.v_cache, position=pos,
+                                            eps=s.eps, add_one_to_weight=True))
+            ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
+                                                  mask=AttentionMask.causal))
+            ks.append(Kernels.MatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
+            ks.append(Kernels.GatedMLP(self.h, w.w_gate, w.w_up, into=self.act, norm_weight=w.mlp_norm, eps=s.eps,
+                                       add_one_to_weight=True, activation=s.activation))
+            ks.append(Kernels.MatmulResidual(self.act, w.w_down, self.h, into=nxt))
+            cur, nxt = nxt, cur
+        self.out = cur
+        self._kernels = ks
+        return ks
+
+    def encoder(self, stream=None):
+        return KernelCommandEncoder(self.library, stream=stream, scratch=self.scratch)
+
+    def set_position(self, pos):
+        self.pos_state.copy_(self._pos_tensor(pos))
+
+    def _pos_tensor(self, pos):
+        import torch
+        return torch.tensor([pos, pos + 1], dtype=torch.int32)
+
+    def encode_step(self, encoder):
+        encoder.encode(*self.kernels())
+        return self.out
+
+    def algorithmic_bytes_per_step(self, ctx):
+        return len(self.layers) * self.shape.bytes_per_token(ctx)
+
+
+__all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack"]
