@@ -55,7 +55,7 @@ def bf16_ulp(x):
     return 2.0 ** (np.floor(np.log2(ax)) - 7)
 
 
-def assert_close(got, exp, dt, atol=ATOL, rtol=RTOL, what=""):
+def assert_close(got, exp, dt, atol=ATOL, rtol=RTOL, what="", bf16_ulps=1):
     """north_star tolerance: within atol + rtol*|exp|. For bf16 outputs a
     difference of one bf16 ulp is also accepted: the tolerance is finer than
     bf16's spacing, so a last-bit rounding flip of two fp32 sums that agree
@@ -67,7 +67,7 @@ def assert_close(got, exp, dt, atol=ATOL, rtol=RTOL, what=""):
     err = np.abs(g - e)
     tol = atol + rtol * np.abs(e)
     if dt == "bf16":
-        tol = np.maximum(tol, bf16_ulp(e) * 1.001)
+        tol = np.maximum(tol, bf16_ulp(e) * bf16_ulps * 1.001)
     bad = err > tol
     if bad.any():
         i = np.argmax(err - tol)

@@ -1,31 +1,116 @@
-"""The decode layer (config-2 shapes) through the C ABI vs the oracle's
-composition of the reference ops (oracle.decode_layer)."""
+"""The decode layer (BASELINE config-2 shapes) through the C ABI vs the
+oracle's composition of the reference ops.
+
+Stage-wise: each fused kernel of the layer is checked against the oracle's
+op sequence on the GPU's own inputs, at the per-kernel tolerance.
+Whole-layer: the GPU output against oracle.decode_layer from the same
+inputs. f16 meets the per-kernel tolerance end to end. bf16 has 10+
+rounding points in a row with 8-bit significands; one intermediate that
+rounds one ulp apart (both sides agree to ~1e-6 before rounding) moves
+later values by several ulps, so the whole-layer bf16 check uses a
+relative-L2 bound and an 8-ulp pointwise bound instead.
+"""
 import numpy as np
 import pytest
 
 import __graft_entry__ as ge
 import oracle
-from tests.gpu_util import assert_close
+from tests.gpu_util import assert_close, bf16_ulp, from_dev
 
 pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _stack(dt, ctx, pos, act, seed):
+    import popcorn_b200 as pc
+    from popcorn_b200.decode import DecodeStack, LayerShape
+    shape = LayerShape(max_ctx=ctx, dtype=dt, activation=act)
+    st = DecodeStack(pc.KernelLibrary(0), shape, 1, seed=seed)
+    st.set_position(pos)
+    st.x.normal_(generator=torch.Generator(device="cuda").manual_seed(seed))
+    return st
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("act", [0, 1])
+def test_decode_layer_stagewise(dt, act):
+    ctx, pos = 4096, 4095
+    st = _stack(dt, ctx, pos, act, seed=11 + act)
+    s = st.shape
+    ks = st.kernels()
+    enc = st.encoder()
+    w = st.layers[0]
+
+    def H(t):
+        return from_dev(t, dt)
+
+    x0 = H(st.x)[0]
+    kc0, vc0 = H(w.k_cache)[0].copy(), H(w.v_cache)[0].copy()
+    nw_a, nw_m = w.attn_norm.cpu().numpy(), w.mlp_norm.cpu().numpy()
+    QN, KN = s.Nq * s.Hd, s.Nkv * s.Hd
+
+    enc.encode(ks[0])
+    torch.cuda.synchronize()
+    xn = oracle.rmsnorm(x0, dt, nw_a, eps=s.eps, add_one=True)
+    qkv = oracle.matvec_nk(xn, dt, H(w.w_qkv), dt, dt)
+    q = H(st.q).ravel()
+    kc, vc = H(w.k_cache)[0], H(w.v_cache)[0]
+    assert_close(q, qkv[:QN], dt, what="q")
+    assert_close(kc[:, pos].ravel(), qkv[QN:QN + KN], dt, what="k row")
+    assert_close(vc[:, pos].ravel(), qkv[QN + KN:], dt, what="v row")
+    other = np.ones(ctx, bool)
+    other[pos] = False
+    assert np.array_equal(kc[:, other].view(np.uint16), kc0[:, other].view(np.uint16))
+
+    enc.encode(ks[1])
+    torch.cuda.synchronize()
+    attn = H(st.attn).ravel()
+    exp_attn = oracle.flash_decoding(q.reshape(1, s.Nq, 1, s.Hd), dt, kc[None], vc[None], dt, dt, s.scale,
+                                     seq_lens=np.array([pos + 1], np.int32))
+    assert_close(attn, exp_attn.ravel(), dt, what="attention")
+
+    enc.encode(ks[2])
+    torch.cuda.synchronize()
+    h = H(st.h)[0]
+    o = oracle.matvec_nk(attn, dt, H(w.w_o), dt, dt)
+    assert_close(h, oracle.add(x0, o, dt), dt, what="o_proj + residual")
+
+    enc.encode(ks[3])
+    torch.cuda.synchronize()
+    a = H(st.act)[0]
+    hn = oracle.rmsnorm(h, dt, nw_m, eps=s.eps, add_one=True)
+    g = oracle.matvec_nk(hn, dt, H(w.w_gate), dt, dt)
+    u = oracle.matvec_nk(hn, dt, H(w.w_up), dt, dt)
+    av = oracle.silu(g, dt) if act == 1 else oracle.gelu_tanh(g, dt)
+    # act(round(g)) is rounded, then multiplied and rounded again: a one-ulp
+    # flip of the first rounding shows as up to two ulps of the product.
+    assert_close(a, oracle.mul(av, u, dt), dt, what="gated mlp", bf16_ulps=2)
+
+    enc.encode(ks[4])
+    torch.cuda.synchronize()
+    out = H(st.out)[0]
+    d = oracle.matvec_nk(a, dt, H(w.w_down), dt, dt)
+    assert_close(out, oracle.add(h, d, dt), dt, what="down_proj + residual")
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("ctx,pos", [(4096, 4095), (512, 300)])
-def test_decode_layer_config2(dt, act, ctx, pos):
+def test_decode_layer_whole(dt, act, ctx, pos):
     from popcorn_b200.decode import LayerShape
     shape = LayerShape(max_ctx=ctx, dtype=dt, activation=act)
     g, e, (kc, vc), ins = ge.smoke_layer(shape, pos=pos, seed=ctx + act)
-    gd = oracle.to_dtype(g, dt)
-    assert_close(gd, oracle.to_dtype(e, dt), dt, what="layer output")
-    # the new K/V rows equal what the oracle's KVCacheWrite stored
-    assert_close(kc[:, pos], ins["k_cache"][:, pos], dt, what="k row")
-    assert_close(vc[:, pos], ins["v_cache"][:, pos], dt, what="v row")
-    # every other row is untouched
     other = np.ones(ctx, bool)
     other[pos] = False
     assert np.array_equal(kc[:, other].view(np.uint16), ins["k_cache"][:, other].view(np.uint16))
+    assert_close(kc[:, pos], ins["k_cache"][:, pos], dt, what="k row")
+    assert_close(vc[:, pos], ins["v_cache"][:, pos], dt, what="v row")
+    if dt == "f16":
+        assert_close(oracle.to_dtype(g, dt), oracle.to_dtype(e, dt), dt, what="layer output")
+    else:
+        rel = np.linalg.norm(g - e) / np.linalg.norm(e)
+        assert rel < 5e-3, rel
+        assert (np.abs(g - e) <= np.maximum(1e-3 + 2e-3 * np.abs(e), 8 * bf16_ulp(e))).all()
 
 
 def test_smoke():
