@@ -8,7 +8,8 @@ inputs. f16 meets the per-kernel tolerance end to end. bf16 has 10+
 rounding points in a row with 8-bit significands; one intermediate that
 rounds one ulp apart (both sides agree to ~1e-6 before rounding) moves
 later values by several ulps, so the whole-layer bf16 check uses a
-relative-L2 bound and an 8-ulp pointwise bound instead.
+relative-L2 bound and an 8-ulp pointwise bound (ulps at the output's RMS
+scale) instead.
 """
 import numpy as np
 import pytest
@@ -110,7 +111,10 @@ def test_decode_layer_whole(dt, act, ctx, pos):
     else:
         rel = np.linalg.norm(g - e) / np.linalg.norm(e)
         assert rel < 5e-3, rel
-        assert (np.abs(g - e) <= np.maximum(1e-3 + 2e-3 * np.abs(e), 8 * bf16_ulp(e))).all()
+        # Outputs near zero come from h + d with |h|, |d| ~ 1 (cancellation),
+        # so the ulps are counted at the output's RMS scale.
+        scale = np.maximum(np.abs(e), np.sqrt(np.mean(e.astype(np.float64) ** 2)))
+        assert (np.abs(g - e) <= np.maximum(1e-3 + 2e-3 * np.abs(e), 8 * bf16_ulp(scale))).all()
 
 
 def test_smoke():
