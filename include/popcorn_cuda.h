@@ -277,6 +277,34 @@ PC_API int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_we
                                     const pc_tensor* k_cache, const pc_tensor* v_cache, int64_t offset,
                                     const pc_tensor* position, pc_kernel** kernel);
 
+/* ---- decode attention without allocation ------------------------------- */
+
+/* No counterpart in the reference. For callers that cannot allocate device
+ * memory — code enqueuing work while a stream is captured into a CUDA graph,
+ * real-time decode loops that must never allocate (an allocation can
+ * synchronise the device), hosts whose device memory belongs to another
+ * framework's pool — this runs the same decode attention as
+ * pc_kernel_flash_attention (Sq == 1) / pc_kernel_flash_decoding_ragged
+ * (seq_lens != NULL) with the same split plan, so the results are
+ * identical, but keeps the partial (m, l, O) buffers in a fixed device array
+ * inside this library instead of borrowing them from a scratch allocator.
+ * The caller passes q [B,Nq,1,Hd], k/v [B,Nkv,S,Hd], out [B,Nq,1,Hd] and
+ * an optional seq_lens (i32 [B] on the device); the work is enqueued on
+ * `stream` (cudaStream_t) of the current device.
+ *  - The array holds pc_flash_decoding_noalloc_capacity() bytes (1 MiB) on
+ *    every GPU that loads the library, until the process exits. A problem
+ *    whose partials need more is rejected with PC_ERR_WORKSPACE_EXHAUSTED
+ *    before anything is launched.
+ *  - Every call shares the array and leaves its contents behind; nothing in
+ *    it has to start at zero. Calls whose GPU work overlaps (e.g. on two
+ *    streams with no ordering) race on it.
+ *  - The first call on a device looks up the array's device address; make
+ *    that first call before any stream capture begins.
+ * It calls no cudaMalloc / cudaFree and no allocating library routine. */
+PC_API int pc_flash_decoding_noalloc(const pc_tensor* q, const pc_tensor* k, const pc_tensor* v, const pc_tensor* out,
+                                     const pc_tensor* seq_lens, float scale, pc_attention_mask mask, void* stream);
+PC_API size_t pc_flash_decoding_noalloc_capacity(void);
+
 #ifdef __cplusplus
 }
 #endif
