@@ -8,24 +8,27 @@
 // (:182-231). Sliding-window masks keep keys with posQ - j < window (:97-99).
 //
 // B200 design.
-//  * One CTA per (b, KV head, head group, split): the G query heads that
-//    share a KV head are served from ONE read of their K/V rows (the
-//    reference re-reads K/V once per query head).
-//  * K and V tiles of 32 keys stream HBM -> shared memory with the Blackwell
-//    bulk-copy engine (cp.async.bulk, 1-D, no multicast) into a 2-4 stage
-//    ring tracked by mbarriers; one elected thread issues the copies, so
-//    the SM's warps only compute while up to 96 KB per CTA is in flight.
-//  * Each warp scores 8 keys per tile: lanes hold Hd/32 contiguous head
-//    dims (one 16-byte shared load per key row at Hd 256, conflict-free),
-//    then a transpose-reduction folds the 8 x G partial dots across the warp
-//    in 9G shuffles instead of 40G.
-//  * The split count is chosen so the grid fills every SM; a second small
-//    kernel merges the splits (skipped when one split covers the keys).
+//  * One CTA per (b, KV head, head group, split), sized to one wave (one
+//    CTA per SM): the G query heads that share a KV head are served from ONE
+//    read of their K/V rows (the reference re-reads K/V once per query head).
+//  * A producer warp streams 32-key K and V tiles HBM -> shared memory with
+//    the bulk-copy engine (cp.async.bulk, 1-D, no multicast) into a ring of
+//    up to 8 stages (<= 192 KB in flight per SM), tracked by full/empty
+//    mbarriers.
+//  * Two groups of four consumer warps take alternate tiles; each warp
+//    scores 8 keys per tile: lanes hold Hd/32 contiguous head dims (one
+//    16-byte shared load per key row at Hd 256, conflict-free), then a
+//    transpose-reduction folds the 8 x G partial dots across the warp in 9G
+//    shuffles instead of 40G. Online softmax per warp; the eight warp states
+//    merge at the end.
+//  * The split count is chosen for whole waves over the SMs; a small
+//    parallel kernel merges the splits (skipped with one split).
 //  * Every mbarrier wait is bounded; a wait that gives up sets a device
 //    error word (pc_device_error_check) and the CTA drains its copies and
 //    leaves.
 #include <algorithm>
 
+#include "async.cuh"
 #include "common.cuh"
 #include "dtype.cuh"
 #include "launch.hpp"
@@ -39,53 +42,13 @@ namespace launch {
 
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = 4;
 constexpr int kTileKeys = 32;  // 8 keys per warp per tile
+constexpr int kGroups = 2;     // consumer groups (alternate tiles)
+constexpr int kCWarps = 4 * kGroups;
+constexpr int kFastThreads = (kCWarps + 1) * 32;
+constexpr int kThreads = 128;  // generic and combine kernels
+constexpr int kWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
-
-// ---- mbarrier / bulk-copy primitives -------------------------------------
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(100000u)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait: ~20k suspended tries of <= 0.1 ms each.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (int i = 0; i < 20000; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    atomicOr(&g_fd_error_word, 1u);
-    return false;
-}
-
-// ---- lane slice loads ----------------------------------------------------------
 
 // E consecutive elements of a row (in shared memory) -> floats.
 template <class KV, int E>
@@ -122,19 +85,14 @@ struct FDShape {
     static constexpr int kRowBytes = HD * Elem<KV>::bytes;
     static constexpr int kTileBytes = kTileKeys * kRowBytes;  // one of K or V
     static constexpr int kStageBytes = 2 * kTileBytes;
-    static constexpr int kStages = (2 * kStageBytes > 200 * 1024) ? 1 : std::max(2, std::min(4, 98304 / kStageBytes));
+    static constexpr int kStages = std::max(1, std::min(8, 196608 / kStageBytes));
 };
-
-template <int G, int HD>
-constexpr int merge_bytes() {
-    return kWarps * G * (HD + 2) * 4;
-}
 
 template <class KV, int HD, int G>
 constexpr size_t fd_smem_bytes() {
     using S = FDShape<KV, HD>;
     size_t ring = size_t(S::kStages) * S::kStageBytes;
-    size_t merge = size_t(merge_bytes<G, HD>());
+    size_t merge = size_t(kCWarps) * G * (HD + 2) * 4;
     return ring > merge ? ring : merge;
 }
 
@@ -160,21 +118,22 @@ __device__ __forceinline__ void split_range(const FDArgs& a, int64_t len, int sp
     }
 }
 
-// Writes this CTA's (m, l, O) for heads hq0..hq0+G-1, or the normalised
-// output when the plan has a single split.
-template <int G, int HD>
+// Merges the NW warp states (mm/ll [NW][G], oo [NW][G][HD]) and writes this
+// CTA's (m, l, O) for heads hq0..hq0+G-1 — or the normalised output when the
+// plan has a single split.
+template <int G, int HD, int NW>
 __device__ __forceinline__ void write_result(const FDArgs& a, int64_t b, int64_t hq0, int split, const float* mm,
-                                             const float* ll, const float* oo, int tid) {
+                                             const float* ll, const float* oo, int tid, int nthreads) {
     const FlashDecode& p = a.p;
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
+    for (int idx = tid; idx < G * HD; idx += nthreads) {
         int g = idx / HD, d = idx % HD;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * G + g]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, mm[w * G + g]);
         float L = 0.f, O = 0.f;
         if (M != -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
+            for (int w = 0; w < NW; ++w) {
                 float mw = mm[w * G + g];
                 float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
                 L += f * ll[w * G + g];
@@ -200,12 +159,15 @@ __device__ __forceinline__ void write_result(const FDArgs& a, int64_t b, int64_t
 }
 
 template <class KV, int HD, int G>
-__global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
+__global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArgs a) {
     using S = FDShape<KV, HD>;
     constexpr int E = S::E;
     constexpr int NST = S::kStages;
     extern __shared__ __align__(128) char smem[];
-    __shared__ __align__(8) uint64_t bars[4];
+    __shared__ __align__(8) uint64_t full[NST], empty[NST];
+    __shared__ volatile int s_abort;
+    __shared__ volatile int s_issued;
+    __shared__ volatile int s_consumed[kGroups];
 
     pdl_launch_dependents();
     const FlashDecode& p = a.p;
@@ -218,8 +180,14 @@ __global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
     const int64_t hq0 = hkv * gtot + int64_t(hg) * G;
 
     if (tid == 0) {
-        for (int s = 0; s < NST; ++s) mbar_init(smem_addr(&bars[s]), 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 4);  // the four warps of the group that read it
+        }
+        s_abort = 0;
+        s_issued = 0;
+        for (int g = 0; g < kGroups; ++g) s_consumed[g] = 0;
+        mbar_fence_init();
     }
     __syncthreads();
 
@@ -230,17 +198,17 @@ __global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
     split_range(a, len, split, jb, je);
 
     float* mm = reinterpret_cast<float*>(smem);
-    float* ll = mm + kWarps * G;
-    float* oo = ll + kWarps * G;
+    float* ll = mm + kCWarps * G;
+    float* oo = ll + kCWarps * G;
 
     if (jb >= je) {  // no keys for this split (FlashDecoding.metal:78-87)
-        if (tid < kWarps * G) {
+        if (tid < kCWarps * G) {
             mm[tid] = -INFINITY;
             ll[tid] = 0.f;
         }
-        for (int i = tid; i < kWarps * G * HD; i += kThreads) oo[i] = 0.f;
+        for (int i = tid; i < kCWarps * G * HD; i += kFastThreads) oo[i] = 0.f;
         __syncthreads();
-        write_result<G, HD>(a, b, hq0, split, mm, ll, oo, tid);
+        write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, tid, kFastThreads);
         return;
     }
 
@@ -248,30 +216,6 @@ __global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
     const char* kbase = static_cast<const char*>(p.k) + head_off * Elem<KV>::bytes;
     const char* vbase = static_cast<const char*>(p.v) + head_off * Elem<KV>::bytes;
     const int ntiles = int((je - jb + kTileKeys - 1) / kTileKeys);
-
-    auto issue = [&](int t) {
-        int s = t % NST;
-        int64_t j0 = jb + int64_t(t) * kTileKeys;
-        int64_t nk = je - j0 < kTileKeys ? je - j0 : kTileKeys;
-        uint32_t bytes = uint32_t(nk) * S::kRowBytes;
-        uint32_t bar = smem_addr(&bars[s]);
-        mbar_expect_tx(bar, 2 * bytes);
-        char* st = smem + size_t(s) * S::kStageBytes;
-        bulk_g2s(smem_addr(st), kbase + j0 * S::kRowBytes, bytes, bar);
-        bulk_g2s(smem_addr(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
-    };
-    if (tid == 0)
-        for (int t = 0; t < NST && t < ntiles; ++t) issue(t);
-
-    // Query slices (pre-scaled, in log2 units) for the G heads.
-    float q[G][E];
-    const float qs = p.scale * kLog2e;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        int64_t qb = ((b * p.Nq) + hq0 + g) * HD + lane * E;
-#pragma unroll
-        for (int e = 0; e < E; ++e) q[g][e] = Elem<KV>::load(p.q, qb + e) * qs;
-    }
 
     float m[G], l[G], o[G][E];
 #pragma unroll
@@ -282,142 +226,175 @@ __global__ void __launch_bounds__(kThreads) fd_partial_kernel(const FDArgs a) {
         for (int e = 0; e < E; ++e) o[g][e] = 0.f;
     }
 
-    bool bad = false;
-    for (int t = 0; t < ntiles; ++t) {
-        const int s = t % NST;
-        const uint32_t parity = uint32_t(t / NST) & 1u;
-        if (!mbar_wait(smem_addr(&bars[s]), parity)) bad = true;
-        bad = __syncthreads_or(bad);
-        if (bad) break;
-
-        const int64_t j0 = jb + int64_t(t) * kTileKeys;
-        const int nk = int(je - j0 < kTileKeys ? je - j0 : kTileKeys);
-        const int kw0 = warp * 8;  // this warp's first key in the tile
-        const char* ktile = smem + size_t(s) * S::kStageBytes;
-        const char* vtile = ktile + S::kTileBytes;
-
-        if (kw0 < nk) {
-            // Partial dots: vals[i*G + g] for the warp's 8 keys.
-            float vals[8 * G];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float kf[E];
-                if (kw0 + i < nk) {
-                    load_slice<KV, E>(ktile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, kf);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < E; ++e) kf[e] = 0.f;
+    if (warp == kCWarps) {
+        // ---- producer ----
+        if (lane == 0) {
+            for (int t = 0; t < ntiles; ++t) {
+                const int s = t % NST;
+                const uint32_t ph = uint32_t(t / NST) & 1u;
+                if (s_abort || !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, &g_fd_error_word)) {
+                    s_abort = 1;
+                    break;
                 }
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int e = 0; e < E; ++e) acc = fmaf(q[g][e], kf[e], acc);
-                    vals[i * G + g] = acc;
-                }
-            }
-            // Transpose-reduction: after the xor-16/8/4 steps lane L holds
-            // the partial sums of key (L >> 2) & 7; xor-2/1 finish them.
-            {
-                const bool hi = lane & 16;
-#pragma unroll
-                for (int i = 0; i < 4 * G; ++i) {
-                    float lo_v = vals[i], hi_v = vals[i + 4 * G];
-                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
-                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-                }
-            }
-            {
-                const bool hi = lane & 8;
-#pragma unroll
-                for (int i = 0; i < 2 * G; ++i) {
-                    float lo_v = vals[i], hi_v = vals[i + 2 * G];
-                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
-                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-                }
-            }
-            {
-                const bool hi = lane & 4;
-#pragma unroll
-                for (int i = 0; i < G; ++i) {
-                    float lo_v = vals[i], hi_v = vals[i + G];
-                    float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
-                    vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-                }
-            }
-            const int my_key = (lane >> 2) & 7;
-            const bool valid = kw0 + my_key < nk;
-            float pr[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float sv = vals[g];
-                sv += __shfl_xor_sync(0xffffffffu, sv, 2);
-                sv += __shfl_xor_sync(0xffffffffu, sv, 1);
-                float mx = valid ? sv : -INFINITY;
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                float mnew = fmaxf(m[g], mx);
-                float so = exp2f(m[g] - mnew);  // 0 while m is -inf
-                float pv = valid ? exp2f(sv - mnew) : 0.f;
-                float ps = pv;
-                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-                l[g] = l[g] * so + ps;
-                m[g] = mnew;
-#pragma unroll
-                for (int e = 0; e < E; ++e) o[g][e] *= so;
-                pr[g] = pv;
-            }
-            // O += p_i * V_i over the warp's keys.
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float pi[G];
-#pragma unroll
-                for (int g = 0; g < G; ++g) pi[g] = __shfl_sync(0xffffffffu, pr[g], i * 4);
-                if (kw0 + i < nk) {
-                    float vf[E];
-                    load_slice<KV, E>(vtile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, vf);
-#pragma unroll
-                    for (int g = 0; g < G; ++g)
-#pragma unroll
-                        for (int e = 0; e < E; ++e) o[g][e] = fmaf(pi[g], vf[e], o[g][e]);
-                }
+                const int64_t j0 = jb + int64_t(t) * kTileKeys;
+                const int64_t nk = je - j0 < kTileKeys ? je - j0 : kTileKeys;
+                const uint32_t bytes = uint32_t(nk) * S::kRowBytes;
+                const uint32_t bar = smem_u32(&full[s]);
+                mbar_expect_tx(bar, 2 * bytes);
+                char* st = smem + size_t(s) * S::kStageBytes;
+                bulk_g2s(smem_u32(st), kbase + j0 * S::kRowBytes, bytes, bar);
+                bulk_g2s(smem_u32(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
+                s_issued = t + 1;
             }
         }
-        __syncthreads();  // every warp is done with stage s
-        if (tid == 0 && t + NST < ntiles) issue(t + NST);
+    } else {
+        // ---- consumers: group `grp` takes tiles grp, grp + 2, ... ----
+        const int grp = warp >> 2, gw = warp & 3;
+        float q[G][E];
+        const float qs = p.scale * kLog2e;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            int64_t qb = ((b * p.Nq) + hq0 + g) * HD + lane * E;
+#pragma unroll
+            for (int e = 0; e < E; ++e) q[g][e] = Elem<KV>::load(p.q, qb + e) * qs;
+        }
+        for (int t = grp; t < ntiles; t += kGroups) {
+            const int s = t % NST;
+            const uint32_t parity = uint32_t(t / NST) & 1u;
+            if (s_abort || !mbar_wait(smem_u32(&full[s]), parity, &g_fd_error_word)) {
+                s_abort = 1;
+                break;
+            }
+            const int64_t j0 = jb + int64_t(t) * kTileKeys;
+            const int nk = int(je - j0 < kTileKeys ? je - j0 : kTileKeys);
+            const int kw0 = gw * 8;  // this warp's first key in the tile
+            const char* ktile = smem + size_t(s) * S::kStageBytes;
+            const char* vtile = ktile + S::kTileBytes;
+
+            if (kw0 < nk) {
+                // Partial dots: vals[i*G + g] for the warp's 8 keys.
+                float vals[8 * G];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float kf[E];
+                    if (kw0 + i < nk) {
+                        load_slice<KV, E>(ktile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, kf);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < E; ++e) kf[e] = 0.f;
+                    }
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float acc = 0.f;
+#pragma unroll
+                        for (int e = 0; e < E; ++e) acc = fmaf(q[g][e], kf[e], acc);
+                        vals[i * G + g] = acc;
+                    }
+                }
+                // Transpose-reduction: after the xor-16/8/4 steps lane L holds
+                // the partial sums of key (L >> 2) & 7; xor-2/1 finish them.
+                {
+                    const bool hi = lane & 16;
+#pragma unroll
+                    for (int i = 0; i < 4 * G; ++i) {
+                        float lo_v = vals[i], hi_v = vals[i + 4 * G];
+                        float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                        vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    }
+                }
+                {
+                    const bool hi = lane & 8;
+#pragma unroll
+                    for (int i = 0; i < 2 * G; ++i) {
+                        float lo_v = vals[i], hi_v = vals[i + 2 * G];
+                        float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                        vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                    }
+                }
+                {
+                    const bool hi = lane & 4;
+#pragma unroll
+                    for (int i = 0; i < G; ++i) {
+                        float lo_v = vals[i], hi_v = vals[i + G];
+                        float send = hi ? lo_v : hi_v, keep = hi ? hi_v : lo_v;
+                        vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                    }
+                }
+                const int my_key = (lane >> 2) & 7;
+                const bool valid = kw0 + my_key < nk;
+                float pr[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float sv = vals[g];
+                    sv += __shfl_xor_sync(0xffffffffu, sv, 2);
+                    sv += __shfl_xor_sync(0xffffffffu, sv, 1);
+                    float mx = valid ? sv : -INFINITY;
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    float mnew = fmaxf(m[g], mx);
+                    float so = exp2f(m[g] - mnew);  // 0 while m is -inf
+                    float pv = valid ? exp2f(sv - mnew) : 0.f;
+                    float ps = pv;
+                    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                    l[g] = l[g] * so + ps;
+                    m[g] = mnew;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) o[g][e] *= so;
+                    pr[g] = pv;
+                }
+                // O += p_i * V_i over the warp's keys.
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float pi[G];
+#pragma unroll
+                    for (int g = 0; g < G; ++g) pi[g] = __shfl_sync(0xffffffffu, pr[g], i * 4);
+                    if (kw0 + i < nk) {
+                        float vf[E];
+                        load_slice<KV, E>(vtile + (kw0 + i) * S::kRowBytes + lane * E * Elem<KV>::bytes, vf);
+#pragma unroll
+                        for (int g = 0; g < G; ++g)
+#pragma unroll
+                            for (int e = 0; e < E; ++e) o[g][e] = fmaf(pi[g], vf[e], o[g][e]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
+            if (gw == 0 && lane == 0) s_consumed[grp] = t + 1;
+        }
     }
 
-    if (bad) {
-        // Drain the copies still in flight (bounded) before the CTA leaves:
-        // for every stage, wait for the last tile that was issued into it.
+    __syncthreads();  // every tile consumed (or abandoned); the ring is free
+    if (s_abort) {
         if (tid == 0) {
-            for (int st = 0; st < NST; ++st) {
-                int last = -1;
-                for (int t = st; t < ntiles; t += NST) last = t;
-                if (last >= 0) mbar_wait(smem_addr(&bars[st]), uint32_t(last / NST) & 1u);
-            }
+            // Drain (bounded) the copies issued for tiles nobody consumed.
+            int done = s_consumed[0] > s_consumed[1] ? s_consumed[0] : s_consumed[1];
+            for (int t = done > 0 ? done - 1 : 0; t < s_issued; ++t)
+                mbar_wait(smem_u32(&full[t % NST]), uint32_t(t / NST) & 1u, &g_fd_error_word);
         }
         __syncthreads();
         return;
     }
 
-    // Merge the four warps' softmax states.
-    if (lane == 0) {
+    // Merge the eight consumer warps' softmax states.
+    if (warp < kCWarps) {
+        if (lane == 0) {
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            mm[warp * G + g] = m[g];
-            ll[warp * G + g] = l[g];
+            for (int g = 0; g < G; ++g) {
+                mm[warp * G + g] = m[g];
+                ll[warp * G + g] = l[g];
+            }
         }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < E; ++e) oo[(warp * G + g) * HD + lane * E + e] = o[g][e];
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int e = 0; e < E; ++e) oo[(warp * G + g) * HD + lane * E + e] = o[g][e];
     __syncthreads();
-    write_result<G, HD>(a, b, hq0, split, mm, ll, oo, tid);
+    write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, tid, kFastThreads);
 }
 
 // Generic kernel (any Hd <= 512, any alignment, q dtype may differ from
@@ -504,11 +481,20 @@ __global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
 }
 
 // Log-sum-exp combine of the splits (FlashDecoding.metal:182-231).
+// One CTA of 256 threads per (b, hq): the split weights exp2(m_s - M) are
+// computed once into shared memory; then 4 thread groups each sum a quarter
+// of the splits for every head dim (several independent loads in flight per
+// thread) and the four partial sums are added in shared memory.
+constexpr int kCombThreads = 256;
+constexpr int kCombPar = 4;
+
 template <class OT>
-__global__ void __launch_bounds__(kThreads) fd_combine_kernel(const float* po, const float* pm, const float* pl,
-                                                              void* out, int64_t Nq, int64_t Hd, int splits) {
-    extern __shared__ float wts[];  // [splits]
-    __shared__ float red[kWarps];
+__global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* po, const float* pm, const float* pl,
+                                                                  void* out, int64_t Nq, int64_t Hd, int splits) {
+    extern __shared__ float sh[];  // wts[splits], part[kCombPar][Hd]
+    float* wts = sh;
+    float* part = sh + ((splits + 3) & ~3);
+    __shared__ float red[kCombThreads / 32];
     __shared__ float s_M, s_L;
     pdl_launch_dependents();
     pdl_wait();
@@ -517,19 +503,19 @@ __global__ void __launch_bounds__(kThreads) fd_combine_kernel(const float* po, c
     const float* m = pm + bh * splits;
     const float* l = pl + bh * splits;
     float mx = -INFINITY;
-    for (int s = tid; s < splits; s += kThreads) mx = fmaxf(mx, m[s]);
+    for (int s = tid; s < splits; s += kCombThreads) mx = fmaxf(mx, m[s]);
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
     if (tid == 0) {
         float v = red[0];
-        for (int w = 1; w < kWarps; ++w) v = fmaxf(v, red[w]);
+        for (int w = 1; w < kCombThreads / 32; ++w) v = fmaxf(v, red[w]);
         s_M = v;
     }
     __syncthreads();
     const float M = s_M;
     float lsum = 0.f;
-    for (int s = tid; s < splits; s += kThreads) {
+    for (int s = tid; s < splits; s += kCombThreads) {
         float f = (M == -INFINITY || m[s] == -INFINITY) ? 0.f : exp2f(m[s] - M);
         wts[s] = f;
         lsum += f * l[s];
@@ -540,16 +526,30 @@ __global__ void __launch_bounds__(kThreads) fd_combine_kernel(const float* po, c
     __syncthreads();
     if (tid == 0) {
         float v = 0.f;
-        for (int w = 0; w < kWarps; ++w) v += red[w];
+        for (int w = 0; w < kCombThreads / 32; ++w) v += red[w];
         s_L = v;
+    }
+    __syncthreads();
+    const float* o = po + bh * splits * Hd;
+    const int per = kCombThreads / kCombPar;  // threads per group
+    const int grp = tid / per, gt = tid % per;
+    for (int64_t d = gt; d < Hd; d += per) {
+        float acc0 = 0.f, acc1 = 0.f;
+        int s = grp;
+        for (; s + kCombPar < splits; s += 2 * kCombPar) {
+            acc0 = fmaf(wts[s], o[int64_t(s) * Hd + d], acc0);
+            acc1 = fmaf(wts[s + kCombPar], o[int64_t(s + kCombPar) * Hd + d], acc1);
+        }
+        if (s < splits) acc0 = fmaf(wts[s], o[int64_t(s) * Hd + d], acc0);
+        part[grp * Hd + d] = acc0 + acc1;
     }
     __syncthreads();
     const float L = s_L;
     const float inv_l = L > 0.f ? 1.0f / L : 0.f;
-    const float* o = po + bh * splits * Hd;
-    for (int64_t d = tid; d < Hd; d += kThreads) {
+    for (int64_t d = tid; d < Hd; d += kCombThreads) {
         float acc = 0.f;
-        for (int s = 0; s < splits; ++s) acc = fmaf(wts[s], o[int64_t(s) * Hd + d], acc);
+#pragma unroll
+        for (int g = 0; g < kCombPar; ++g) acc += part[g * Hd + d];
         Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
     }
 }
@@ -577,7 +577,7 @@ cudaError_t run_fast(const FDArgs& a, dim3 grid, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    return launch_k(kern, grid, dim3(kThreads), smem, s, a);
+    return launch_k(kern, grid, dim3(kFastThreads), smem, s, a);
 }
 
 // Register budget: q and O slices take 2*G*Hd/32 floats per lane; keep
@@ -621,21 +621,36 @@ cudaError_t run_generic_q(const FDArgs& a, dim3 grid, cudaStream_t s) {
 
 }  // namespace
 
+// Split plan. The fast kernel runs one CTA per SM, so the grid should be
+// whole waves of sm_count CTAs: among split counts from the smallest that
+// fills one wave up to four times that, pick the one whose waves x
+// keys-per-split is least (ties: fewer splits, i.e. less combine work).
 FlashDecodePlan flash_decode_plan(const FlashDecode& p, int sm_count) {
     FlashDecodePlan plan{};
     plan.fast = fast_path(p);
     plan.heads_per_cta = plan.fast ? heads_per_cta(p) : 1;
-    int64_t hgroups = (p.Nq / p.Nkv) / plan.heads_per_cta;
-    int64_t base = p.B * p.Nkv * hgroups;
-    int64_t target = int64_t(sm_count) * 2;
+    const int64_t hgroups = (p.Nq / p.Nkv) / plan.heads_per_cta;
+    const int64_t base = p.B * p.Nkv * hgroups;
+    const int64_t wave = plan.fast ? int64_t(sm_count) : int64_t(sm_count) * 4;
     int64_t max_tiles = (p.S + kTileKeys - 1) / kTileKeys;
     if (max_tiles < 1) max_tiles = 1;
-    int64_t splits = (target + base - 1) / base;
-    if (splits < 1) splits = 1;
-    if (splits > max_tiles) splits = max_tiles;
-    if (splits > 1024) splits = 1024;
-    int64_t tiles_per_split = (max_tiles + splits - 1) / splits;
-    plan.chunk = tiles_per_split * kTileKeys;
+    int64_t s_lo = (wave + base - 1) / base;
+    if (s_lo < 1) s_lo = 1;
+    int64_t best_tiles = 0;
+    double best_cost = 1e30;
+    for (int64_t s = 1; s <= s_lo * 4 && s <= max_tiles && s <= 1024; ++s) {
+        int64_t tiles = (max_tiles + s - 1) / s;   // tiles per split
+        int64_t splits = (max_tiles + tiles - 1) / tiles;
+        int64_t ctas = base * splits;
+        int64_t waves = (ctas + wave - 1) / wave;
+        double cost = double(waves) * double(tiles) + 0.02 * double(splits);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best_tiles = tiles;
+        }
+    }
+    if (best_tiles == 0) best_tiles = max_tiles;
+    plan.chunk = best_tiles * kTileKeys;
     plan.splits = int((p.S + plan.chunk - 1) / plan.chunk);
     if (plan.splits < 1) plan.splits = 1;
     plan.scratch_o = size_t(p.B * p.Nq) * plan.splits * p.Hd * 4;
@@ -646,36 +661,39 @@ FlashDecodePlan flash_decode_plan(const FlashDecode& p, int sm_count) {
 cudaError_t flash_decode(const FlashDecode& p, const FlashDecodePlan& plan, float* po, float* pm, float* pl,
                          cudaStream_t s) {
     FDArgs a{p, plan.splits, plan.chunk, plan.heads_per_cta, int((p.Nq / p.Nkv) / plan.heads_per_cta), po, pm, pl};
-    cudaError_t err;
     if (plan.fast) {
         dim3 grid(unsigned(plan.splits), unsigned(p.Nkv * a.hgroups), unsigned(p.B));
         switch (p.kv_dtype) {
-        case PC_BF16: err = run_fast_hd<TBF16>(a, grid, s); break;
-        case PC_F16: err = run_fast_hd<TF16>(a, grid, s); break;
-        case PC_F32: err = run_fast_hd<TF32>(a, grid, s); break;
-        default: return cudaErrorInvalidValue;
-        }
-    } else {
-        dim3 grid(unsigned(plan.splits), unsigned(p.Nq), unsigned(p.B));
-        switch (p.q_dtype) {
-        case PC_F32: err = run_generic_q<TF32>(a, grid, s); break;
-        case PC_F16: err = run_generic_q<TF16>(a, grid, s); break;
-        case PC_BF16: err = run_generic_q<TBF16>(a, grid, s); break;
+        case PC_BF16: return run_fast_hd<TBF16>(a, grid, s);
+        case PC_F16: return run_fast_hd<TF16>(a, grid, s);
+        case PC_F32: return run_fast_hd<TF32>(a, grid, s);
         default: return cudaErrorInvalidValue;
         }
     }
-    return err;
+    dim3 grid(unsigned(plan.splits), unsigned(p.Nq), unsigned(p.B));
+    switch (p.q_dtype) {
+    case PC_F32: return run_generic_q<TF32>(a, grid, s);
+    case PC_F16: return run_generic_q<TF16>(a, grid, s);
+    case PC_BF16: return run_generic_q<TBF16>(a, grid, s);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& plan, const float* po, const float* pm,
                                  const float* pl, cudaStream_t s) {
     if (plan.splits <= 1) return cudaSuccess;
     dim3 grid(unsigned(p.Nq), unsigned(p.B));
-    size_t smem = size_t(plan.splits) * 4;
+    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(kCombPar) * p.Hd) * 4;
     switch (p.out_dtype) {
-    case PC_F32: return launch_k(fd_combine_kernel<TF32>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
-    case PC_F16: return launch_k(fd_combine_kernel<TF16>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
-    case PC_BF16: return launch_k(fd_combine_kernel<TBF16>, grid, dim3(kThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd, plan.splits);
+    case PC_F32:
+        return launch_k(fd_combine_kernel<TF32>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
+                        plan.splits);
+    case PC_F16:
+        return launch_k(fd_combine_kernel<TF16>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
+                        plan.splits);
+    case PC_BF16:
+        return launch_k(fd_combine_kernel<TBF16>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
+                        plan.splits);
     }
     return cudaErrorInvalidValue;
 }
@@ -702,6 +720,8 @@ RegisterFunctions reg_fd({
 });
 }  // namespace
 
+uint32_t read_and_clear_gemv_errors();
+
 }  // namespace launch
 }  // namespace popcorn
 
@@ -713,7 +733,7 @@ extern "C" int pc_device_error_check(int device, uint32_t* flags) {
         return PC_ERR_GPU_DEVICE_REMOVED;
     }
     cudaDeviceSynchronize();
-    *flags = popcorn::launch::read_and_clear_fd_errors();
+    *flags = popcorn::launch::read_and_clear_fd_errors() | popcorn::launch::read_and_clear_gemv_errors();
     cudaSetDevice(prev);
     return PC_OK;
 }

@@ -9,21 +9,26 @@
 // stored in the activation dtype).
 //
 // B200 design. The op is HBM-bound: every weight byte is read once, 2 bytes
-// per 2 FLOPs. Each warp owns ROWS rows; each lane streams 16-byte chunks of
-// its rows with ld.global.nc.L1::no_allocate (no L1 pollution), several
-// chunks per row in flight, double-buffered in registers so the next batch
-// is in flight while the current one is reduced. The activation row is
-// converted to fp32 once per CTA into shared memory, split into two float4
-// planes (elements 0-3 / 4-7 of every chunk) so a warp's x reads are
-// conflict-free. The first weight batch is issued before griddepcontrol.wait,
-// so under programmatic dependent launch the weight stream starts while the
-// previous kernel is still draining.
+// per 2 FLOPs. One persistent CTA per SM: a producer warp streams 8-row x
+// kc-column weight tiles HBM -> shared memory with 1-D bulk copies
+// (cp.async.bulk, no multicast) into a 2-8 stage mbarrier ring of up to
+// ~190 KB, starting before griddepcontrol.wait (weights never depend on the
+// previous kernel, so under programmatic dependent launch the stream starts
+// while that kernel drains). Eight consumer warps own one weight row each
+// per stage; the activation row is converted to fp32 once per CTA into
+// shared memory, split into two float4 planes (elements 0-3 / 4-7 of every
+// 16-byte chunk) so a warp's x reads are conflict-free. Rows whose length
+// is not a multiple of 16 bytes use a plain one-warp-per-row kernel.
+#include "async.cuh"
 #include "common.cuh"
 #include "dtype.cuh"
 #include "launch.hpp"
 #include "popcorn.hpp"
 
 namespace popcorn {
+
+__device__ unsigned int g_gemv_error_word;
+
 namespace launch {
 
 namespace {
@@ -72,140 +77,193 @@ __device__ __forceinline__ void gemv_store(const Gemv& p, int64_t n, float a, fl
     }
 }
 
-// Vectorised kernel: K % VEC == 0, W rows 16-byte aligned, K*4 bytes of x
-// fit in shared memory.
-template <class XT, class WT, class OT, int ROWS, int U, bool NORM, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_vec_kernel(const Gemv p) {
+// Bulk-copy kernel: K % VEC == 0 and 16-byte aligned weight rows.
+//
+// One CTA per SM (persistent): warp 8 is the producer, warps 0-7 consume.
+// A tile is 8 outputs; a stage holds their 8 weight rows (16 when gated:
+// the 8 W_gate rows, then the 8 W_up rows) over kc columns, one bulk copy
+// per row segment. The producer fills the ring before the CTA waits for
+// its predecessor (griddepcontrol.wait): weights never depend on it. Each
+// consumer warp owns one output (its gate and up rows when gated), lanes
+// stride 16-byte chunks (conflict-free shared loads), and the k-chunks of a
+// row accumulate in registers until the warp reduction and the epilogue.
+struct GemvPlan {
+    int kc;           // columns per stage (multiple of 8)
+    int nkc;          // stages per tile
+    int ntiles;       // tiles of 8 outputs
+    int stages;       // ring depth
+    int stage_bytes;  // 8 * R rows * kc * elem
+};
+
+constexpr int kConsumers = 8;
+constexpr int kTmaThreads = (kConsumers + 1) * 32;
+
+template <class XT, class WT, class OT, bool NORM, int EPI>
+__global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, const GemvPlan g) {
     constexpr int VEC = WVec<WT>::n;
-    constexpr int NR = (EPI == int(Epilogue::kGated) ? 2 : 1) * ROWS;
-    extern __shared__ float4 xs[];  // [nchunks] lo plane, then [nchunks] hi plane (VEC == 8)
-    __shared__ float red[kWarps];
+    constexpr int es = Elem<WT>::bytes;
+    constexpr bool GATED = EPI == int(Epilogue::kGated);
+    constexpr int R = GATED ? 2 : 1;  // weight rows per output
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t full[8], empty[8];
+    __shared__ float red[kConsumers];
     __shared__ float s_scale;
+    __shared__ volatile int s_abort;
+    __shared__ volatile int s_issued;
+    __shared__ volatile int s_consumed;
 
     pdl_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t K = p.K;
-    const int nchunks = int(K / VEC);
-    const int64_t n0 = (int64_t(blockIdx.x) * kWarps + warp) * ROWS;
-    constexpr int es = Elem<WT>::bytes;
+    const int nx = int(K / VEC);  // 16-byte chunks of a full row
+    unsigned char* ring = smem;
+    float4* xs = reinterpret_cast<float4*>(smem + size_t(g.stages) * g.stage_bytes);
 
-    const char* wp[NR];
-    bool valid[NR];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        int64_t n = n0 + r;
-        bool v = n < p.N;
-        int64_t nn = v ? n : 0;
-        if constexpr (EPI == int(Epilogue::kGated)) {
-            wp[2 * r] = static_cast<const char*>(p.w) + nn * K * es;
-            wp[2 * r + 1] = static_cast<const char*>(p.w2) + nn * K * es;
-            valid[2 * r] = valid[2 * r + 1] = v;
-        } else {
-            wp[r] = static_cast<const char*>(p.w) + nn * K * es;
-            valid[r] = v;
+    if (tid == 0) {
+        for (int s = 0; s < g.stages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kConsumers);
         }
-    }
-
-    uint4 cur[NR][U];
-    auto load_batch = [&](uint4 (&dst)[NR][U], int c0) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            int c = c0 + 32 * u;
-#pragma unroll
-            for (int r = 0; r < NR; ++r)
-                if (valid[r] && c < nchunks) dst[r][u] = ldg_stream(wp[r] + int64_t(c) * 16);
-        }
-    };
-    // Weights do not depend on the previous kernel: start streaming them now.
-    load_batch(cur, lane);
-
-    pdl_wait();
-
-    // Activation row -> fp32 shared memory (optionally RMS-normalised and
-    // rounded to the activation dtype, as RMSNorm would have stored it).
-    float ss = 0.f;
-    for (int64_t i = tid; i < K; i += kThreads) {
-        float v = Elem<XT>::load(p.x, i);
-        if constexpr (NORM) ss += v * v;
-        int c = int(i / VEC), e = int(i % VEC);
-        float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nchunks) + c);
-        plane[e & 3] = v;
-    }
-    if constexpr (NORM) {
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        if (warp == 0) {
-            float v = lane < kWarps ? red[lane] : 0.f;
-            v = warp_sum(v);
-            if (lane == 0) s_scale = rsqrtf(v / float(K) + p.eps);
-        }
-        __syncthreads();
-        float scale = s_scale;
-        for (int64_t i = tid; i < K; i += kThreads) {
-            int c = int(i / VEC), e = int(i % VEC);
-            float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nchunks) + c);
-            float v = plane[e & 3] * scale;
-            if (p.norm_weight) {
-                float w = p.norm_weight[i];
-                if (p.add_one) w = 1.0f + w;
-                v *= w;
-            }
-            plane[e & 3] = Elem<XT>::round(v);
-        }
+        s_abort = 0;
+        s_issued = 0;
+        s_consumed = 0;
+        mbar_fence_init();
     }
     __syncthreads();
 
-    float acc[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) acc[r] = 0.f;
-
-    for (int c0 = lane; c0 < nchunks; c0 += 32 * U) {
-        uint4 nxt[NR][U];
-        if (c0 + 32 * U < nchunks) load_batch(nxt, c0 + 32 * U);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            int c = c0 + 32 * u;
-            if (c < nchunks) {
-                float xf[8];
-                float4 lo = xs[c];
-                xf[0] = lo.x; xf[1] = lo.y; xf[2] = lo.z; xf[3] = lo.w;
-                if constexpr (VEC == 8) {
-                    float4 hi = xs[nchunks + c];
-                    xf[4] = hi.x; xf[5] = hi.y; xf[6] = hi.z; xf[7] = hi.w;
+    if (warp == kConsumers) {
+        // ---- producer ----
+        if (lane == 0) {
+            int it = 0;
+            for (int tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
+                for (int kci = 0; kci < g.nkc; ++kci, ++it) {
+                    const int s = it % g.stages;
+                    const uint32_t ph = uint32_t(it / g.stages) & 1u;
+                    if (s_abort || !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, &g_gemv_error_word)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    const int64_t k0 = int64_t(kci) * g.kc;
+                    const int kcols = int(K - k0 < g.kc ? K - k0 : g.kc);
+                    const uint32_t row_bytes = uint32_t(kcols) * es;
+                    const int64_t n0 = int64_t(tile) * 8;
+                    const int nvalid = int(p.N - n0 < 8 ? p.N - n0 : 8);
+                    const uint32_t bar = smem_u32(&full[s]);
+                    mbar_expect_tx(bar, row_bytes * nvalid * R);
+                    unsigned char* st = ring + size_t(s) * g.stage_bytes;
+                    for (int m = 0; m < R; ++m) {
+                        const char* base = static_cast<const char*>(m == 0 ? p.w : p.w2);
+                        for (int r = 0; r < nvalid; ++r)
+                            bulk_g2s(smem_u32(st + size_t(m * 8 + r) * g.kc * es), base + ((n0 + r) * K + k0) * es,
+                                     row_bytes, bar);
+                    }
+                    s_issued = it + 1;
                 }
-#pragma unroll
-                for (int r = 0; r < NR; ++r) {
-                    float wf[8];
-                    widen<WT>(cur[r][u], wf);
-                    float a = acc[r];
-#pragma unroll
-                    for (int e = 0; e < VEC; ++e) a = fmaf(xf[e], wf[e], a);
-                    acc[r] = a;
-                }
+                if (s_abort) break;
             }
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-            for (int r = 0; r < NR; ++r) cur[r][u] = nxt[r][u];
-    }
-
-#pragma unroll
-    for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
-
-    int64_t pos = -1;
-    if constexpr (EPI == int(Epilogue::kQKV)) pos = p.pos_dev ? int64_t(*p.pos_dev) : p.offset;
-    if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-            int64_t n = n0 + r;
-            if (n >= p.N) break;
-            if constexpr (EPI == int(Epilogue::kGated))
-                gemv_store<OT, EPI>(p, n, acc[2 * r], acc[2 * r + 1], pos);
-            else
-                gemv_store<OT, EPI>(p, n, acc[r], 0.f, pos);
+    } else {
+        // ---- consumers ----
+        pdl_wait();
+        float ss = 0.f;
+        for (int64_t i = tid; i < K; i += kConsumers * 32) {
+            float v = Elem<XT>::load(p.x, i);
+            if constexpr (NORM) ss += v * v;
+            int c = int(i / VEC), e = int(i % VEC);
+            float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
+            plane[e & 3] = v;
         }
+        if constexpr (NORM) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            named_sync(1, kConsumers * 32);
+            if (warp == 0) {
+                float v = lane < kConsumers ? red[lane] : 0.f;
+                v = warp_sum(v);
+                if (lane == 0) s_scale = rsqrtf(v / float(K) + p.eps);
+            }
+            named_sync(1, kConsumers * 32);
+            const float scale = s_scale;
+            for (int64_t i = tid; i < K; i += kConsumers * 32) {
+                int c = int(i / VEC), e = int(i % VEC);
+                float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
+                float v = plane[e & 3] * scale;
+                if (p.norm_weight) {
+                    float w = p.norm_weight[i];
+                    if (p.add_one) w = 1.0f + w;
+                    v *= w;
+                }
+                plane[e & 3] = Elem<XT>::round(v);
+            }
+        }
+        named_sync(1, kConsumers * 32);
+
+        int64_t pos = -1;
+        if constexpr (EPI == int(Epilogue::kQKV)) pos = p.pos_dev ? int64_t(*p.pos_dev) : p.offset;
+
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < g.ntiles && ok; tile += gridDim.x) {
+            const int64_t n = int64_t(tile) * 8 + warp;
+            const bool valid = n < p.N;
+            float acc[R];
+#pragma unroll
+            for (int m = 0; m < R; ++m) acc[m] = 0.f;
+            for (int kci = 0; kci < g.nkc; ++kci, ++it) {
+                const int s = it % g.stages;
+                const uint32_t ph = uint32_t(it / g.stages) & 1u;
+                if (s_abort || !mbar_wait(smem_u32(&full[s]), ph, &g_gemv_error_word)) {
+                    s_abort = 1;
+                    ok = false;
+                    break;
+                }
+                const int64_t k0 = int64_t(kci) * g.kc;
+                const int kcols = int(K - k0 < g.kc ? K - k0 : g.kc);
+                if (valid) {
+                    const int c0 = int(k0 / VEC);
+                    const int nc = kcols / VEC;
+#pragma unroll
+                    for (int m = 0; m < R; ++m) {
+                        const unsigned char* row =
+                            ring + size_t(s) * g.stage_bytes + size_t(m * 8 + warp) * g.kc * es;
+                        float a = acc[m];
+#pragma unroll 4
+                        for (int c = lane; c < nc; c += 32) {
+                            uint4 wv = *reinterpret_cast<const uint4*>(row + size_t(c) * 16);
+                            float wf[8];
+                            widen<WT>(wv, wf);
+                            float4 lo = xs[c0 + c];
+                            a = fmaf(lo.x, wf[0], a);
+                            a = fmaf(lo.y, wf[1], a);
+                            a = fmaf(lo.z, wf[2], a);
+                            a = fmaf(lo.w, wf[3], a);
+                            if constexpr (VEC == 8) {
+                                float4 hi = xs[nx + c0 + c];
+                                a = fmaf(hi.x, wf[4], a);
+                                a = fmaf(hi.y, wf[5], a);
+                                a = fmaf(hi.z, wf[6], a);
+                                a = fmaf(hi.w, wf[7], a);
+                            }
+                        }
+                        acc[m] = a;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
+                if (warp == 0 && lane == 0) s_consumed = it + 1;
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int m = 0; m < R; ++m) acc[m] = warp_sum(acc[m]);
+            if (lane == 0 && valid) gemv_store<OT, EPI>(p, n, acc[0], R > 1 ? acc[R - 1] : 0.f, pos);
+        }
+    }
+    __syncthreads();
+    if (s_abort && tid == 0) {
+        // A wait gave up: drain (bounded) the copies that were issued but not
+        // consumed, so none lands after the CTA has left.
+        for (int j = s_consumed; j < s_issued; ++j)
+            mbar_wait(smem_u32(&full[j % g.stages]), uint32_t(j / g.stages) & 1u, &g_gemv_error_word);
     }
 }
 
@@ -264,21 +322,6 @@ __global__ void __launch_bounds__(kThreads) gemv_scalar_kernel(const Gemv p) {
 
 constexpr size_t kMaxSmem = 200 * 1024;
 
-template <class XT, class WT, class OT, int ROWS, int U, bool NORM, int EPI>
-cudaError_t run_vec(const Gemv& p, cudaStream_t s) {
-    auto kern = gemv_vec_kernel<XT, WT, OT, ROWS, U, NORM, EPI>;
-    size_t smem = size_t(p.K) * 4;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = allow_smem(kern, kMaxSmem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
-    int64_t rows_per_cta = int64_t(kWarps) * ROWS;
-    int64_t grid = (p.N + rows_per_cta - 1) / rows_per_cta;
-    return launch_k(kern, dim3(unsigned(grid)), dim3(kThreads), smem, s, p);
-}
-
 template <class XT, class WT, class OT, bool NORM, int EPI>
 cudaError_t run_scalar(const Gemv& p, cudaStream_t s) {
     auto kern = gemv_scalar_kernel<XT, WT, OT, NORM, EPI>;
@@ -293,17 +336,51 @@ cudaError_t run_scalar(const Gemv& p, cudaStream_t s) {
     return launch_k(kern, dim3(unsigned(grid)), dim3(kThreads), smem, s, p);
 }
 
-// Rows per warp: enough CTAs to cover every SM at least ~3 times over.
+constexpr size_t kTmaSmemBudget = 200 * 1024;
+
+bool make_plan(const Gemv& p, GemvPlan& g) {
+    const int es = dtype_stride(p.w_dtype);
+    const int R = p.epilogue == Epilogue::kGated ? 2 : 1;
+    const int64_t K = p.K;
+    const int64_t max_stage = 40 * 1024;
+    int nkc = int((K * es * 8 * R + max_stage - 1) / max_stage);
+    if (nkc < 1) nkc = 1;
+    int64_t kc = (K + nkc - 1) / nkc;
+    kc = (kc + 7) / 8 * 8;
+    nkc = int((K + kc - 1) / kc);
+    g.kc = int(kc);
+    g.nkc = nkc;
+    g.ntiles = int((p.N + 7) / 8);
+    g.stage_bytes = int(8 * R * kc * es);
+    size_t xbytes = size_t(K) * 4;
+    if (xbytes + 2 * size_t(g.stage_bytes) > kTmaSmemBudget) return false;
+    g.stages = int((kTmaSmemBudget - xbytes) / g.stage_bytes);
+    if (g.stages > 8) g.stages = 8;
+    return g.stages >= 2;
+}
+
+template <class XT, class WT, class OT, bool NORM, int EPI>
+cudaError_t run_tma(const Gemv& p, const GemvPlan& g, cudaStream_t s) {
+    auto kern = gemv_tma_kernel<XT, WT, OT, NORM, EPI>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = allow_smem(kern, kTmaSmemBudget + 1024);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    size_t smem = size_t(g.stages) * g.stage_bytes + size_t(p.K) * 4;
+    int grid = g.ntiles < current_sm_count() ? g.ntiles : current_sm_count();
+    return launch_k(kern, dim3(unsigned(grid)), dim3(kTmaThreads), smem, s, p, g);
+}
+
 template <class XT, class WT, class OT, bool NORM, int EPI>
 cudaError_t dispatch_rows(const Gemv& p, cudaStream_t s) {
     constexpr int VEC = WVec<WT>::n;
-    bool vec_ok = (p.K % VEC == 0) && aligned16(p.w) && (EPI != int(Epilogue::kGated) || aligned16(p.w2));
-    if (!vec_ok) return run_scalar<XT, WT, OT, NORM, EPI>(p, s);
-    int sms = current_sm_count();
-    int64_t ctas_rows2 = (p.N + 2 * kWarps - 1) / (2 * kWarps);
-    if (EPI != int(Epilogue::kGated) && ctas_rows2 >= int64_t(sms) * 4)
-        return run_vec<XT, WT, OT, 2, 4, NORM, EPI>(p, s);
-    return run_vec<XT, WT, OT, 1, 4, NORM, EPI>(p, s);
+    bool vec_ok = (p.K % VEC == 0) && (p.K * Elem<WT>::bytes) % 16 == 0 && aligned16(p.w) &&
+                  (EPI != int(Epilogue::kGated) || aligned16(p.w2));
+    GemvPlan g{};
+    if (vec_ok && make_plan(p, g)) return run_tma<XT, WT, OT, NORM, EPI>(p, g, s);
+    return run_scalar<XT, WT, OT, NORM, EPI>(p, s);
 }
 
 template <class XT, class WT, class OT>
@@ -359,27 +436,37 @@ cudaError_t gemv(const Gemv& p, cudaStream_t s) {
     return cudaErrorInvalidValue;
 }
 
+uint32_t read_and_clear_gemv_errors() {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_error_word, sizeof(v)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) cudaMemcpyToSymbol(g_gemv_error_word, &zero, sizeof(zero));
+    return v;
+}
+
 namespace {
 RegisterFunctions reg_gemv({
-    {"matvec_nk_f32_f32_f32", reinterpret_cast<const void*>(gemv_vec_kernel<TF32, TF32, TF32, 1, 4, false, 0>)},
-    {"matvec_nk_f32_bf16_f32", reinterpret_cast<const void*>(gemv_vec_kernel<TF32, TBF16, TF32, 1, 4, false, 0>)},
-    {"matvec_nk_bf16_bf16_f32", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TF32, 1, 4, false, 0>)},
-    {"matvec_nk_bf16_bf16_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, false, 0>)},
-    {"matvec_nk_f32_bf16_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TF32, TBF16, TBF16, 1, 4, false, 0>)},
-    {"matvec_nk_f32_f16_f32", reinterpret_cast<const void*>(gemv_vec_kernel<TF32, TF16, TF32, 1, 4, false, 0>)},
-    {"matvec_nk_f16_f16_f32", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF32, 1, 4, false, 0>)},
-    {"matvec_nk_f16_f16_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, false, 0>)},
-    {"matvec_nk_f32_f16_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF32, TF16, TF16, 1, 4, false, 0>)},
-    {"rmsnorm_matvec_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, true, 0>)},
-    {"rmsnorm_matvec_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, true, 0>)},
-    {"matvec_residual_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, false, 1>)},
-    {"matvec_residual_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, false, 1>)},
-    {"geglu_matvec_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, true, 2>)},
-    {"geglu_matvec_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, true, 2>)},
-    {"swiglu_matvec_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, false, 2>)},
-    {"swiglu_matvec_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, false, 2>)},
-    {"qkv_matvec_bf16", reinterpret_cast<const void*>(gemv_vec_kernel<TBF16, TBF16, TBF16, 1, 4, true, 3>)},
-    {"qkv_matvec_f16", reinterpret_cast<const void*>(gemv_vec_kernel<TF16, TF16, TF16, 1, 4, true, 3>)},
+    {"matvec_nk_f32_f32_f32", reinterpret_cast<const void*>(gemv_tma_kernel<TF32, TF32, TF32, false, 0>)},
+    {"matvec_nk_f32_bf16_f32", reinterpret_cast<const void*>(gemv_tma_kernel<TF32, TBF16, TF32, false, 0>)},
+    {"matvec_nk_bf16_bf16_f32", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TF32, false, 0>)},
+    {"matvec_nk_bf16_bf16_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, false, 0>)},
+    {"matvec_nk_f32_bf16_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TF32, TBF16, TBF16, false, 0>)},
+    {"matvec_nk_f32_f16_f32", reinterpret_cast<const void*>(gemv_tma_kernel<TF32, TF16, TF32, false, 0>)},
+    {"matvec_nk_f16_f16_f32", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF32, false, 0>)},
+    {"matvec_nk_f16_f16_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, false, 0>)},
+    {"matvec_nk_f32_f16_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF32, TF16, TF16, false, 0>)},
+    {"rmsnorm_matvec_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, true, 0>)},
+    {"rmsnorm_matvec_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, true, 0>)},
+    {"matvec_residual_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, false, 1>)},
+    {"matvec_residual_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, false, 1>)},
+    {"geglu_matvec_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, true, 2>)},
+    {"geglu_matvec_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, true, 2>)},
+    {"swiglu_matvec_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, false, 2>)},
+    {"swiglu_matvec_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, false, 2>)},
+    {"qkv_matvec_bf16", reinterpret_cast<const void*>(gemv_tma_kernel<TBF16, TBF16, TBF16, true, 3>)},
+    {"qkv_matvec_f16", reinterpret_cast<const void*>(gemv_tma_kernel<TF16, TF16, TF16, true, 3>)},
 });
 }  // namespace
 

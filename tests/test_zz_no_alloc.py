@@ -67,10 +67,10 @@ def test_noalloc_rejects_oversized_problem():
     from popcorn_b200 import _native as N
     cap = N.lib().pc_flash_decoding_noalloc_capacity()
     assert cap == 1 << 20
-    # head_dim 512, 16 query heads sharing 8 KV heads, 4096 keys: the split
-    # plan (32 splits) needs 16 x 32 x 512 x 4 B of partial O plus m and l,
-    # just over 1 MiB.
-    B, Nq, Nkv, S, Hd = 1, 16, 8, 4096, 512
+    # head_dim 512, 16 query heads on 2 KV heads, 32768 keys: the split plan
+    # (37 splits on a 148-SM B200) needs 16 x 37 x 512 x 4 B of partial O
+    # plus m and l, about 1.2 MB.
+    B, Nq, Nkv, S, Hd = 1, 16, 2, 32768, 512
     q = torch.zeros(B, Nq, 1, Hd, dtype=torch.bfloat16, device="cuda")
     k = torch.zeros(B, Nkv, S, Hd, dtype=torch.bfloat16, device="cuda")
     out = torch.full_like(q, 7.0)
