@@ -176,6 +176,16 @@ PC_API int pc_kernel_binding(const pc_kernel* kernel, int index, pc_tensor* tens
 /* Function names this kernel will launch, ';'-separated (route visible). */
 PC_API const char* pc_kernel_function_names(const pc_kernel* kernel);
 
+/* Extension (no reference counterpart): an L2 prefetch hint for the kernels
+ * that stream their operands from HBM (decode FlashAttention, the m == 1
+ * Matmul and the fused decode ops). Once the kernel has issued its own
+ * loads, its CTAs pull [ptr, ptr + bytes) into L2 — typically the next
+ * kernel's weights or KV cache — so that a chain of dependent kernels keeps
+ * HBM busy across kernel boundaries. Two slots (0, 1); bytes 0 clears a
+ * slot. Results never change. Other kernels return
+ * PC_ERR_KERNEL_FUNCTION_NOT_FOUND. */
+PC_API int pc_kernel_set_l2_prefetch(pc_kernel* kernel, int32_t slot, const void* ptr, uint64_t bytes);
+
 /* FlashAttention.Path, FlashAttention.swift:94-98 + route(sq:hd:supportsMPP:)
  * :109-113. On B200 the tensor-core prefill kernel plays the MPP role. */
 typedef enum pc_attention_path { PC_PATH_PLAIN = 0, PC_PATH_TENSOR = 1, PC_PATH_DECODING = 2 } pc_attention_path;

@@ -378,6 +378,20 @@ class Kernel:
             out.append((t.data or 0, tuple(t.shape[:t.rank]), DataType(t.dtype), Access(acc.value)))
         return out
 
+    def set_l2_prefetch(self, slot, region, nbytes=None):
+        """L2 prefetch hint: after issuing its own loads the kernel pulls
+        `region` (a torch tensor or a device address, `nbytes` long) into L2."""
+        if region is None:
+            ptr, n = None, 0
+        elif isinstance(region, int):
+            ptr, n = region, int(nbytes)
+        else:
+            ptr = region.data_ptr()
+            n = region.numel() * region.element_size() if nbytes is None else int(nbytes)
+            self._keep = self._keep + (region,)
+        _check(N.lib().pc_kernel_set_l2_prefetch(self._h, int(slot), ptr, n))
+        return self
+
     def encode(self, encoder):
         encoder.encode(self)
 

@@ -64,6 +64,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     return false;
 }
 
+// Pulls this CTA's share (part `part` of `nparts`) of [ptr, ptr+bytes) into
+// L2, in pieces of at most 64 KB. Ranges are trimmed to 16-byte boundaries.
+__device__ __forceinline__ void prefetch_share_l2(const void* ptr, uint64_t bytes, int part, int nparts) {
+    if (!ptr || bytes < 16) return;
+    uint64_t base = (reinterpret_cast<uint64_t>(ptr) + 15) & ~uint64_t(15);
+    uint64_t end = (reinterpret_cast<uint64_t>(ptr) + bytes) & ~uint64_t(15);
+    if (end <= base) return;
+    uint64_t total = end - base;
+    uint64_t share = ((total / uint64_t(nparts)) + 15) & ~uint64_t(15);
+    uint64_t lo = base + share * uint64_t(part);
+    uint64_t hi = lo + share < end ? lo + share : end;
+    for (uint64_t a = lo; a < hi; a += 65536) {
+        uint64_t n = hi - a < 65536 ? hi - a : 65536;
+        bulk_prefetch_l2(reinterpret_cast<const void*>(a), uint32_t(n));
+    }
+}
+
 // Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

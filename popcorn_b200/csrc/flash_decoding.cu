@@ -23,6 +23,9 @@
 //    merge at the end.
 //  * The split count is chosen for whole waves over the SMs; a small
 //    parallel kernel merges the splits (skipped with one split).
+//  * Before griddepcontrol.wait the producer warms L2 with the split's K/V
+//    rows (cp.async.bulk.prefetch.L2), overlapping the read with the
+//    previous kernel's tail.
 //  * Every mbarrier wait is bounded; a wait that gives up sets a device
 //    error word (pc_device_error_check) and the CTA drains its copies and
 //    leaves.
@@ -85,7 +88,10 @@ struct FDShape {
     static constexpr int kRowBytes = HD * Elem<KV>::bytes;
     static constexpr int kTileBytes = kTileKeys * kRowBytes;  // one of K or V
     static constexpr int kStageBytes = 2 * kTileBytes;
-    static constexpr int kStages = std::max(1, std::min(8, 196608 / kStageBytes));
+    // An even ring depth: tiles t and t + kStages then belong to the same
+    // consumer group, so a group never waits on a stage's phase two steps
+    // ahead of the one in flight (the parity would alias).
+    static constexpr int kStages = std::max(2, std::min(8, 196608 / kStageBytes) & ~1);
 };
 
 template <class KV, int HD, int G>
@@ -191,6 +197,25 @@ __global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArg
     }
     __syncthreads();
 
+    const int64_t head_off = (b * p.Nkv + hkv) * p.S * HD;  // elements
+    const char* kbase = static_cast<const char*>(p.k) + head_off * Elem<KV>::bytes;
+    const char* vbase = static_cast<const char*>(p.v) + head_off * Elem<KV>::bytes;
+    if (warp == kCWarps && lane == 0) {
+        // Before waiting for the previous kernel: warm L2 with this split's
+        // keys. A prefetch only fills L2 (which always holds the latest data),
+        // so rows the previous kernel is still writing are read correctly
+        // after the wait; seq_lens read here only bounds the hint.
+        int64_t hint_len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
+        if (hint_len < 0 || hint_len > p.S) hint_len = p.S;
+        int64_t pb, pe;
+        split_range(a, hint_len, split, pb, pe);
+        for (int64_t j0 = pb; j0 < pe; j0 += kTileKeys) {
+            const uint32_t bytes = uint32_t((pe - j0 < kTileKeys ? pe - j0 : kTileKeys) * S::kRowBytes);
+            bulk_prefetch_l2(kbase + j0 * S::kRowBytes, bytes);
+            bulk_prefetch_l2(vbase + j0 * S::kRowBytes, bytes);
+        }
+    }
+
     pdl_wait();  // q, the cache and seq_lens may come from the previous kernel
 
     const int64_t len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
@@ -212,9 +237,6 @@ __global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArg
         return;
     }
 
-    const int64_t head_off = (b * p.Nkv + hkv) * p.S * HD;  // elements
-    const char* kbase = static_cast<const char*>(p.k) + head_off * Elem<KV>::bytes;
-    const char* vbase = static_cast<const char*>(p.v) + head_off * Elem<KV>::bytes;
     const int ntiles = int((je - jb + kTileKeys - 1) / kTileKeys);
 
     float m[G], l[G], o[G][E];
@@ -246,6 +268,10 @@ __global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArg
                 bulk_g2s(smem_u32(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
                 s_issued = t + 1;
             }
+            // Own loads issued: warm L2 for the next kernel of the chain.
+            const int part = int(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+            const int nparts = int(gridDim.x * gridDim.y * gridDim.z);
+            for (int r = 0; r < 2; ++r) prefetch_share_l2(p.pf.ptr[r], p.pf.bytes[r], part, nparts);
         }
     } else {
         // ---- consumers: group `grp` takes tiles grp, grp + 2, ... ----
@@ -481,17 +507,17 @@ __global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
 }
 
 // Log-sum-exp combine of the splits (FlashDecoding.metal:182-231).
-// One CTA of 256 threads per (b, hq): the split weights exp2(m_s - M) are
-// computed once into shared memory; then 4 thread groups each sum a quarter
-// of the splits for every head dim (several independent loads in flight per
-// thread) and the four partial sums are added in shared memory.
+// One CTA of 256 threads per (b, hq). The split weights exp2(m_s - M) go to
+// shared memory once; then the threads form groups x columns (a column is 4
+// head dims, loaded as float4): each thread sums its column over every
+// groups-th split with several independent loads in flight, and the group
+// partial sums are added in shared memory.
 constexpr int kCombThreads = 256;
-constexpr int kCombPar = 4;
 
 template <class OT>
 __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* po, const float* pm, const float* pl,
                                                                   void* out, int64_t Nq, int64_t Hd, int splits) {
-    extern __shared__ float sh[];  // wts[splits], part[kCombPar][Hd]
+    extern __shared__ float sh[];  // wts[splits (padded to 4)], part[groups][Hd]
     float* wts = sh;
     float* part = sh + ((splits + 3) & ~3);
     __shared__ float red[kCombThreads / 32];
@@ -531,32 +557,52 @@ __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* p
     }
     __syncthreads();
     const float* o = po + bh * splits * Hd;
-    const int per = kCombThreads / kCombPar;  // threads per group
-    const int grp = tid / per, gt = tid % per;
-    for (int64_t d = gt; d < Hd; d += per) {
-        float acc0 = 0.f, acc1 = 0.f;
-        int s = grp;
-        for (; s + kCombPar < splits; s += 2 * kCombPar) {
-            acc0 = fmaf(wts[s], o[int64_t(s) * Hd + d], acc0);
-            acc1 = fmaf(wts[s + kCombPar], o[int64_t(s + kCombPar) * Hd + d], acc1);
-        }
-        if (s < splits) acc0 = fmaf(wts[s], o[int64_t(s) * Hd + d], acc0);
-        part[grp * Hd + d] = acc0 + acc1;
-    }
-    __syncthreads();
     const float L = s_L;
     const float inv_l = L > 0.f ? 1.0f / L : 0.f;
-    for (int64_t d = tid; d < Hd; d += kCombThreads) {
-        float acc = 0.f;
-#pragma unroll
-        for (int g = 0; g < kCombPar; ++g) acc += part[g * Hd + d];
-        Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+    if ((Hd & 3) == 0 && Hd / 4 <= kCombThreads) {
+        const int cols = int(Hd / 4);
+        const int groups = kCombThreads / cols;
+        const int col = tid % cols, grp = tid / cols;
+        if (grp < groups) {
+            float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+            int s = grp;
+            for (; s + groups < splits; s += 2 * groups) {
+                float4 v0 = reinterpret_cast<const float4*>(o + int64_t(s) * Hd)[col];
+                float4 v1 = reinterpret_cast<const float4*>(o + int64_t(s + groups) * Hd)[col];
+                float w0 = wts[s], w1 = wts[s + groups];
+                a0.x = fmaf(w0, v0.x, a0.x); a0.y = fmaf(w0, v0.y, a0.y);
+                a0.z = fmaf(w0, v0.z, a0.z); a0.w = fmaf(w0, v0.w, a0.w);
+                a1.x = fmaf(w1, v1.x, a1.x); a1.y = fmaf(w1, v1.y, a1.y);
+                a1.z = fmaf(w1, v1.z, a1.z); a1.w = fmaf(w1, v1.w, a1.w);
+            }
+            if (s < splits) {
+                float4 v0 = reinterpret_cast<const float4*>(o + int64_t(s) * Hd)[col];
+                float w0 = wts[s];
+                a0.x = fmaf(w0, v0.x, a0.x); a0.y = fmaf(w0, v0.y, a0.y);
+                a0.z = fmaf(w0, v0.z, a0.z); a0.w = fmaf(w0, v0.w, a0.w);
+            }
+            float4 r = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
+            reinterpret_cast<float4*>(part + int64_t(grp) * Hd)[col] = r;
+        }
+        __syncthreads();
+        for (int64_t d = tid; d < Hd; d += kCombThreads) {
+            float acc = 0.f;
+            for (int g = 0; g < groups; ++g) acc += part[g * Hd + d];
+            Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+        }
+    } else {
+        for (int64_t d = tid; d < Hd; d += kCombThreads) {
+            float acc = 0.f;
+            for (int s = 0; s < splits; ++s) acc = fmaf(wts[s], o[int64_t(s) * Hd + d], acc);
+            Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+        }
     }
 }
 
 bool fast_path(const FlashDecode& p) {
     bool hd_ok = p.Hd == 64 || p.Hd == 128 || p.Hd == 256 || p.Hd == 512;
-    return hd_ok && p.q_dtype == p.kv_dtype && aligned16(p.k) && aligned16(p.v);
+    bool ring_fits = !(p.kv_dtype == PC_F32 && p.Hd == 512);  // two stages must fit
+    return hd_ok && ring_fits && p.q_dtype == p.kv_dtype && aligned16(p.k) && aligned16(p.v);
 }
 
 int heads_per_cta(const FlashDecode& p) {
@@ -683,7 +729,8 @@ cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& pl
                                  const float* pl, cudaStream_t s) {
     if (plan.splits <= 1) return cudaSuccess;
     dim3 grid(unsigned(p.Nq), unsigned(p.B));
-    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(kCombPar) * p.Hd) * 4;
+    const int64_t groups = (p.Hd % 4 == 0 && p.Hd / 4 <= kCombThreads) ? kCombThreads / (p.Hd / 4) : 0;
+    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(groups) * p.Hd) * 4;
     switch (p.out_dtype) {
     case PC_F32:
         return launch_k(fd_combine_kernel<TF32>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,

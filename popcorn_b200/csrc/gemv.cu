@@ -161,6 +161,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
                 }
                 if (s_abort) break;
             }
+            // Own loads issued: warm L2 for the next kernel of the chain.
+            for (int r = 0; r < 2; ++r) prefetch_share_l2(p.pf.ptr[r], p.pf.bytes[r], blockIdx.x, gridDim.x);
         }
     } else {
         // ---- consumers ----

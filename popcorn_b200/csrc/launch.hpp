@@ -17,6 +17,14 @@ struct DeviceInfo {
 };
 DeviceInfo device_info(int device);
 
+// Up to two address ranges whose lines a kernel pulls into L2 once its own
+// loads are issued (cp.async.bulk.prefetch.L2), so the next kernel of a
+// chain finds its operands in L2. A hint only: it never changes results.
+struct L2Prefetch {
+    const void* ptr[2];
+    uint64_t bytes[2];
+};
+
 // KVCacheWrite.metal:7-59 semantics. When pos_dev != nullptr the offset is
 // read from device memory (*pos_dev) at run time.
 struct KVWrite {
@@ -73,6 +81,7 @@ struct Gemv {
     void* v_cache;
     int64_t q_rows, kv_rows, Hd, Smax, offset;
     const int32_t* pos_dev;
+    L2Prefetch pf;
 };
 cudaError_t gemv(const Gemv& p, cudaStream_t stream);
 
@@ -113,6 +122,7 @@ struct FlashDecode {
     float scale;
     int mask_kind;
     int32_t window;
+    L2Prefetch pf;
 };
 struct FlashDecodePlan {
     int splits;

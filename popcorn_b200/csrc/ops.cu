@@ -11,7 +11,17 @@ namespace popcorn {
 void set_last_error(const std::string& m);
 KernelCommandEncoder& encoder_impl(pc_encoder* e);
 
+void Kernel::set_prefetch(int, const void*, uint64_t) {
+    fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, std::string(name()) + " takes no L2 prefetch hint.");
+}
+
 namespace {
+
+void put_prefetch(launch::L2Prefetch& pf, int slot, const void* ptr, uint64_t bytes) {
+    if (slot < 0 || slot > 1) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "prefetch slot must be 0 or 1.");
+    pf.ptr[slot] = bytes ? ptr : nullptr;
+    pf.bytes[slot] = ptr ? bytes : 0;
+}
 
 std::string dims_string(const std::vector<int64_t>& v) {
     std::ostringstream os;
@@ -97,6 +107,11 @@ public:
 
     const char* name() const override { return "FlashAttention"; }
 
+    void set_prefetch(int slot, const void* ptr, uint64_t bytes) override {
+        if (path_ != PC_PATH_DECODING) Kernel::set_prefetch(slot, ptr, bytes);
+        put_prefetch(pf_, slot, ptr, bytes);
+    }
+
     std::vector<Binding> tensors() const override {
         std::vector<Binding> b = {{q_, PC_ACCESS_READ}, {k_, PC_ACCESS_READ}, {v_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
         if (has_lens_) b.push_back({lens_, PC_ACCESS_READ});
@@ -117,7 +132,7 @@ public:
         }
         launch::FlashDecode p{q_.data(), q_.dtype(), k_.data(), v_.data(), k_.dtype(), out_.data(), out_.dtype(),
                               B_, Nq_, Nkv_, Sk_, Hd_, has_lens_ ? static_cast<const int32_t*>(lens_.data()) : nullptr,
-                              scale_, mask_.kind, mask_.window};
+                              scale_, mask_.kind, mask_.window, pf_};
         launch::FlashDecodePlan plan = launch::flash_decode_plan(p, enc.sm_count());
         // FlashDecoding.swift:55-59: partial O [B,Nq,P,Hd], m and l [B,Nq,P], f32.
         std::vector<ScratchSpec> specs = {{{B_, Nq_, plan.splits, Hd_}, PC_F32},
@@ -159,6 +174,7 @@ private:
     float scale_;
     pc_attention_mask mask_;
     int path_ = PC_PATH_DECODING;
+    launch::L2Prefetch pf_{};
 };
 
 // ---------------------------------------------------------------------------
@@ -285,6 +301,10 @@ public:
         return launch::Matmul{a_.data(), a_.dtype(), b_.data(), b_.dtype(), c_.data(), c_.dtype(), m_, k_, n_, tb_ ? 1 : 0};
     }
     const char* name() const override { return "Matmul"; }
+    void set_prefetch(int slot, const void* ptr, uint64_t bytes) override {
+        if (!gemv_) Kernel::set_prefetch(slot, ptr, bytes);
+        put_prefetch(pf_, slot, ptr, bytes);
+    }
     std::vector<Binding> tensors() const override {
         return {{a_, PC_ACCESS_READ}, {b_, PC_ACCESS_READ}, {c_, PC_ACCESS_WRITE}};
     }
@@ -295,6 +315,7 @@ public:
             g.x = a_.data(); g.x_dtype = a_.dtype(); g.w = b_.data(); g.w_dtype = b_.dtype();
             g.out = c_.data(); g.out_dtype = c_.dtype(); g.K = k_; g.N = n_;
             g.epilogue = launch::Epilogue::kStore;
+            g.pf = pf_;
             enc.dispatch(function_names_, tensors(), [g](cudaStream_t s) { return launch::gemv(g, s); });
             return;
         }
@@ -307,6 +328,7 @@ private:
     int64_t m_, k_, n_;
     bool tb_;
     bool gemv_ = false;
+    launch::L2Prefetch pf_{};
 };
 
 // ---------------------------------------------------------------------------
@@ -402,6 +424,7 @@ public:
     }
     const char* name() const override { return name_; }
     std::vector<Binding> tensors() const override { return bindings_; }
+    void set_prefetch(int slot, const void* ptr, uint64_t bytes) override { put_prefetch(g_.pf, slot, ptr, bytes); }
     void encode(KernelCommandEncoder& enc) const override {
         launch::Gemv g = g_;
         enc.dispatch(function_names_, bindings_, [g](cudaStream_t s) { return launch::gemv(g, s); });
@@ -563,6 +586,17 @@ int pc_kernel_binding(const pc_kernel* kernel, int index, pc_tensor* tensor, int
     }
     if (tensor) *tensor = kernel->bindings[size_t(index)].tensor.d;
     if (access) *access = kernel->bindings[size_t(index)].access;
+    return PC_OK;
+}
+
+int pc_kernel_set_l2_prefetch(pc_kernel* kernel, int32_t slot, const void* ptr, uint64_t bytes) {
+    try {
+        if (!kernel) fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, "kernel is null.");
+        kernel->impl->set_prefetch(slot, ptr, bytes);
+    } catch (const PopcornError& e) {
+        set_last_error(e.message);
+        return e.code;
+    }
     return PC_OK;
 }
 

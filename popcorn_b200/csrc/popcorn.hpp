@@ -162,6 +162,9 @@ public:
     virtual void encode(KernelCommandEncoder& encoder) const = 0;
     // The function names the kernel launches, ';'-separated.
     const std::string& function_names() const { return function_names_; }
+    // L2 prefetch hint (slot 0 or 1) for kernels that stream from HBM; the
+    // default rejects it.
+    virtual void set_prefetch(int slot, const void* ptr, uint64_t bytes);
 
 protected:
     std::string function_names_;

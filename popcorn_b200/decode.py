@@ -90,7 +90,7 @@ class DecodeStack:
     output on exit (it ping-pongs through two buffers).
     """
 
-    def __init__(self, library, shape, n_layers, seed=0, device=0):
+    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False):
         import torch
         self.shape = shape
         self.library = library
@@ -111,6 +111,7 @@ class DecodeStack:
         self.pos_state = torch.zeros(2, dtype=torch.int32, device=dev)
         # scratch for the decode attention partials (reused by every layer)
         self.scratch = FixedScratch(64 << 20, device)
+        self.l2_prefetch = l2_prefetch
         self._kernels = None
 
     def kernels(self):
@@ -132,9 +133,32 @@ class DecodeStack:
                                        add_one_to_weight=True, activation=s.activation))
             ks.append(Kernels.MatmulResidual(self.act, w.w_down, self.h, into=nxt))
             cur, nxt = nxt, cur
+        if self.l2_prefetch:
+            self._chain_prefetch(ks)
         self.out = cur
         self._kernels = ks
         return ks
+
+    # Bytes of the next operand each kernel pulls into L2 once its own loads
+    # are issued (an L2 of 126 MB holds these comfortably).
+    PREFETCH_CAP = 16 << 20
+
+    def _chain_prefetch(self, ks):
+        """Each kernel warms L2 with the start of the next kernel's operand
+        (QKV -> this layer's K/V cache, attention -> W_o, o_proj -> W_gate and
+        W_up, gated MLP -> W_down, down_proj -> the next layer's W_qkv), so
+        HBM stays busy across kernel boundaries."""
+        cap = self.PREFETCH_CAP
+        L = len(self.layers)
+        for i, w in enumerate(self.layers):
+            nxt = self.layers[(i + 1) % L]
+            qkv, fd, oproj, mlp, down = ks[5 * i:5 * i + 5]
+            qkv.set_l2_prefetch(0, w.k_cache).set_l2_prefetch(1, w.v_cache)
+            fd.set_l2_prefetch(0, w.w_o)
+            oproj.set_l2_prefetch(0, w.w_gate, min(cap, _nbytes(w.w_gate)))
+            oproj.set_l2_prefetch(1, w.w_up, min(cap, _nbytes(w.w_up)))
+            mlp.set_l2_prefetch(0, w.w_down, min(2 * cap, _nbytes(w.w_down)))
+            down.set_l2_prefetch(0, nxt.w_qkv)
 
     def encoder(self, stream=None):
         return KernelCommandEncoder(self.library, stream=stream, scratch=self.scratch)
@@ -152,6 +176,10 @@ class DecodeStack:
 
     def algorithmic_bytes_per_step(self, ctx):
         return len(self.layers) * self.shape.bytes_per_token(ctx)
+
+
+def _nbytes(t):
+    return t.numel() * t.element_size()
 
 
 __all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack"]
