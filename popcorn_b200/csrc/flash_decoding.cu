@@ -13,9 +13,9 @@
 //    read of their K/V rows (the reference re-reads K/V once per query head).
 //  * A producer warp streams 32-key K and V tiles HBM -> shared memory with
 //    the bulk-copy engine (cp.async.bulk, 1-D, no multicast) into a ring of
-//    up to 8 stages (<= 192 KB in flight per SM), tracked by full/empty
+//    up to 8 stages (<= 128 KB in flight per SM), tracked by full/empty
 //    mbarriers.
-//  * Two groups of four consumer warps take alternate tiles; each warp
+//  * Four groups of four consumer warps take tiles round-robin; each warp
 //    scores 8 keys per tile: lanes hold Hd/32 contiguous head dims (one
 //    16-byte shared load per key row at Hd 256, conflict-free), then a
 //    transpose-reduction folds the 8 x G partial dots across the warp in 9G
@@ -23,9 +23,9 @@
 //    merge at the end.
 //  * The split count is chosen for whole waves over the SMs; a small
 //    parallel kernel merges the splits (skipped with one split).
-//  * Before griddepcontrol.wait the producer warms L2 with the split's K/V
-//    rows (cp.async.bulk.prefetch.L2), overlapping the read with the
-//    previous kernel's tail.
+//  * Before griddepcontrol.wait the producer warms L2 with the first ring's
+//    worth of the split's K/V rows (cp.async.bulk.prefetch.L2), overlapping
+//    the read with the previous kernel's tail.
 //  * Every mbarrier wait is bounded; a wait that gives up sets a device
 //    error word (pc_device_error_check) and the CTA drains its copies and
 //    leaves.
@@ -46,9 +46,6 @@ namespace launch {
 namespace {
 
 constexpr int kTileKeys = 32;  // 8 keys per warp per tile
-constexpr int kGroups = 2;     // consumer groups (alternate tiles)
-constexpr int kCWarps = 4 * kGroups;
-constexpr int kFastThreads = (kCWarps + 1) * 32;
 constexpr int kThreads = 128;  // generic and combine kernels
 constexpr int kWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -88,17 +85,23 @@ struct FDShape {
     static constexpr int kRowBytes = HD * Elem<KV>::bytes;
     static constexpr int kTileBytes = kTileKeys * kRowBytes;  // one of K or V
     static constexpr int kStageBytes = 2 * kTileBytes;
-    // An even ring depth: tiles t and t + kStages then belong to the same
-    // consumer group, so a group never waits on a stage's phase two steps
-    // ahead of the one in flight (the parity would alias).
-    static constexpr int kStages = std::max(2, std::min(8, 196608 / kStageBytes) & ~1);
+    // Four consumer groups of four warps take tiles round-robin (two when
+    // the ring has fewer than four stages). The ring depth is a multiple of
+    // the group count, so tiles t and t + kStages belong to the same group
+    // and no group ever waits on a stage's phase two steps ahead of the one
+    // in flight (the parity would alias).
+    static constexpr int kRing = std::max(2, std::min(8, 131072 / kStageBytes));
+    static constexpr int kGroups = kRing >= 4 ? 4 : 2;
+    static constexpr int kStages = kRing / kGroups * kGroups;
+    static constexpr int kCWarps = 4 * kGroups;
+    static constexpr int kThreads = (kCWarps + 1) * 32;
 };
 
 template <class KV, int HD, int G>
 constexpr size_t fd_smem_bytes() {
     using S = FDShape<KV, HD>;
     size_t ring = size_t(S::kStages) * S::kStageBytes;
-    size_t merge = size_t(kCWarps) * G * (HD + 2) * 4;
+    size_t merge = size_t(S::kCWarps) * G * (HD + 2) * 4;
     return ring > merge ? ring : merge;
 }
 
@@ -165,10 +168,13 @@ __device__ __forceinline__ void write_result(const FDArgs& a, int64_t b, int64_t
 }
 
 template <class KV, int HD, int G>
-__global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArgs a) {
+__global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kernel(const FDArgs a) {
     using S = FDShape<KV, HD>;
     constexpr int E = S::E;
     constexpr int NST = S::kStages;
+    constexpr int kGroups = S::kGroups;
+    constexpr int kCWarps = S::kCWarps;
+    constexpr int kFastThreads = S::kThreads;
     extern __shared__ __align__(128) char smem[];
     __shared__ __align__(8) uint64_t full[NST], empty[NST];
     __shared__ volatile int s_abort;
@@ -209,6 +215,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArg
         if (hint_len < 0 || hint_len > p.S) hint_len = p.S;
         int64_t pb, pe;
         split_range(a, hint_len, split, pb, pe);
+        // Only the first ring's worth: L2 must still hold the lines when the
+        // bulk copies read them, or the prefetch would double the traffic.
+        if (pe > pb + int64_t(NST) * kTileKeys) pe = pb + int64_t(NST) * kTileKeys;
         for (int64_t j0 = pb; j0 < pe; j0 += kTileKeys) {
             const uint32_t bytes = uint32_t((pe - j0 < kTileKeys ? pe - j0 : kTileKeys) * S::kRowBytes);
             bulk_prefetch_l2(kbase + j0 * S::kRowBytes, bytes);
@@ -397,8 +406,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) fd_partial_kernel(const FDArg
     if (s_abort) {
         if (tid == 0) {
             // Drain (bounded) the copies issued for tiles nobody consumed.
-            int done = s_consumed[0] > s_consumed[1] ? s_consumed[0] : s_consumed[1];
-            for (int t = done > 0 ? done - 1 : 0; t < s_issued; ++t)
+            int done = s_consumed[0];
+            for (int g = 1; g < kGroups; ++g) done = s_consumed[g] < done ? s_consumed[g] : done;
+            for (int t = done; t < s_issued; ++t)
                 mbar_wait(smem_u32(&full[t % NST]), uint32_t(t / NST) & 1u, &g_fd_error_word);
         }
         __syncthreads();
@@ -623,7 +633,7 @@ cudaError_t run_fast(const FDArgs& a, dim3 grid, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    return launch_k(kern, grid, dim3(kFastThreads), smem, s, a);
+    return launch_k(kern, grid, dim3(FDShape<KV, HD>::kThreads), smem, s, a);
 }
 
 // Register budget: q and O slices take 2*G*Hd/32 floats per lane; keep
@@ -682,9 +692,15 @@ FlashDecodePlan flash_decode_plan(const FlashDecode& p, int sm_count) {
     if (max_tiles < 1) max_tiles = 1;
     int64_t s_lo = (wave + base - 1) / base;
     if (s_lo < 1) s_lo = 1;
+    // Cap the keys per split so that uneven work (ragged lengths leave some
+    // splits short or empty; later waves start when earlier CTAs finish)
+    // averages out over many CTAs.
+    const int64_t tile_cap = p.seq_lens ? 64 : 256;
+    const int64_t s_min = (max_tiles + tile_cap - 1) / tile_cap;
+    const int64_t s_hi = std::max(s_lo * 4, s_min);
     int64_t best_tiles = 0;
     double best_cost = 1e30;
-    for (int64_t s = 1; s <= s_lo * 4 && s <= max_tiles && s <= 1024; ++s) {
+    for (int64_t s = std::max<int64_t>(1, s_min); s <= s_hi && s <= max_tiles && s <= 1024; ++s) {
         int64_t tiles = (max_tiles + s - 1) / s;   // tiles per split
         int64_t splits = (max_tiles + tiles - 1) / tiles;
         int64_t ctas = base * splits;
