@@ -784,6 +784,7 @@ RegisterFunctions reg_fd({
 }  // namespace
 
 uint32_t read_and_clear_gemv_errors();
+uint32_t read_and_clear_gemm_errors();
 
 }  // namespace launch
 }  // namespace popcorn
@@ -796,7 +797,8 @@ extern "C" int pc_device_error_check(int device, uint32_t* flags) {
         return PC_ERR_GPU_DEVICE_REMOVED;
     }
     cudaDeviceSynchronize();
-    *flags = popcorn::launch::read_and_clear_fd_errors() | popcorn::launch::read_and_clear_gemv_errors();
+    *flags = popcorn::launch::read_and_clear_fd_errors() | popcorn::launch::read_and_clear_gemv_errors() |
+             popcorn::launch::read_and_clear_gemm_errors();
     cudaSetDevice(prev);
     return PC_OK;
 }

@@ -1,0 +1,463 @@
+// gemm_tcgen05.cu — tensor-core Matmul for sm_100a (5th-generation tensor
+// cores: tcgen05.mma with TMEM accumulators, TMA-fed shared memory).
+//
+// Semantics: C[m,n] = sum_k A[m,k] * B[n,k] (transposeB, the linear-layer
+// layout) with fp32 accumulation and one rounding at the store — the
+// product Matmul.metal:7-27 / MPPMatmul.metal:20-63 compute. A and B are
+// both bf16 or both f16; C is f32 or the input type.
+//
+// Design (persistent, one CTA per SM, 128 x BN output tiles, BN = 256 for
+// large N):
+//  * warp 0 lane 0 issues TMA tiled loads (cp.async.bulk.tensor.2d, 128-B
+//    swizzle, no multicast) of a 128 x 64 A tile and a BN x 64 B tile per
+//    stage into a 4-stage ring (full/empty mbarriers);
+//  * warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M = 128,
+//    N = BN, K = 16, four per stage) into one of two 128 x BN fp32
+//    accumulators in tensor memory; tcgen05.commit releases each stage back
+//    to the producer when its MMAs are done and then hands the accumulator
+//    to the epilogue;
+//  * warps 2-5 read the accumulator with tcgen05.ld, convert, stage 32 x 32
+//    boxes in shared memory and store them with TMA (cp.async.bulk.tensor
+//    store), while the MMAs of the next tile run into the other accumulator.
+// Skinny problems (M <= 64, e.g. batched decode) run swapped: the weight
+// matrix takes the 128-row MMA side and the activations the N side, and the
+// epilogue writes the transpose.
+//
+// Every mbarrier wait is bounded; on give-up the CTA sets the error word,
+// skips the rest of its work, frees its tensor memory and leaves.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "async.cuh"
+#include "common.cuh"
+#include "dtype.cuh"
+#include "launch.hpp"
+#include "popcorn.hpp"
+
+namespace popcorn {
+
+__device__ unsigned int g_gemm_error_word;
+
+namespace launch {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle atom of 16-bit elements
+constexpr int kStages = 4;
+
+// ---- PTX wrappers -----------------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// Box of shared memory -> global through the tensor map (bounds clipped).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (tcgen05): K-major operand tile written by
+// TMA with 128-byte swizzle; rows of 128 B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3FFF);         // start address
+    d |= uint64_t(1) << 16;                        // leading byte offset (unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;                // stride byte offset: next 8-row group
+    d |= uint64_t(1) << 46;                        // descriptor version (sm100)
+    d |= uint64_t(2) << 61;                        // layout: 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B type, K-major
+// A and B, N and M sizes.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int M, int N) {
+    return (1u << 4)                                    // D: f32
+           | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B: bf16 or f16
+           | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+struct GemmArgs {
+    void* c;
+    int in_f16;           // 1: A/B are f16, 0: bf16
+    int64_t M, N, K;      // of the MMA problem (swapped when `swap`)
+    int64_t ldc;          // row stride of C in elements
+    int swap;             // 1: MMA rows are C columns (C^T = B A^T)
+    int tma_store;        // 1: C tiles leave through map_c
+};
+
+// Persistent form: one CTA per SM walks output tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... Warp 0 lane 0 loads (TMA), warp 1 lane 0
+// multiplies (tcgen05.mma), warps 2-5 drain accumulators (tcgen05.ld, warp w
+// owns TMEM lanes 32*(w%4)..+31). Two accumulators in tensor memory (2 x BN
+// columns) let the epilogue of tile i overlap the MMAs of tile i+1.
+constexpr int kEpiWarps = 4;
+constexpr int kPersistThreads = (2 + kEpiWarps) * 32;
+
+template <int BN, class CT>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_c, const GemmArgs g) {
+    constexpr int A_BYTES = kBM * kBK * 2;
+    constexpr int B_BYTES = BN * kBK * 2;
+    constexpr int STAGE = A_BYTES + B_BYTES;
+    constexpr uint32_t ACC_COLS = BN < 32 ? 32 : BN;
+    constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+    constexpr int ES = int(sizeof(typename CT::storage));
+    constexpr int BOX = 32 * 32 * ES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tfull[2], tempty[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ volatile int s_abort;
+
+    pdl_launch_dependents();
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* staging = smem + size_t(kStages) * STAGE;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ktiles = int((g.K + kBK - 1) / kBK);
+    const int ntm = int((g.M + kBM - 1) / kBM), ntn = int((g.N + BN - 1) / BN);
+    const int ntiles = ntm * ntn;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull[a]), 1);
+            mbar_init(smem_u32(&tempty[a]), kEpiWarps);
+        }
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(&s_tmem), TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            int it = 0;
+            for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+                const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * BN;
+                for (int kt = 0; kt < ktiles; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = uint32_t(it / kStages) & 1u;
+                    if (s_abort || !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, &g_gemm_error_word)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&full[s]);
+                    mbar_expect_tx(bar, STAGE);
+                    unsigned char* st = smem + size_t(s) * STAGE;
+                    tma_load_2d(smem_u32(st), &map_a, kt * kBK, m0, bar);
+                    tma_load_2d(smem_u32(st + A_BYTES), &map_b, kt * kBK, n0, bar);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            const uint32_t idesc = g.in_f16 ? make_idesc(false, kBM, BN) : make_idesc(true, kBM, BN);
+            int it = 0, lt = 0;
+            for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, ++lt) {
+                const int acc = lt & 1;
+                if (!mbar_wait(smem_u32(&tempty[acc]), (uint32_t(lt >> 1) & 1u) ^ 1u, &g_gemm_error_word)) {
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc) * ACC_COLS;
+                for (int kt = 0; kt < ktiles; ++kt, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = uint32_t(it / kStages) & 1u;
+                    if (s_abort || !mbar_wait(smem_u32(&full[s]), ph, &g_gemm_error_word)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(smem + size_t(s) * STAGE);
+                    const uint32_t b_base = a_base + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        tc_mma(d, smem_desc_sw128(a_base + kk * 32), smem_desc_sw128(b_base + kk * 32), idesc,
+                               (kt > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(smem_u32(&empty[s]));
+                }
+                tc_commit(smem_u32(&tfull[acc]));
+            }
+        }
+    } else {
+        // ---- epilogue warps ----
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        unsigned char* wbuf = staging + size_t(warp - 2) * BOX;
+        int lt = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+            const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * BN;
+            const int acc = lt & 1;
+            if (s_abort || !mbar_wait(smem_u32(&tfull[acc]), uint32_t(lt >> 1) & 1u, &g_gemm_error_word)) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t src = tmem + uint32_t(acc) * ACC_COLS + (uint32_t(q * 32) << 16);
+            const int64_t gr = int64_t(m0) + q * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(src + uint32_t(c0), v);
+                if (g.tma_store) {
+                    if (lane == 0) bulk_wait_read<0>();  // the buffer's previous store has read it
+                    __syncwarp();
+                    unsigned char* dst = wbuf + lane * 32 * ES;
+                    if constexpr (ES == 4) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(dst + j * 4) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8)
+                            *reinterpret_cast<uint4*>(dst + j * 2) =
+                                make_uint4(pack2<CT>(v[j], v[j + 1]), pack2<CT>(v[j + 2], v[j + 3]),
+                                           pack2<CT>(v[j + 4], v[j + 5]), pack2<CT>(v[j + 6], v[j + 7]));
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && n0 + c0 < g.N && m0 + q * 32 < g.M) {
+                        tma_store_2d(&map_c, n0 + c0, m0 + q * 32, smem_u32(wbuf));
+                        bulk_commit();
+                    }
+                } else if (gr < g.M) {
+                    if (!g.swap) {
+                        const int64_t base = gr * g.ldc + n0 + c0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c0 + j < g.N) Elem<CT>::store(g.c, base + j, v[j]);
+                    } else {
+                        // MMA row = output column gr; MMA column = output row
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c0 + j < g.N) Elem<CT>::store(g.c, int64_t(n0 + c0 + j) * g.ldc + gr, v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+        }
+        if (g.tma_store && lane == 0) bulk_wait_read<0>();
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---- host: tensor maps ----------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Row-major [rows, cols] output map with a 32 x 32 box, no swizzle.
+bool make_out_map(CUtensorMap* map, void* base, int dtype, int64_t rows, int64_t cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const int es = dtype == PC_F32 ? 4 : 2;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(cols) * es};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUtensorMapDataType t = dtype == PC_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                            : dtype == PC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(map, t, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// 2-D K-major tensor map over rows x K (16-bit), box = box_rows x 64.
+bool make_map(CUtensorMap* map, const void* base, int dtype, int64_t rows, int64_t K, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+    cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype == PC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, class CT>
+cudaError_t launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& g,
+                      cudaStream_t s) {
+    auto kern = gemm_tcgen05_kernel<BN, CT>;
+    constexpr size_t smem = size_t(kStages) * (kBM * kBK * 2 + BN * kBK * 2) +
+                            size_t(kEpiWarps) * 32 * 32 * sizeof(typename CT::storage) + 1024;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = allow_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const int64_t tiles = ((g.N + BN - 1) / BN) * ((g.M + kBM - 1) / kBM);
+    const int sms = current_sm_count();
+    dim3 grid(unsigned(tiles < sms ? tiles : sms));
+    return launch_k(kern, grid, dim3(kPersistThreads), smem, s, ma, mb, mc, g);
+}
+
+template <class CT>
+cudaError_t launch_ct(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, int bn, const GemmArgs& g,
+                      cudaStream_t s) {
+    switch (bn) {
+    case 256: return launch_bn<256, CT>(ma, mb, mc, g, s);
+    case 128: return launch_bn<128, CT>(ma, mb, mc, g, s);
+    case 64: return launch_bn<64, CT>(ma, mb, mc, g, s);
+    case 32: return launch_bn<32, CT>(ma, mb, mc, g, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+// Served: transposeB, A and B both bf16 or both f16, C f32 or the same type,
+// K a multiple of 8 (16-byte row pitch for TMA), 16-byte aligned bases, and
+// a problem big enough to use the tensor cores (M >= 16).
+bool tcgen05_supports(const Matmul& p) {
+    bool types = (p.a_dtype == PC_BF16 || p.a_dtype == PC_F16) && p.b_dtype == p.a_dtype &&
+                 (p.c_dtype == PC_F32 || p.c_dtype == p.a_dtype);
+    return types && p.transpose_b && p.M >= 16 && p.N >= 16 && p.K >= 16 && p.K % 8 == 0 && aligned16(p.a) &&
+           aligned16(p.b) && p.M < (int64_t(1) << 31) && p.N < (int64_t(1) << 31) && encode_fn() != nullptr;
+}
+
+cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
+    // Skinny M: swap so the weight rows fill the 128-row MMA side.
+    const bool swap = p.M <= 64;
+    GemmArgs g{};
+    g.c = p.c;
+    g.in_f16 = p.a_dtype == PC_F16 ? 1 : 0;
+    g.K = p.K;
+    g.ldc = p.N;
+    g.swap = swap ? 1 : 0;
+    const void* a = swap ? p.b : p.a;
+    const void* b = swap ? p.a : p.b;
+    g.M = swap ? p.N : p.M;
+    g.N = swap ? p.M : p.N;
+    int bn = swap ? (g.N <= 32 ? 32 : 64) : (g.N >= 256 ? 256 : 128);
+    CUtensorMap ma, mb, mc;
+    if (!make_map(&ma, a, p.a_dtype, g.M, p.K, kBM) || !make_map(&mb, b, p.a_dtype, g.N, p.K, bn))
+        return cudaErrorInvalidValue;
+    const int ces = p.c_dtype == PC_F32 ? 4 : 2;
+    g.tma_store = (!swap && (p.N * ces) % 16 == 0 && aligned16(p.c) && make_out_map(&mc, p.c, p.c_dtype, p.M, p.N))
+                      ? 1 : 0;
+    if (!g.tma_store) mc = ma;  // unused
+    switch (p.c_dtype) {
+    case PC_F32: return launch_ct<TF32>(ma, mb, mc, bn, g, s);
+    case PC_BF16: return launch_ct<TBF16>(ma, mb, mc, bn, g, s);
+    case PC_F16: return launch_ct<TF16>(ma, mb, mc, bn, g, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+uint32_t read_and_clear_gemm_errors() {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemm_error_word, sizeof(v)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) cudaMemcpyToSymbol(g_gemm_error_word, &zero, sizeof(zero));
+    return v;
+}
+
+namespace {
+RegisterFunctions reg_gemm({
+    {"matmul_tc_bf16_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TBF16>)},
+    {"matmul_tc_f32out_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TF32>)},
+    {"matmul_tc_f16_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TF16>)},
+});
+}  // namespace
+
+}  // namespace launch
+}  // namespace popcorn

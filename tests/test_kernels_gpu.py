@@ -439,3 +439,40 @@ def test_prefill_attention(pc, enc, dt, odt, mask, window, B, Nq, Nkv, Sq, Sk, H
 
 def test_no_device_errors_recorded(pc):
     assert pc.device_error_check(0) == 0
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 tensor-core Matmul (m > 1, 16-bit inputs, transposeB)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M,K,N,dt,odt", [(128, 64, 256, "bf16", "f32"), (256, 2304, 512, "bf16", "bf16"),
+                                          (300, 520, 200, "f16", "f32"), (32, 2304, 4096, "bf16", "bf16"),
+                                          (64, 64, 64, "bf16", "bf16"), (17, 136, 40, "f16", "f16"),
+                                          (1000, 1024, 1000, "bf16", "f32")])
+def test_matmul_tcgen05(pc, enc, M, K, N, dt, odt):
+    rng = np.random.default_rng(M + K + N)
+    a = rand(rng, (M, K), dt)
+    b = rand(rng, (N, K), dt, 0.05)
+    out = empty_dev((M, N), odt)
+    kern = pc.Kernels.Matmul(to_dev(a, dt), to_dev(b, dt), into=out, transpose_b=True)
+    assert kern.function_names == ["matmul_tc_bf16_tb"]
+    run(enc, kern)
+    exp = oracle.matmul(a, dt, b, dt, odt, True)
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul %dx%dx%d" % (M, K, N))
+
+
+def test_matmul_tcgen05_config4_rows(pc, enc):
+    """BASELINE config 4 GEMM (8192 x 2304 x 9216, bf16, transposeB): the full
+    product on the GPU, 24 sampled rows checked against the oracle."""
+    M, K, N = 8192, 2304, 9216
+    g = torch.Generator(device="cuda").manual_seed(4)
+    a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    run(enc, pc.Kernels.Matmul(a, b, into=out, transpose_b=True))
+    rows = np.random.default_rng(0).choice(M, 24, replace=False)
+    rows.sort()
+    a_np = from_dev(a[torch.from_numpy(rows).cuda()].contiguous(), "bf16")
+    exp = oracle.matmul(a_np, "bf16", from_dev(b, "bf16"), "bf16", "bf16", True)
+    got = from_dev(out, "bf16")[rows]
+    assert_close(got, exp, "bf16", what="config-4 GEMM rows")
