@@ -255,6 +255,86 @@ def run_fd_sweep(args):
 
 
 # ---------------------------------------------------------------------------
+# Tensor-parallel 9B-shape batched decode
+# ---------------------------------------------------------------------------
+
+def run_tp(args):
+    """Config 5: Gemma-2-9B-shape decoder (42 layers, vocab 256000), batch 32,
+    KV context 8192, bf16, tensor-parallel over the torchrun ranks with an
+    NCCL all-reduce after o_proj and down_proj. A step = one token for all 32
+    sequences through every layer and the LM head, replayed from one CUDA
+    graph (NCCL captured). Total work is fixed as N grows (strong scaling);
+    value = 32 / step time."""
+    import torch
+    import torch.distributed as dist
+    import popcorn_b200 as pc
+    from popcorn_b200.tp import TPDecodeModel, TPShape
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    hbm_gbs, _, peak_kind = peaks()
+    shape = TPShape(layers=args.tp_layers)
+    model = TPDecodeModel(pc.KernelLibrary(local), shape, rank=rank, world=world, seed=5, device=local)
+    stream = torch.cuda.Stream(device=local)
+
+    def all_reduce(t):
+        if world > 1:
+            dist.all_reduce(t)
+
+    with torch.cuda.stream(stream):
+        model.x.normal_()
+        enc = model.encoder(stream)
+        model.step(enc, all_reduce)  # eager warm-up (NCCL communicator set-up)
+        torch.cuda.synchronize()
+        n0 = enc.dispatch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            model.step(enc, all_reduce)
+        launches = enc.dispatch_count - n0
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = ClockSampler(local)
+        clocks.start()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    per_rank_bytes = model.bytes_per_step()
+    line = {"metric": "Gemma-2-9B-shape batched decode tok/s (42 layers, batch 32, ctx 8192, TP)",
+            "value": shape.B * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV)",
+            "config": {"workload": "config5: 9B-shape decode, %d layers, vocab 256000, batch 32, KV ctx 8192"
+                                   % shape.L, "global_batch": shape.B, "seq_len": shape.ctx,
+                       "parallelism": "tp%d" % world,
+                       "l2": "inputs larger than L2"},
+            "per_rank_hbm_gbs": per_rank_bytes / (ms * 1e-3) / 1e9,
+            "per_rank_frac_of_measured_hbm": per_rank_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, "peak_kind": peak_kind,
+            "allreduce_per_step": 2 * shape.L, "allreduce_bytes": shape.B * shape.H * 2,
+            "gpu_launches": launches * args.steps, "clocks": clk}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 
@@ -266,13 +346,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
-    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep"])
+    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b"])
+    ap.add_argument("--tp-layers", type=int, default=42)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "fd_sweep":
         return run_fd_sweep(args)
+    if args.workload == "tp9b":
+        return run_tp(args)
 
     import torch
     import torch.distributed as dist

@@ -1,0 +1,175 @@
+"""Tensor-parallel batched decode over the C ABI.
+
+Gemma-2-9B-shape decoder (hidden 3584, 16 Q / 8 KV heads, head_dim 256, FFN
+14336, vocab 256000, 42 layers) at batch 32, one process per GPU. Each rank
+holds:
+
+  * Q / K / V projections: the rows of its query heads and KV heads
+    (column-parallel: no communication);
+  * o_proj: the columns of its query heads (row-parallel: partial sums);
+  * gate / up: a contiguous slice of FFN rows (column-parallel);
+  * down_proj: the matching slice of FFN columns (row-parallel);
+  * the LM head (tied embedding): a contiguous slice of the vocabulary.
+
+After o_proj and after down_proj each rank holds a partial [B, hidden] sum;
+one all-reduce (NCCL over NVLink, `torch.distributed`) completes it before
+the residual add — two all-reduces per layer. Norms and residual adds are
+replicated. KV heads must divide evenly: TP <= 8 for 8 KV heads.
+
+Every computation is a popcorn_b200 kernel (Matmul on the tcgen05 tensor
+cores for M = 32, RMSNorm, KVCacheWrite, ragged FlashDecoding, GeluTanh,
+Mul, Add); torch provides device memory, streams and the collective.
+"""
+from .api import AttentionMask, FixedScratch, KernelCommandEncoder, Kernels
+
+
+class TPShape:
+    def __init__(self, hidden=3584, q_heads=16, kv_heads=8, head_dim=256, ffn=14336, vocab=256000, layers=42,
+                 batch=32, ctx=8192, dtype="bf16", eps=1e-6, attn_scale=1.0 / 16):
+        self.H, self.Nq, self.Nkv, self.Hd, self.F, self.V = hidden, q_heads, kv_heads, head_dim, ffn, vocab
+        self.L, self.B, self.ctx, self.dtype, self.eps, self.scale = layers, batch, ctx, dtype, eps, attn_scale
+
+    def weight_bytes(self, world=1):
+        s = self
+        per_layer = ((s.Nq + 2 * s.Nkv) * s.Hd * s.H + s.H * s.Nq * s.Hd + 3 * s.F * s.H) * 2
+        return (s.L * per_layer + s.V * s.H * 2) // world
+
+    def kv_bytes(self, world=1):
+        s = self
+        return s.L * 2 * s.B * s.Nkv * s.ctx * s.Hd * 2 // world
+
+
+def shard_plan(shape, rank, world):
+    """Index ranges a rank owns (the same plan the CPU gloo test checks)."""
+    s = shape
+    if s.Nkv % world or s.Nq % world or s.F % world or s.V % world:
+        raise ValueError("heads, FFN and vocab must divide by the TP degree %d" % world)
+    nq, nkv, f, v = s.Nq // world, s.Nkv // world, s.F // world, s.V // world
+    return {
+        "q_heads": (rank * nq, (rank + 1) * nq),
+        "kv_heads": (rank * nkv, (rank + 1) * nkv),
+        "ffn": (rank * f, (rank + 1) * f),
+        "vocab": (rank * v, (rank + 1) * v),
+    }
+
+
+def shard_layer(full, shape, plan):
+    """Slices a full layer's weights (numpy or torch, [out, in]) for one rank."""
+    s = shape
+    q0, q1 = plan["q_heads"]
+    k0, k1 = plan["kv_heads"]
+    f0, f1 = plan["ffn"]
+    return {
+        "w_q": full["w_q"][q0 * s.Hd:q1 * s.Hd],
+        "w_k": full["w_k"][k0 * s.Hd:k1 * s.Hd],
+        "w_v": full["w_v"][k0 * s.Hd:k1 * s.Hd],
+        "w_o": full["w_o"][:, q0 * s.Hd:q1 * s.Hd],
+        "w_gate": full["w_gate"][f0:f1],
+        "w_up": full["w_up"][f0:f1],
+        "w_down": full["w_down"][:, f0:f1],
+        "attn_norm": full["attn_norm"],
+        "mlp_norm": full["mlp_norm"],
+    }
+
+
+class TPDecodeModel:
+    """One rank's shard of the config-5 model with its KV cache and buffers.
+
+    step() enqueues one decode token for the whole batch through every layer
+    and the LM head; all_reduce(t) is called on each partial sum (NCCL in the
+    benchmark). The position (fixed at ctx - 1, every sequence attends to
+    ctx keys) makes each step the same work as a real step at that context.
+    """
+
+    def __init__(self, library, shape, rank=0, world=1, seed=0, device=0):
+        import torch
+        self.s = s = shape
+        self.rank, self.world = rank, world
+        self.plan = shard_plan(shape, rank, world)
+        self.library = library
+        dev = "cuda:%d" % device
+        dt = {"bf16": torch.bfloat16, "f16": torch.float16}[s.dtype]
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000003 + rank)
+        nq, nkv, f = s.Nq // world, s.Nkv // world, s.F // world
+
+        def w(*shape_, std=0.02):
+            return (torch.randn(*shape_, device=dev, generator=g) * std).to(dt)
+
+        self.layers = []
+        for _ in range(s.L):
+            self.layers.append({
+                "attn_norm": (torch.randn(s.H, device=dev, generator=g) * 0.1).float(),
+                "mlp_norm": (torch.randn(s.H, device=dev, generator=g) * 0.1).float(),
+                "w_q": w(nq * s.Hd, s.H), "w_k": w(nkv * s.Hd, s.H), "w_v": w(nkv * s.Hd, s.H),
+                "w_o": w(s.H, nq * s.Hd), "w_gate": w(f, s.H), "w_up": w(f, s.H), "w_down": w(s.H, f),
+                "k_cache": w(s.B, nkv, s.ctx, s.Hd, std=1.0), "v_cache": w(s.B, nkv, s.ctx, s.Hd, std=1.0),
+            })
+        self.final_norm = (torch.randn(s.H, device=dev, generator=g) * 0.1).float()
+        self.lm_head = w(s.V // world, s.H)
+        B = s.B
+        self.x = torch.zeros(B, s.H, device=dev, dtype=dt)
+        self.xn = torch.zeros_like(self.x)
+        self.h = torch.zeros_like(self.x)
+        self.o = torch.zeros_like(self.x)
+        self.q = torch.zeros(B, nq, 1, s.Hd, device=dev, dtype=dt)
+        self.k = torch.zeros(B, nkv, 1, s.Hd, device=dev, dtype=dt)
+        self.v = torch.zeros(B, nkv, 1, s.Hd, device=dev, dtype=dt)
+        self.attn = torch.zeros(B, nq, 1, s.Hd, device=dev, dtype=dt)
+        self.gate = torch.zeros(B, f, device=dev, dtype=dt)
+        self.up = torch.zeros(B, f, device=dev, dtype=dt)
+        self.logits = torch.zeros(B, s.V // world, device=dev, dtype=dt)
+        self.lens = torch.full((B,), s.ctx, device=dev, dtype=torch.int32)
+        self.scratch = FixedScratch(64 << 20, device)
+        self._ks = None
+
+    def kernels(self):
+        """Kernel objects of one step in order; None marks an all-reduce of
+        self.o (the partial o_proj / down_proj sum)."""
+        if self._ks is not None:
+            return self._ks
+        s, K = self.s, Kernels
+        nq = s.Nq // self.world
+        ks = []
+        for w in self.layers:
+            ks += [K.RMSNorm(self.x, w["attn_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True),
+                   K.Matmul(self.xn, w["w_q"], into=self.q.view(s.B, -1), transpose_b=True),
+                   K.Matmul(self.xn, w["w_k"], into=self.k.view(s.B, -1), transpose_b=True),
+                   K.Matmul(self.xn, w["w_v"], into=self.v.view(s.B, -1), transpose_b=True),
+                   K.KVCacheWrite(self.k, w["k_cache"], offset=s.ctx - 1),
+                   K.KVCacheWrite(self.v, w["v_cache"], offset=s.ctx - 1),
+                   K.FlashDecodingRagged(self.q, w["k_cache"], w["v_cache"], self.lens, into=self.attn,
+                                         scale=s.scale, mask=AttentionMask.causal),
+                   K.Matmul(self.attn.view(s.B, nq * s.Hd), w["w_o"], into=self.o, transpose_b=True),
+                   None,
+                   K.Add(self.x, self.o, into=self.h),
+                   K.RMSNorm(self.h, w["mlp_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True),
+                   K.Matmul(self.xn, w["w_gate"], into=self.gate, transpose_b=True),
+                   K.Matmul(self.xn, w["w_up"], into=self.up, transpose_b=True),
+                   K.GeluTanh(self.gate, into=self.gate),
+                   K.Mul(self.gate, self.up, into=self.gate),
+                   K.Matmul(self.gate, w["w_down"], into=self.o, transpose_b=True),
+                   None,
+                   K.Add(self.h, self.o, into=self.x)]
+        ks += [K.RMSNorm(self.x, self.final_norm, into=self.xn, eps=s.eps, add_one_to_weight=True),
+               K.Matmul(self.xn, self.lm_head, into=self.logits, transpose_b=True)]
+        self._ks = ks
+        return ks
+
+    def encoder(self, stream=None):
+        return KernelCommandEncoder(self.library, stream=stream, scratch=self.scratch)
+
+    def step(self, encoder, all_reduce):
+        for k in self.kernels():
+            if k is None:
+                all_reduce(self.o)
+            else:
+                encoder.encode(k)
+
+    def bytes_per_step(self):
+        """Algorithmic HBM bytes one rank moves per step: its weight shard
+        once and its KV-cache shard once."""
+        return self.s.weight_bytes(self.world) + self.s.kv_bytes(self.world)
+
+
+__all__ = ["TPShape", "TPDecodeModel", "shard_plan", "shard_layer"]
