@@ -330,7 +330,12 @@ def run_tp(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        # Leave without tearing the communicator down: a destroy after a
+        # graph-captured NCCL collective was seen to block for minutes.
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
     return 0
 
 
@@ -526,7 +531,12 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        # Leave without tearing the communicator down: a destroy after a
+        # graph-captured NCCL collective was seen to block for minutes.
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
     return 0
 
 
