@@ -287,6 +287,66 @@ PC_API int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_we
                                     const pc_tensor* k_cache, const pc_tensor* v_cache, int64_t offset,
                                     const pc_tensor* position, pc_kernel** kernel);
 
+/* ---- fused decode step (extension) ---------------------------------------- */
+
+/* One decode layer's weights and KV caches (device pointers). Weights are
+ * [out, in]: w_qkv [(Nq+2*Nkv)*Hd, H], w_o [H, Nq*Hd], w_gate / w_up [F, H],
+ * w_down [H, F]; norms f32 [H] (NULL = no weight); caches [Nkv, Smax, Hd]. */
+typedef struct pc_decode_layer {
+    const void* w_qkv;
+    const void* w_o;
+    const void* w_gate;
+    const void* w_up;
+    const void* w_down;
+    const float* attn_norm;
+    const float* mlp_norm;
+    void* k_cache;
+    void* v_cache;
+} pc_decode_layer;
+
+/* A batch-1 decode step through a stack of layers. Each layer is the op
+ * sequence of Gemma4TextInference.swift:312-436 restricted to RMSNorm ->
+ * QKV -> KVCacheWrite -> FlashAttention (Sq = 1) -> o_proj -> Add ->
+ * RMSNorm -> gated MLP -> Add, with every intermediate rounded to `dtype`
+ * where the reference ops store it. `layers` points to `num_layers`
+ * pc_decode_layer entries in DEVICE memory. Activation buffers (device,
+ * `dtype`): x [H] holds the input and, for an even layer count, the output
+ * (odd: x2); h [H], q [Nq*Hd], attn [Nq*Hd], act [F]. position: int32 [1]
+ * on the device (the new token's index; it attends to keys 0..position).
+ * workspace: pc_decode_stack_workspace_bytes() bytes, zero-filled once
+ * before the first use; every launch leaves it zeroed (except after a
+ * device error, see pc_device_error_check). Head dim 256, f16 or bf16,
+ * Nq / Nkv in {1, 2, 4}, hidden and ffn multiples of 8, hidden <= 8192,
+ * max(hidden, ffn, Nq*Hd) <= 12288; every buffer and weight 16-byte
+ * aligned. */
+typedef struct pc_decode_stack_desc {
+    int32_t dtype;
+    int32_t num_layers;
+    int32_t hidden, q_heads, kv_heads, head_dim, ffn, max_ctx;
+    float eps, attn_scale;
+    int32_t activation;        /* pc_activation */
+    int32_t add_one_to_weight; /* RMSNorm weight is (1 + w) */
+    const pc_decode_layer* layers;
+    void* x;
+    void* x2;
+    void* h;
+    void* q;
+    void* attn;
+    void* act;
+    const int32_t* position;
+    void* workspace;
+    uint64_t workspace_bytes;
+} pc_decode_stack_desc;
+
+/* Extension (no reference counterpart): workspace size for a descriptor. */
+PC_API int pc_decode_stack_workspace_bytes(const pc_decode_stack_desc* desc, uint64_t* bytes);
+/* Extension: the whole step as ONE persistent kernel (one CTA per SM, all
+ * co-resident, ordered by arrival counters in the workspace): per-group
+ * producer warps stream the next ops' weights into shared memory while the
+ * current op finishes. Results equal the per-op kernels' within the chain
+ * tolerance of a whole layer (dot products sum in another order). */
+PC_API int pc_kernel_decode_stack(const pc_decode_stack_desc* desc, pc_kernel** kernel);
+
 /* ---- decode attention without allocation ------------------------------- */
 
 /* No counterpart in the reference. For callers that cannot allocate device

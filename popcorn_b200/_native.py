@@ -28,6 +28,16 @@ RELEASE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_void_p)
 HOOK_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p)
 
 
+class pc_decode_stack_desc(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("num_layers", ctypes.c_int32), ("hidden", ctypes.c_int32),
+                ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("ffn", ctypes.c_int32), ("max_ctx", ctypes.c_int32), ("eps", ctypes.c_float),
+                ("attn_scale", ctypes.c_float), ("activation", ctypes.c_int32), ("add_one_to_weight", ctypes.c_int32),
+                ("layers", ctypes.c_void_p), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("h", ctypes.c_void_p),
+                ("q", ctypes.c_void_p), ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p),
+                ("position", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64)]
+
+
 class pc_scratch_allocator(ctypes.Structure):
     _fields_ = [("ctx", ctypes.c_void_p), ("borrow", BORROW_FN), ("release", RELEASE_FN)]
 
@@ -105,6 +115,8 @@ def _declare(L):
         "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
         "pc_flash_decoding_noalloc": ([T, T, T, T, T, F, M, P], I),
         "pc_flash_decoding_noalloc_capacity": ([], ctypes.c_size_t),
+        "pc_decode_stack_workspace_bytes": ([ctypes.POINTER(pc_decode_stack_desc), ctypes.POINTER(ctypes.c_uint64)], I),
+        "pc_kernel_decode_stack": ([ctypes.POINTER(pc_decode_stack_desc), PP], I),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -521,6 +521,25 @@ class Kernels:
                              keep=_keep(x, norm_weight, w_qkv, q_out, k_cache, v_cache, position))
 
 
+class DecodeStackKernel(Kernel):
+    """Extension: a whole batch-1 decode step through a layer stack as one
+    persistent kernel (pc_kernel_decode_stack). `desc` is a filled
+    _native.pc_decode_stack_desc; `keep` holds the tensors it points into."""
+
+    def __init__(self, desc, keep=()):
+        self._desc = desc
+        super().__init__(N.lib().pc_kernel_decode_stack, ctypes.byref(desc), keep=tuple(keep))
+
+    @staticmethod
+    def workspace_bytes(desc):
+        out = ctypes.c_uint64()
+        _check(N.lib().pc_decode_stack_workspace_bytes(ctypes.byref(desc), ctypes.byref(out)))
+        return out.value
+
+
+Kernels.DecodeStack = DecodeStackKernel
+
+
 def device_error_check(device=0):
     """Reads and clears the device error word (bit 0: a bounded wait gave up)."""
     flags = ctypes.c_uint32()

@@ -158,5 +158,44 @@ struct FlashAttention {
 cudaError_t flash_attention(const FlashAttention& p, cudaStream_t stream);
 bool flash_attention_uses_tensor_cores(const FlashAttention& p);
 
+// One persistent kernel for a batch-1 decode step through a layer stack
+// (decode_step.cu). `layers` points to device memory.
+struct DecodeLayer {
+    const void* w_qkv;
+    const void* w_o;
+    const void* w_gate;
+    const void* w_up;
+    const void* w_down;
+    const float* attn_norm;
+    const float* mlp_norm;
+    void* k_cache;  // [Nkv, Smax, Hd]
+    void* v_cache;
+};
+struct DecodeStep {
+    const DecodeLayer* layers;
+    int L, H, Nq, Nkv, Hd, F, Smax;
+    float eps, scale;
+    int activation, add_one, dtype;
+    void* x;   // [H] input; the output lands in x when L is even, else x2
+    void* x2;
+    void* h;
+    void* q;
+    void* attn;
+    void* act;
+    float* po;
+    float* pm;
+    float* pl;
+    unsigned int* counters;  // L*6 + 1 op counters, then L*Nkv head counters; zero before the first launch; left zero
+    const int32_t* pos;      // [1] on the device: position of the new token
+    int splits, chunk_tiles;
+    int rows[4], kc[4], nkc[4];  // per GEMV op: rows per tile, columns per stage, stages per tile
+    int xs_bytes;
+    int grid;
+    int64_t l2_ahead;  // bytes of L2 prefetch the producer keeps ahead of its ring
+};
+bool decode_step_plan(DecodeStep& p, int sm_count);
+size_t decode_step_workspace_bytes(const DecodeStep& p);
+cudaError_t decode_step(const DecodeStep& p, cudaStream_t stream);
+
 }  // namespace launch
 }  // namespace popcorn

@@ -538,6 +538,79 @@ std::unique_ptr<Kernel> make_qkv(const Tensor& x, const Tensor* nw, float eps, b
     return std::make_unique<FusedGemvKernel>("QKVProjection", b, g, std::string("qkv_matvec_") + dt_tag(dt));
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode step (decode_step.cu)
+// ---------------------------------------------------------------------------
+launch::DecodeStep make_step(const pc_decode_stack_desc* d) {
+    if (!d) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "descriptor is null.");
+    if (d->dtype != PC_F16 && d->dtype != PC_BF16)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "decode stack needs f16 or bf16.");
+    if (d->num_layers < 1 || d->hidden < 8 || d->ffn < 8 || d->max_ctx < 1 || d->q_heads < 1 || d->kv_heads < 1)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "decode stack dimensions must be positive.");
+    if (d->q_heads % d->kv_heads != 0)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "query heads must be divisible by KV heads.");
+    if (d->activation != PC_ACT_GELU_TANH && d->activation != PC_ACT_SILU)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "unknown activation.");
+    if (!d->layers || !d->x || !d->x2 || !d->h || !d->q || !d->attn || !d->act || !d->position)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "decode stack buffers must all be given.");
+    launch::DecodeStep p{};
+    p.layers = reinterpret_cast<const launch::DecodeLayer*>(d->layers);
+    p.L = d->num_layers;
+    p.H = d->hidden; p.Nq = d->q_heads; p.Nkv = d->kv_heads; p.Hd = d->head_dim; p.F = d->ffn; p.Smax = d->max_ctx;
+    p.eps = d->eps; p.scale = d->attn_scale; p.activation = d->activation; p.add_one = d->add_one_to_weight != 0;
+    p.dtype = d->dtype;
+    p.x = d->x; p.x2 = d->x2; p.h = d->h; p.q = d->q; p.attn = d->attn; p.act = d->act; p.pos = d->position;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    p.grid = launch::device_info(dev).sm_count;
+    if (!launch::decode_step_plan(p, p.grid))
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+             "fused decode step serves head dim 256, Nq/Nkv in {1,2,4}, hidden/ffn multiples of 8.");
+    return p;
+}
+
+class DecodeStackKernel : public Kernel {
+public:
+    explicit DecodeStackKernel(const pc_decode_stack_desc* d) : p_(make_step(d)) {
+        const size_t need = launch::decode_step_workspace_bytes(p_);
+        if (!d->workspace || d->workspace_bytes < need)
+            fail(PC_ERR_WORKSPACE_EXHAUSTED, "decode stack workspace needs " + std::to_string(need) + " bytes; got " +
+                                                 std::to_string(d->workspace_bytes) + ".");
+        char* ws = static_cast<char*>(d->workspace);
+        const size_t o = size_t(p_.Nq) * p_.splits * p_.Hd * 4, ml = size_t(p_.Nq) * p_.splits * 4;
+        p_.counters = reinterpret_cast<unsigned int*>(ws);
+        size_t off = (size_t(p_.L * 6 + 1 + p_.L * p_.Nkv) * 4 + 255) / 256 * 256;
+        p_.po = reinterpret_cast<float*>(ws + off);
+        p_.pm = reinterpret_cast<float*>(ws + off + o);
+        p_.pl = reinterpret_cast<float*>(ws + off + o + ml);
+        function_names_ = d->dtype == PC_BF16 ? "decode_step_bf16" : "decode_step_f16";
+        auto t = [](void* ptr, int64_t n, int dt) {
+            pc_tensor x{};
+            x.data = ptr;
+            x.dtype = dt;
+            x.rank = 1;
+            x.shape[0] = n;
+            return Tensor(x);
+        };
+        int dt = d->dtype;
+        bindings_ = {{t(d->x, p_.H, dt), PC_ACCESS_READ_WRITE}, {t(d->x2, p_.H, dt), PC_ACCESS_READ_WRITE},
+                     {t(d->h, p_.H, dt), PC_ACCESS_READ_WRITE}, {t(d->q, p_.Nq * p_.Hd, dt), PC_ACCESS_READ_WRITE},
+                     {t(d->attn, p_.Nq * p_.Hd, dt), PC_ACCESS_READ_WRITE}, {t(d->act, p_.F, dt), PC_ACCESS_READ_WRITE},
+                     {t(d->workspace, int64_t(need), PC_U8), PC_ACCESS_READ_WRITE},
+                     {t(const_cast<int32_t*>(d->position), 1, PC_I32), PC_ACCESS_READ}};
+    }
+    const char* name() const override { return "DecodeStack"; }
+    std::vector<Binding> tensors() const override { return bindings_; }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::DecodeStep p = p_;
+        enc.dispatch(function_names_, bindings_, [p](cudaStream_t s) { return launch::decode_step(p, s); });
+    }
+
+private:
+    launch::DecodeStep p_;
+    std::vector<Binding> bindings_;
+};
+
 }  // namespace
 }  // namespace popcorn
 
@@ -849,6 +922,23 @@ int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, f
                          tensor_arg(w_qkv, "w_qkv"), tensor_arg(q_out, "q_out"), tensor_arg(k_cache, "k_cache"),
                          tensor_arg(v_cache, "v_cache"), offset, position ? &pos : nullptr),
                 kernel);
+    PC_GUARD_END
+}
+
+int pc_decode_stack_workspace_bytes(const pc_decode_stack_desc* desc, uint64_t* bytes) {
+    try {
+        launch::DecodeStep p = make_step(desc);
+        *bytes = launch::decode_step_workspace_bytes(p);
+    } catch (const PopcornError& e) {
+        set_last_error(e.message);
+        return e.code;
+    }
+    return PC_OK;
+}
+
+int pc_kernel_decode_stack(const pc_decode_stack_desc* desc, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<DecodeStackKernel>(desc), kernel);
     PC_GUARD_END
 }
 

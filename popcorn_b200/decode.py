@@ -90,7 +90,7 @@ class DecodeStack:
     output on exit (it ping-pongs through two buffers).
     """
 
-    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False):
+    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False):
         import torch
         self.shape = shape
         self.library = library
@@ -112,12 +112,15 @@ class DecodeStack:
         # scratch for the decode attention partials (reused by every layer)
         self.scratch = FixedScratch(64 << 20, device)
         self.l2_prefetch = l2_prefetch
+        self.fused = fused
         self._kernels = None
 
     def kernels(self):
         """The validated kernel objects of one step (built once)."""
         if self._kernels is not None:
             return self._kernels
+        if self.fused:
+            return self._fused_kernels()
         s = self.shape
         pos = self.pos_state[0:1]
         lens = self.pos_state[1:2]
@@ -138,6 +141,31 @@ class DecodeStack:
         self.out = cur
         self._kernels = ks
         return ks
+
+    def _fused_kernels(self):
+        """The whole step as one persistent kernel (Kernels.DecodeStack)."""
+        import torch
+        from . import _native as N
+        from .api import DecodeStackKernel
+        s = self.shape
+        dev = self.x.device
+        rows = [[w.w_qkv.data_ptr(), w.w_o.data_ptr(), w.w_gate.data_ptr(), w.w_up.data_ptr(), w.w_down.data_ptr(),
+                 w.attn_norm.data_ptr(), w.mlp_norm.data_ptr(), w.k_cache.data_ptr(), w.v_cache.data_ptr()]
+                for w in self.layers]
+        self._layer_table = torch.tensor(rows, dtype=torch.int64).to(dev)
+        dt = {"f16": 9, "bf16": 10}[s.dtype]
+        desc = N.pc_decode_stack_desc(dt, len(self.layers), s.H, s.Nq, s.Nkv, s.Hd, s.F, s.Smax, s.eps, s.scale,
+                                      s.activation, 1, self._layer_table.data_ptr(), self.x.data_ptr(),
+                                      self.x2.data_ptr(), self.h.data_ptr(), self.q.data_ptr(),
+                                      self.attn.data_ptr(), self.act.data_ptr(), self.pos_state.data_ptr(), None, 0)
+        nbytes = DecodeStackKernel.workspace_bytes(desc)
+        self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        desc.workspace = self._workspace.data_ptr()
+        desc.workspace_bytes = nbytes
+        k = DecodeStackKernel(desc, keep=(self._layer_table, self._workspace))
+        self.out = self.x if len(self.layers) % 2 == 0 else self.x2
+        self._kernels = [k]
+        return self._kernels
 
     # Bytes of the next operand each kernel pulls into L2 once its own loads
     # are issued (an L2 of 126 MB holds these comfortably).

@@ -55,6 +55,29 @@ def bf16_ulp(x):
     return 2.0 ** (np.floor(np.log2(ax)) - 7)
 
 
+def f16_ulp(x):
+    """Spacing of f16 numbers at |x| (11 significant bits, normal range)."""
+    ax = np.maximum(np.abs(x).astype(np.float64), 2.0 ** -14)
+    return 2.0 ** (np.floor(np.log2(ax)) - 10)
+
+
+def assert_chain_close(g, e, dt, what="", ulps=8, rel=5e-3):
+    """End-to-end bound for a chain of 10+ rounding points (a whole decode
+    layer or stack): relative L2 below `rel`, and pointwise within the
+    per-kernel tolerance or `ulps` ulps of the dtype at the output's RMS
+    scale (outputs near zero come from h + d with |h|, |d| ~ 1). One
+    intermediate that rounds one ulp apart moves later values by several
+    ulps, so a chain cannot meet the per-kernel bound everywhere."""
+    g = np.asarray(g, np.float64)
+    e = np.asarray(e, np.float64)
+    r = np.linalg.norm(g - e) / max(np.linalg.norm(e), 1e-30)
+    assert r < rel, (what, r)
+    scale = np.maximum(np.abs(e), np.sqrt(np.mean(e ** 2)))
+    ulp = bf16_ulp(scale) if dt == "bf16" else f16_ulp(scale)
+    bad = np.abs(g - e) > np.maximum(ATOL + RTOL * np.abs(e), ulps * ulp)
+    assert not bad.any(), "%s: %d/%d outside the chain bound" % (what, int(bad.sum()), bad.size)
+
+
 def assert_close(got, exp, dt, atol=ATOL, rtol=RTOL, what="", bf16_ulps=1):
     """north_star tolerance: within atol + rtol*|exp|. For bf16 outputs a
     difference of one bf16 ulp is also accepted: the tolerance is finer than
