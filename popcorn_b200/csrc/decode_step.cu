@@ -28,13 +28,15 @@
 //
 // Ops are ordered by per-op arrival counters in global memory (release: a
 // CTA barrier, then one thread's threadfence + atomicAdd; acquire:
-// ld.acquire, plus fence.proxy.async before bulk copies read data other SMs
-// wrote). Only the attention tile holding the new K/V row waits for op0;
-// weights never wait. The split-KV combine (op2) is done by the last CTA to
-// finish a KV head's splits (a per-head arrival counter), inside op1.
+// ld.acquire). No copy ever waits: the attention tile holding the new K/V row
+// is copied early too, and its consumers patch that one row from global
+// memory after op0's counter is complete. The split-KV combine (op2) runs
+// inside op1: the splits of a KV head (never more attention items than
+// CTAs, so all run at once) count in on a per-head counter, wait for each
+// other, and each combines a 1/splits slice of the head's outputs.
 //
-// Measured on B200 (config 2, 26 layers, ctx 4096): the same 1.45 ms per
-// token as the five-kernel graph. Streaming phases reach 5.4-6.9 TB/s; what
+// Measured on B200 (config 2, 26 layers, ctx 4096): 1.415 ms per token
+// against 1.437 ms for the five-kernel graph. Streaming phases reach 5.4-6.9 TB/s; what
 // remains is latency at each op boundary (the activation row's loads queue
 // behind the SM's in-flight weight copies) and in the attention phase.
 //
@@ -98,10 +100,6 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() {
-    asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // Bounded spin until *c >= target; false on give-up.
@@ -227,7 +225,8 @@ struct StageCursor {
         next_op();
     }
     // Source, size and group of the current stage; `needs_op0` when it holds
-    // the K/V row that op0 of this layer writes.
+    // the K/V row that op0 of this layer writes (the copy is then stale in
+    // that row and the consumers patch it).
     __device__ const char* src(uint32_t& bytes, int& group, bool& needs_op0) const {
         group = rot % kGroups;
         if (k == 1) {
@@ -256,7 +255,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
     __shared__ float red[kCW];
     __shared__ float gpart[2][kGroups][kGW * 2];  // per-warp row segment sums
     __shared__ volatile int s_abort;
-    __shared__ int s_last;
     unsigned char* ring = smem;
     // The activation planes (GEMV ops) and the attention warp states share
     // one area: ops are separated by a barrier of all consumer warps.
@@ -320,7 +318,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
             pc = ic;
             int64_t issued = 0, prefetched = 0;
             const int64_t ahead = p.l2_ahead / kGroups;
-            int waited_layer = -1;
             while (ic.valid && !s_abort) {
                 if (ic.rot % kGroups != g) {
                     ic.advance();
@@ -340,17 +337,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                 }
                 uint32_t bytes;
                 int gg;
-                bool needs_op0;
-                const char* a = ic.src(bytes, gg, needs_op0);
-                if (needs_op0 && waited_layer != ic.l) {
-                    // the tile holding the new key/value row waits for op0
-                    if (!wait_counter(&p.counters[ic.l * kOps + 0], unsigned(grid))) {
-                        s_abort = 1;
-                        break;
-                    }
-                    fence_proxy_async_global();
-                    waited_layer = ic.l;
-                }
+                bool holds_new_row;  // patched by the consumers (see op1)
+                const char* a = ic.src(bytes, gg, holds_new_row);
                 const int b = g * kSlots + fill % kSlots;
                 if (!mbar_wait(smem_u32(&empty[b]), (uint32_t(fill / kSlots) & 1u) ^ 1u, &g_step_error_word)) {
                     s_abort = 1;
@@ -382,7 +370,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         for (int l = 0; l < p.L; ++l) {
             const DecodeLayer& L = p.layers[l];
             for (int k = 0; k < kOps; ++k) {
-                if (k == 2) continue;  // the split combine runs inside op1 (last CTA of each KV head)
+                if (k == 2) continue;  // the split combine runs inside op1
                 // Norm weights depend on nothing: load them before waiting.
                 const bool norm = (k == 0 || k == 4);
                 const float* nw = k == 0 ? L.attn_norm : L.mlp_norm;
@@ -443,8 +431,23 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                             const int64_t j0 = int64_t(t0 + tt) * kTileKeys;
                             const int nk = int(len - j0 < kTileKeys ? len - j0 : kTileKeys);
                             const int kw0 = gw * 8;
-                            const char* ktile = reinterpret_cast<const char*>(ring + sk * kStageMax);
-                            const char* vtile = reinterpret_cast<const char*>(ring + sv * kStageMax);
+                            char* ktile = reinterpret_cast<char*>(ring + sk * kStageMax);
+                            char* vtile = reinterpret_cast<char*>(ring + sv * kStageMax);
+                            if (t0 + tt == ktiles_total - 1) {
+                                // The tile was copied before op0 wrote the new key/value
+                                // row (copies never wait); patch that row from global
+                                // memory now that op0 is complete.
+                                if (gw == 0 && !s_abort) {
+                                    const int64_t row = (int64_t(hkv) * p.Smax + pos) * kHD * 2 + lane * 16;
+                                    const uint4 kv = ldcg16(static_cast<const char*>(L.k_cache) + row);
+                                    const uint4 vv = ldcg16(static_cast<const char*>(L.v_cache) + row);
+                                    *reinterpret_cast<uint4*>(ktile + (pos - j0) * kHD * 2 + lane * 16) = kv;
+                                    *reinterpret_cast<uint4*>(vtile + (pos - j0) * kHD * 2 + lane * 16) = vv;
+                                    // generic writes before the slot's next bulk copy
+                                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                }
+                                named_sync(2 + grp, kGW * 32);
+                            }
                             if (!s_abort && kw0 < nk) {
                                 float vals[8 * G];
 #pragma unroll
@@ -540,6 +543,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                             }
                         }
                         // merge the 16 warp states of the G heads
+                        if (ctid == 0) TRACE(l, 2, 2);
                         float* mm = merge;
                         float* ll = mm + kCW * G;
                         float* oo = ll + kCW * G;
@@ -573,35 +577,56 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                 p.pl[slot] = Ls;
                             }
                         }
-                        // The last split of this KV head to finish combines all of them.
+                        // Every split of this KV head arrives, waits for the others,
+                        // then combines its own slice of the G heads' outputs (one
+                        // load per thread). Items never exceed the grid, so all
+                        // splits of a head run concurrently.
                         named_sync(1, kCW * 32);
-                        if (ctid == 0) {
+                        if (ctid == 0 && !s_abort) {
                             __threadfence();
-                            s_last = atomicAdd(&head_cnt[l * p.Nkv + hkv], 1u) == unsigned(p.splits) - 1;
+                            atomicAdd(&head_cnt[l * p.Nkv + hkv], 1u);
+                            if (!wait_counter(&head_cnt[l * p.Nkv + hkv], unsigned(p.splits))) s_abort = 1;
                         }
                         named_sync(1, kCW * 32);
-                        if (s_last) {
-                            __threadfence();
-                            for (int idx = ctid; idx < G * kHD; idx += kCW * 32) {
-                                const int hq = hq0 + idx / kHD, d = idx % kHD;
-                                const float* pm = p.pm + int64_t(hq) * p.splits;
-                                const float* pl = p.pl + int64_t(hq) * p.splits;
-                                const float* po = p.po + int64_t(hq) * p.splits * kHD + d;
+                        {
+                            if (ctid == 0) TRACE(l, 2, 0);
+                            const int ns = p.splits;
+                            const int nout = G * kHD;
+                            const int slice = (nout + ns - 1) / ns;
+                            const int o0 = split * slice;
+                            const int o1 = o0 + slice < nout ? o0 + slice : nout;
+                            float* sm_m = merge;              // [G][ns]
+                            float* sm_l = sm_m + G * ns;      // [G][ns]
+                            float* sm_v = sm_l + G * ns;      // [slice][ns]
+                            for (int i2 = ctid; i2 < G * ns; i2 += kCW * 32) {
+                                sm_m[i2] = __ldcg(p.pm + int64_t(hq0) * ns + i2);
+                                sm_l[i2] = __ldcg(p.pl + int64_t(hq0) * ns + i2);
+                            }
+                            for (int i2 = ctid; i2 < (o1 - o0) * ns; i2 += kCW * 32) {
+                                const int o = o0 + i2 / ns, s2 = i2 % ns;
+                                const int g = o / kHD, d = o % kHD;
+                                sm_v[i2] = __ldcg(p.po + (int64_t(hq0 + g) * ns + s2) * kHD + d);
+                            }
+                            named_sync(1, kCW * 32);
+                            if (ctid < o1 - o0 && !s_abort) {
+                                const int o = o0 + ctid;
+                                const int g = o / kHD, d = o % kHD;
+                                const float* mg = sm_m + g * ns;
+                                const float* lg = sm_l + g * ns;
+                                const float* vg = sm_v + ctid * ns;
                                 float M = -INFINITY;
-#pragma unroll 8
-                                for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(pm + s));
+                                for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, mg[s2]);
                                 float Ls = 0.f, acc = 0.f;
-#pragma unroll 8
-                                for (int s = 0; s < p.splits; ++s) {
-                                    const float ms = __ldcg(pm + s);
+                                for (int s2 = 0; s2 < ns; ++s2) {
+                                    const float ms = mg[s2];
                                     const float f = (M == -INFINITY || ms == -INFINITY) ? 0.f : exp2f(ms - M);
-                                    Ls += f * __ldcg(pl + s);
-                                    acc = fmaf(f, __ldcg(po + int64_t(s) * kHD), acc);
+                                    Ls += f * lg[s2];
+                                    acc = fmaf(f, vg[s2], acc);
                                 }
                                 const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
-                                Elem<T>::store(p.attn, int64_t(hq) * kHD + d, acc * inv);
+                                Elem<T>::store(p.attn, int64_t(hq0 + g) * kHD + d, acc * inv);
                             }
-                            if (ctid == 0) head_cnt[l * p.Nkv + hkv] = 0u;  // every split has arrived
+                            if (ctid == 0) TRACE(l, 2, 1);
                         }
                         named_sync(1, kCW * 32);
                     }
@@ -761,12 +786,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
         }
     }
     __syncthreads();
-    // The last CTA out resets the op counters for the next launch.
+    // The last CTA out resets the op and head counters for the next launch.
     if (tid == 0 && !s_abort) {
         __threadfence();
         const unsigned int done = atomicAdd(&p.counters[p.L * kOps], 1u);
         if (done == unsigned(grid) - 1) {
-            for (int i = 0; i <= p.L * kOps; ++i) atomicExch(&p.counters[i], 0u);
+            for (int i = 0; i <= p.L * kOps + p.L * p.Nkv; ++i) atomicExch(&p.counters[i], 0u);
             __threadfence();
         }
     }
@@ -774,7 +799,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
 size_t decode_step_smem(const DecodeStep& p) {
     const size_t xs = size_t(p.xs_bytes);
-    const size_t mg = size_t(kCW) * (p.Nq / p.Nkv) * (kHD + 2) * 4;
+    const int G = p.Nq / p.Nkv;
+    size_t mg = size_t(kCW) * G * (kHD + 2) * 4;  // warp states of the merge
+    const size_t cmb = (size_t(2) * G * p.splits + size_t((G * kHD + p.splits - 1) / p.splits + 1) * p.splits) * 4;
+    if (cmb > mg) mg = cmb;
     return size_t(kRing) * kStageMax + (xs > mg ? xs : mg);
 }
 
@@ -810,9 +838,11 @@ bool decode_step_plan(DecodeStep& p, int sm_count) {
     p.l2_ahead = 256 * 1024;
     if (const char* e = getenv("POPCORN_STEP_L2_AHEAD")) p.l2_ahead = atoll(e);
     p.xs_bytes = (kmax * 4 + 127) / 128 * 128;
-    // attention split: about one item per SM
+    // attention split: about one item per SM and never more items than CTAs
+    // (the splits of a head wait for each other)
+    if (p.Nkv > sm_count) return false;
     const int max_tiles = (p.Smax + kTileKeys - 1) / kTileKeys;
-    int splits = (sm_count + p.Nkv - 1) / p.Nkv;
+    int splits = sm_count / p.Nkv;
     if (splits > max_tiles) splits = max_tiles;
     if (splits < 1) splits = 1;
     p.chunk_tiles = (max_tiles + splits - 1) / splits;
