@@ -33,7 +33,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one gemv_tma_kernel
 # <f16,f16,f16,NORM,kGated> launch (one layer's gate/up), from the ncu
 # capture summarised in profiles/gemv_geglu_config2.md.
-GEGLU_NCU_TRAFFIC = 87_321_600
+GEGLU_NCU_TRAFFIC = 87_425_024
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
@@ -47,13 +47,13 @@ def peaks():
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def metric_name():
-    return "Gemma-2-2B-shape decode tok/s (26-layer stack, batch 1, ctx 4096)"
+def metric_name(layers=LAYERS):
+    return "Gemma-2-2B-shape decode tok/s (%d-layer stack, batch 1, ctx 4096)" % layers
 
 
-def config_dict(parallelism):
-    return {"workload": "config2: Gemma-2-2B-shape decode layer x%d, batch 1, KV ctx %d, f16" % (LAYERS, CTX),
-            "layers": LAYERS, "hidden": 2304, "q_heads": 8, "kv_heads": 4, "head_dim": 256, "ffn": 9216,
+def config_dict(parallelism, layers=LAYERS):
+    return {"workload": "config2: Gemma-2-2B-shape decode layer x%d, batch 1, KV ctx %d, f16" % (layers, CTX),
+            "layers": layers, "hidden": 2304, "q_heads": 8, "kv_heads": 4, "head_dim": 256, "ffn": 9216,
             "global_batch": 1, "seq_len": CTX, "activation": "gelu_tanh (GeGLU)",
             "l2": "inputs larger than L2 (weights + KV of the stack stream from HBM every step)",
             "parallelism": parallelism}
@@ -353,6 +353,8 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b"])
     ap.add_argument("--tp-layers", type=int, default=42)
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="config-2 stack depth (26 for the bench line; fewer for small profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -379,9 +381,10 @@ def main():
         if world > 1:
             dist.barrier()
 
+    n_layers = args.layers
     shape = LayerShape(max_ctx=CTX, dtype="f16")
     lib = pc.KernelLibrary(local)
-    stack = DecodeStack(lib, shape, LAYERS, seed=1234 + rank, device=local)
+    stack = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local)
     stream = torch.cuda.Stream(device=local)
     pos = CTX - 1
     hbm_gbs, _, peak_kind = peaks()
@@ -457,7 +460,7 @@ def main():
                     "down_proj_residual_f16": 4}
         kern_us = {}
         for name, idx in role_idx.items():
-            sel = [ks[l * 5 + idx] for l in range(LAYERS)]
+            sel = [ks[l * 5 + idx] for l in range(n_layers)]
             g_role = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g_role, stream=stream):
                 enc.encode(*sel)
@@ -472,8 +475,31 @@ def main():
                 g_role.replay()
             b_ev.record(stream)
             torch.cuda.synchronize()
-            kern_us[name] = a_ev.elapsed_time(b_ev) * 1000.0 / reps / LAYERS
+            kern_us[name] = a_ev.elapsed_time(b_ev) * 1000.0 / reps / n_layers
             del g_role
+
+        # ---- the same step as one persistent kernel (DecodeStack(fused=True)) ----
+        fused = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, fused=True)
+        fused.set_position(pos)
+        fused.x.normal_()
+        fused.kernels()
+        enc_f = fused.encoder(stream)
+        g_f = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_f, stream=stream):
+            fused.encode_step(enc_f)
+        for _ in range(args.warmup):
+            g_f.replay()
+        torch.cuda.synchronize()
+        f_start = torch.cuda.Event(enable_timing=True)
+        f_end = torch.cuda.Event(enable_timing=True)
+        f_start.record(stream)
+        for _ in range(args.steps):
+            g_f.replay()
+        f_end.record(stream)
+        torch.cuda.synchronize()
+        fused_ms = f_start.elapsed_time(f_end) / args.steps
+        fused_err = pc.device_error_check(local)
+        del g_f, fused
 
     # max over ranks of the timed step
     if world > 1:
@@ -502,11 +528,11 @@ def main():
     e2e_tok_s = world * 1000.0 / e2e_ms
     bytes_step = stack.algorithmic_bytes_per_step(CTX)
     line = {
-        "metric": metric_name(), "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric_name(n_layers), "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV cache and input)",
-        "config": config_dict("replicas" if world > 1 else "single GPU"),
+        "config": config_dict("replicas" if world > 1 else "single GPU", n_layers),
         "step_hbm_gbs": bytes_step / (ms * 1e-3) / 1e9,
         "step_frac_of_measured_hbm": bytes_step / (ms * 1e-3) / 1e9 / hbm_gbs,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": dom_gbs, "peak": hbm_gbs, "unit": "GB/s",
@@ -517,6 +543,9 @@ def main():
         "flash_decode": {"kernel": "flash_decoding_f16 (partial + combine)", "achieved_gbs": fd["gbs"],
                          "frac_of_measured_hbm": fd["frac_of_measured_hbm"], "bytes_per_launch": fd["bytes"]},
         "kernels": kernels,
+        "fused_step": {"kernel": "decode_step_f16 (one persistent launch per token, all 26 layers)",
+                       "ms_per_step": fused_ms, "tok_s": 1000.0 / fused_ms,
+                       "step_hbm_gbs": bytes_step / (fused_ms * 1e-3) / 1e9, "device_error_word": fused_err},
         "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": H * 2 + 8, "d2h_bytes_per_step": H * 2,
                 "path": "pc_memcpy_htod_async (pinned host) -> graph of C-ABI kernels -> pc_memcpy_dtoh_async"},
         "gpu_launches": launches_per_step * args.steps,
@@ -525,9 +554,9 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         t_layer, cores, reps = time_cpu_layer()
-        line["cpu_baseline"] = {"value": 1.0 / (t_layer * LAYERS), "unit": "tok/s", "cores": cores, "kind": "port",
+        line["cpu_baseline"] = {"value": 1.0 / (t_layer * n_layers), "unit": "tok/s", "cores": cores, "kind": "port",
                                 "sample": "%d run(s) of one layer (ctx %d) of the oracle on the host, median; "
-                                          "tok/s = 1 / (%d x layer time)" % (reps, CTX, LAYERS)}
+                                          "tok/s = 1 / (%d x layer time)" % (reps, CTX, n_layers)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
