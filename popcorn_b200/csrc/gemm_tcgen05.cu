@@ -2,7 +2,8 @@
 // cores: tcgen05.mma with TMEM accumulators, TMA-fed shared memory).
 //
 // Semantics: C[m,n] = sum_k A[m,k] * B[n,k] (transposeB, the linear-layer
-// layout) with fp32 accumulation and one rounding at the store — the
+// layout) or sum_k A[m,k] * B[k,n] (B not transposed: MN-major tiles), with
+// fp32 accumulation and one rounding at the store — the
 // product Matmul.metal:7-27 / MPPMatmul.metal:20-63 compute. A and B are
 // both bf16 or both f16; C is f32 or the input type.
 //
@@ -128,11 +129,26 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, A/B type, K-major
-// A and B, N and M sizes.
-__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int M, int N) {
+// MN-major operand tile (B stored [K, N], N contiguous) written by TMA in
+// boxes of 64 MN-elements (one 128-byte swizzle row) x 64 K-rows: 8-K-row
+// groups 1024 B apart (stride byte offset), 64-element MN blocks
+// `mn_block_bytes` apart (leading byte offset).
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr, uint32_t mn_block_bytes) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3FFF);
+    d |= uint64_t((mn_block_bytes >> 4) & 0x3FFF) << 16;
+    d |= uint64_t(1024 >> 4) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B type, A K-major,
+// B K-major or MN-major (bit 16), N and M sizes.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int M, int N, bool b_mn = false) {
     return (1u << 4)                                    // D: f32
            | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B: bf16 or f16
+           | ((b_mn ? 1u : 0u) << 16)                   // B major-ness
            | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
@@ -143,6 +159,7 @@ struct GemmArgs {
     int64_t ldc;          // row stride of C in elements
     int swap;             // 1: MMA rows are C columns (C^T = B A^T)
     int tma_store;        // 1: C tiles leave through map_c
+    int b_mn;             // 1: B is [K, N] (not transposed): MN-major tiles
 };
 
 // Persistent form: one CTA per SM walks output tiles t = blockIdx.x,
@@ -215,14 +232,21 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                     mbar_expect_tx(bar, STAGE);
                     unsigned char* st = smem + size_t(s) * STAGE;
                     tma_load_2d(smem_u32(st), &map_a, kt * kBK, m0, bar);
-                    tma_load_2d(smem_u32(st + A_BYTES), &map_b, kt * kBK, n0, bar);
+                    if (g.b_mn) {
+                        // BN / 64 boxes of 64 N-columns x 64 K-rows
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(smem_u32(st + A_BYTES + j * (kBK * 128)), &map_b, n0 + j * 64, kt * kBK, bar);
+                    } else {
+                        tma_load_2d(smem_u32(st + A_BYTES), &map_b, kt * kBK, n0, bar);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer ----
-            const uint32_t idesc = g.in_f16 ? make_idesc(false, kBM, BN) : make_idesc(true, kBM, BN);
+            const uint32_t idesc = make_idesc(!g.in_f16, kBM, BN, g.b_mn != 0);
             int it = 0, lt = 0;
             for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, ++lt) {
                 const int acc = lt & 1;
@@ -243,9 +267,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                     const uint32_t a_base = smem_u32(smem + size_t(s) * STAGE);
                     const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk)
-                        tc_mma(d, smem_desc_sw128(a_base + kk * 32), smem_desc_sw128(b_base + kk * 32), idesc,
-                               (kt > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        // K-major: the next 16 K-elements are 32 B further along the
+                        // swizzled row; MN-major: 16 K-rows (2048 B) further
+                        const uint64_t bd = g.b_mn ? smem_desc_sw128_mn(b_base + kk * 2048, kBK * 128)
+                                                   : smem_desc_sw128(b_base + kk * 32);
+                        tc_mma(d, smem_desc_sw128(a_base + kk * 32), bd, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+                    }
                     tc_commit(smem_u32(&empty[s]));
                 }
                 tc_commit(smem_u32(&tfull[acc]));
@@ -370,6 +398,21 @@ bool make_map(CUtensorMap* map, const void* base, int dtype, int64_t rows, int64
     return r == CUDA_SUCCESS;
 }
 
+// 2-D MN-major tensor map over a [K, N] matrix (16-bit), box = 64 N x 64 K.
+bool make_map_mn(CUtensorMap* map, const void* base, int dtype, int64_t K, int64_t N) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(K)};
+    cuuint64_t strides[1] = {cuuint64_t(N) * 2};
+    cuuint32_t box[2] = {64, cuuint32_t(kBK)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype == PC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 template <int BN, class CT>
 cudaError_t launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& g,
                       cudaStream_t s) {
@@ -402,13 +445,15 @@ cudaError_t launch_ct(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
 
 }  // namespace
 
-// Served: transposeB, A and B both bf16 or both f16, C f32 or the same type,
-// K a multiple of 8 (16-byte row pitch for TMA), 16-byte aligned bases, and
-// a problem big enough to use the tensor cores (M >= 16).
+// Served: A and B both bf16 or both f16, C f32 or the same type, K a
+// multiple of 8 (16-byte row pitch for TMA), 16-byte aligned bases, and a
+// problem big enough to use the tensor cores (M >= 16). transposeB (B
+// [N, K]) at any such M; B [K, N] when M > 64 (unswapped) and N % 8 == 0.
 bool tcgen05_supports(const Matmul& p) {
     bool types = (p.a_dtype == PC_BF16 || p.a_dtype == PC_F16) && p.b_dtype == p.a_dtype &&
                  (p.c_dtype == PC_F32 || p.c_dtype == p.a_dtype);
-    return types && p.transpose_b && p.M >= 16 && p.N >= 16 && p.K >= 16 && p.K % 8 == 0 && aligned16(p.a) &&
+    bool layout = p.transpose_b || (p.M > 64 && p.N % 8 == 0 && p.N >= 64);
+    return types && layout && p.M >= 16 && p.N >= 16 && p.K >= 16 && p.K % 8 == 0 && aligned16(p.a) &&
            aligned16(p.b) && p.M < (int64_t(1) << 31) && p.N < (int64_t(1) << 31) && encode_fn() != nullptr;
 }
 
@@ -426,9 +471,10 @@ cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
     g.M = swap ? p.N : p.M;
     g.N = swap ? p.M : p.N;
     int bn = swap ? (g.N <= 32 ? 32 : 64) : (g.N >= 256 ? 256 : 128);
+    g.b_mn = p.transpose_b ? 0 : 1;  // supports() keeps B [K, N] unswapped
     CUtensorMap ma, mb, mc;
-    if (!make_map(&ma, a, p.a_dtype, g.M, p.K, kBM) || !make_map(&mb, b, p.a_dtype, g.N, p.K, bn))
-        return cudaErrorInvalidValue;
+    const bool mb_ok = g.b_mn ? make_map_mn(&mb, b, p.a_dtype, p.K, g.N) : make_map(&mb, b, p.a_dtype, g.N, p.K, bn);
+    if (!make_map(&ma, a, p.a_dtype, g.M, p.K, kBM) || !mb_ok) return cudaErrorInvalidValue;
     const int ces = p.c_dtype == PC_F32 ? 4 : 2;
     g.tma_store = (!swap && (p.N * ces) % 16 == 0 && aligned16(p.c) && make_out_map(&mc, p.c, p.c_dtype, p.M, p.N))
                       ? 1 : 0;
@@ -456,6 +502,7 @@ RegisterFunctions reg_gemm({
     {"matmul_tc_bf16_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TBF16>)},
     {"matmul_tc_f32out_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TF32>)},
     {"matmul_tc_f16_tb", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TF16>)},
+    {"matmul_tc_bf16_nn", reinterpret_cast<const void*>(gemm_tcgen05_kernel<256, TBF16>)},
 });
 }  // namespace
 

@@ -295,7 +295,9 @@ public:
                                                                dtype_name(ad) + ", " + dtype_name(bd) + ", " +
                                                                dtype_name(cd) + ".");
         launch::Matmul p = params();
-        function_names_ = launch::matmul_uses_tensor_cores(p) ? "matmul_tc_bf16_tb" : "matmul";
+        function_names_ = !launch::matmul_uses_tensor_cores(p) ? "matmul"
+                          : p.transpose_b                       ? "matmul_tc_bf16_tb"
+                                                                : "matmul_tc_bf16_nn";
     }
     launch::Matmul params() const {
         return launch::Matmul{a_.data(), a_.dtype(), b_.data(), b_.dtype(), c_.data(), c_.dtype(), m_, k_, n_, tb_ ? 1 : 0};

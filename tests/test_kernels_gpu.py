@@ -461,6 +461,22 @@ def test_matmul_tcgen05(pc, enc, M, K, N, dt, odt):
     assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul %dx%dx%d" % (M, K, N))
 
 
+@pytest.mark.parametrize("M,K,N,dt,odt", [(128, 64, 256, "bf16", "f32"), (256, 2304, 512, "bf16", "bf16"),
+                                          (300, 520, 200, "f16", "f32"), (1000, 1024, 1000, "bf16", "f32"),
+                                          (130, 72, 64, "f16", "f16")])
+def test_matmul_tcgen05_b_not_transposed(pc, enc, M, K, N, dt, odt):
+    """C = A . B with B stored [K, N]: MN-major B tiles on the tensor cores."""
+    rng = np.random.default_rng(M * 3 + K + N)
+    a = rand(rng, (M, K), dt)
+    b = rand(rng, (K, N), dt, 0.05)
+    out = empty_dev((M, N), odt)
+    kern = pc.Kernels.Matmul(to_dev(a, dt), to_dev(b, dt), into=out, transpose_b=False)
+    assert kern.function_names == ["matmul_tc_bf16_nn"]
+    run(enc, kern)
+    exp = oracle.matmul(a, dt, b, dt, odt, False)
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul (B [K,N]) %dx%dx%d" % (M, K, N))
+
+
 def test_matmul_tcgen05_config4_rows(pc, enc):
     """BASELINE config 4 GEMM (8192 x 2304 x 9216, bf16, transposeB): the full
     product on the GPU, 24 sampled rows checked against the oracle."""
