@@ -254,6 +254,63 @@ def run_fd_sweep(args):
     return 0
 
 
+def run_prefill(args):
+    """Config 4: the prefill GEMM (M 8192 x K 2304 x N 9216, bf16, transposeB,
+    2*M*N*K = 347.9 GFLOP) and causal FlashAttention (B 4, 8 Q / 4 KV heads,
+    S 2048, hd 256, bf16: 4*B*Nq*(S(S+1)/2)*hd = 68.75 GFLOP), each on the
+    tcgen05 tensor cores, CUDA events over graph replays after warm-up.
+    Operands (GEMM 370 MB in+out) exceed L2."""
+    import torch
+    import popcorn_b200 as pc
+    torch.cuda.set_device(0)
+    _, tf_peak, peak_kind = peaks()
+    lib = pc.KernelLibrary(0)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    M, K, N = 8192, 2304, 9216
+    a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    B, Nq, Nkv, S, Hd = 4, 8, 4, 2048, 256
+    q = torch.randn(B, Nq, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Nkv, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Nkv, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    gemm = pc.Kernels.Matmul(a, w, into=c, transpose_b=True)
+    fa = pc.Kernels.FlashAttention(q, k, v, into=o, scale=1.0 / 16, mask=pc.AttentionMask.causal)
+    stream = torch.cuda.Stream()
+    res = {}
+    with torch.cuda.stream(stream):
+        enc = pc.KernelCommandEncoder(lib, stream=stream)
+        for name, kern, flops in (("gemm", gemm, 2.0 * M * N * K),
+                                  ("flash_attention", fa, 4.0 * B * Nq * (S * (S + 1) / 2) * Hd)):
+            enc.encode(kern)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                enc.encode(kern)
+            for _ in range(max(args.warmup, 3)):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = max(args.steps, 5)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000.0 / reps
+            tf = flops / (us * 1e-6) / 1e12
+            res[name] = {"kernel": kern.function_names[0], "us": round(us, 2), "gflop": round(flops / 1e9, 2),
+                         "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / tf_peak, 3)}
+    line = {"metric": "prefill TFLOP/s (config 4)", "unit": "TFLOP/s", "peak": tf_peak, "peak_kind": peak_kind,
+            "dtype": "bf16", "data": "synthetic seeded N(0,1) activations / q,k,v, N(0,0.02) weights",
+            "config": {"workload": "config4: GEMM 8192x2304x9216 tb; causal FA B4 8Q/4KV S2048 hd256"},
+            "kernels": res, "device_error_word": pc.device_error_check(0)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------------------
 # Tensor-parallel 9B-shape batched decode (BASELINE config 5)
 # ---------------------------------------------------------------------------
@@ -351,7 +408,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
-    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b"])
+    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill"])
     ap.add_argument("--tp-layers", type=int, default=42)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="config-2 stack depth (26 for the bench line; fewer for small profiling captures)")
@@ -363,6 +420,8 @@ def main():
         return run_fd_sweep(args)
     if args.workload == "tp9b":
         return run_tp(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
 
     import torch
     import torch.distributed as dist

@@ -1,0 +1,439 @@
+// fa_tcgen05.cu — prefill FlashAttention on the 5th-generation tensor cores
+// (sm_100a): S = Q.K^T and O += P.V as tcgen05.mma with fp32 accumulators in
+// tensor memory, Q/K/V tiles by TMA (128-byte swizzle, no multicast).
+//
+// Semantics (FlashAttention.metal:31-162; MPPFlashAttention.metal:39-244):
+// query row q of (b, hq) sits at posQ = Sk - Sq + q and attends to the keys
+// its mask allows (causal j <= posQ; sliding window also posQ - j < window;
+// bidirectional all); KV head hkv = hq * Nkv / Nq; online softmax in fp32
+// (natural exp, evaluated as exp2 of log2e-scaled scores); O / l stored once.
+// The scale multiplies the fp32 scores (the reference scales q first: the
+// same product up to fp32 rounding). P enters the second product in the
+// input type: f16 directly (11 significant bits), bf16 as a hi + lo pair
+// (P = hi + lo, two MMAs, ~16 significant bits), so the output keeps the
+// fp32-accumulation tolerance of the reference semantics.
+//
+// One CTA per (128-query tile, query head, batch), heaviest causal tiles
+// first. Warp 0 lane 0 loads Q once and then the K and V tile of every
+// 64-key step; warp 1 lane 0 issues the MMAs: S(j+1) = Q.K(j+1)^T into the
+// other of two S accumulators while the softmax warps work on S(j), then
+// O += P(j).V(j). Warps 2-5 own one query row per thread (TMEM lane): they
+// read S, mask, keep the running max and sum, write P to shared memory in
+// the MMA's swizzled K-major layout, and rescale O in tensor memory only
+// when the running max grows by more than 2^8 (P stays <= 256; the final
+// O / l is exact for any max used consistently). TMEM: S0, S1 (64 columns
+// each) and O (Hd columns) in one 512-column allocation.
+//
+// Every mbarrier wait is bounded; on give-up the CTA sets the error word,
+// skips its remaining work, frees its tensor memory and leaves.
+#include "async.cuh"
+#include "common.cuh"
+#include "dtype.cuh"
+#include "launch.hpp"
+#include "popcorn.hpp"
+#include "tcgen05.cuh"
+
+namespace popcorn {
+
+__device__ unsigned int g_fa_error_word;
+
+namespace launch {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kBMq = 128;               // query rows per CTA (MMA M)
+constexpr int kBNk = 64;                // keys per step (one 128-byte swizzle atom of P)
+constexpr int kFaThreads = 6 * 32;      // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;    // rescale O when the max grows by more than this (log2 units)
+constexpr uint32_t kTmemCols = 512;
+
+struct FaArgs {
+    void* out;
+    int64_t Sq, Sk;
+    int B, Nq, Nkv;
+    float c;          // scale * log2(e)
+    int mask_kind;    // 0 causal, 1 sliding window, 2 bidirectional
+    int window;
+    int n_qtiles;
+};
+
+// Warp-uniform bounded wait: lane 0 waits, the warp learns the outcome.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int lane) {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(bar, parity, &g_fa_error_word) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+template <int HD, class IT, class OT>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    fa_tcgen05_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v, const FaArgs a) {
+    constexpr int ATOMS = HD / 64;                    // 128-byte swizzle atoms along the head dim
+    constexpr int Q_BYTES = kBMq * HD * 2;            // ATOMS blocks of 128 rows x 128 B
+    constexpr int KV_BYTES = kBNk * HD * 2;
+    constexpr int Q_BLOCK = kBMq * 128, KV_BLOCK = kBNk * 128, P_BLOCK = kBMq * 128;
+    constexpr uint32_t S_COLS = kBNk;
+    constexpr uint32_t O_COL = 2 * S_COLS;
+    constexpr bool BF = IT::code == TBF16::code;
+    constexpr int NP = BF ? 2 : 1;  // P parts: bf16 hi + lo, or one f16
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t q_full, k_full, k_empty, v_full, v_empty, s_full[2], s_free[2], p_full, o_done;
+    __shared__ uint32_t s_tmem;
+    __shared__ volatile int s_abort;
+
+    pdl_launch_dependents();
+    unsigned char* sq =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sk = sq + Q_BYTES;
+    unsigned char* sv = sk + KV_BYTES;
+    unsigned char* sp = sv + KV_BYTES;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // This CTA's query tile (heaviest causal tiles first), head and batch.
+    const int qt = a.n_qtiles - 1 - int(blockIdx.x);
+    const int hq = int(blockIdx.y), b = int(blockIdx.z);
+    const int hkv = int(int64_t(hq) * a.Nkv / a.Nq);
+    const int64_t q0 = int64_t(qt) * kBMq;
+    const int64_t qlast = (q0 + kBMq < a.Sq ? q0 + kBMq : a.Sq) - 1;
+    // Key tiles [t_lo, t_lo + nt) that hold an allowed key for some row.
+    const int64_t nkt_all = (a.Sk + kBNk - 1) / kBNk;
+    int64_t t_lo = 0, t_hi = nkt_all;
+    if (a.mask_kind != 2) {
+        const int64_t kmax = a.Sk - a.Sq + qlast;
+        t_hi = kmax < 0 ? 0 : (kmax / kBNk + 1 < nkt_all ? kmax / kBNk + 1 : nkt_all);
+    }
+    if (a.mask_kind == 1) {
+        const int64_t kmin = a.Sk - a.Sq + q0 - a.window + 1;
+        if (kmin > 0) t_lo = kmin / kBNk;
+    }
+    const int nt = t_hi > t_lo ? int(t_hi - t_lo) : 0;
+
+    if (tid == 0) {
+        mbar_init(smem_u32(&q_full), 1);
+        mbar_init(smem_u32(&k_full), 1);
+        mbar_init(smem_u32(&k_empty), 1);
+        mbar_init(smem_u32(&v_full), 1);
+        mbar_init(smem_u32(&v_empty), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&s_full[i]), 1);
+            mbar_init(smem_u32(&s_free[i]), 4);
+        }
+        mbar_init(smem_u32(&p_full), 4);
+        mbar_init(smem_u32(&o_done), 1);
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(&s_tmem), kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0 && nt > 0) {
+            // ---- TMA loads ----
+            const int zq = b * a.Nq + hq, zkv = b * a.Nkv + hkv;
+            mbar_expect_tx(smem_u32(&q_full), Q_BYTES);
+#pragma unroll
+            for (int at = 0; at < ATOMS; ++at)
+                tma_load_3d(smem_u32(sq + at * Q_BLOCK), &map_q, at * 64, int(q0), zq, smem_u32(&q_full));
+            int kf = 0, vf = 0;  // K and V tiles issued
+            for (int j = 0; j < nt && !s_abort; ++j) {
+                const int key0 = int((t_lo + j) * kBNk);
+                const uint32_t ph = (uint32_t(j) & 1u) ^ 1u;
+                if (!mbar_wait(smem_u32(&k_empty), ph, &g_fa_error_word)) {
+                    s_abort = 1;
+                    break;
+                }
+                mbar_expect_tx(smem_u32(&k_full), KV_BYTES);
+#pragma unroll
+                for (int at = 0; at < ATOMS; ++at)
+                    tma_load_3d(smem_u32(sk + at * KV_BLOCK), &map_k, at * 64, key0, zkv, smem_u32(&k_full));
+                ++kf;
+                if (!mbar_wait(smem_u32(&v_empty), ph, &g_fa_error_word)) {
+                    s_abort = 1;
+                    break;
+                }
+                mbar_expect_tx(smem_u32(&v_full), KV_BYTES);
+#pragma unroll
+                for (int at = 0; at < ATOMS; ++at)
+                    tma_load_3d(smem_u32(sv + at * KV_BLOCK), &map_v, at * 64, key0, zkv, smem_u32(&v_full));
+                ++vf;
+            }
+            if (s_abort) {
+                // leave no copy in flight: wait (bounded) for the last ones issued
+                mbar_wait(smem_u32(&q_full), 0u, &g_fa_error_word);
+                if (kf > 0) mbar_wait(smem_u32(&k_full), uint32_t(kf - 1) & 1u, &g_fa_error_word);
+                if (vf > 0) mbar_wait(smem_u32(&v_full), uint32_t(vf - 1) & 1u, &g_fa_error_word);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && nt > 0) {
+            // ---- MMA issue ----
+            const uint32_t idesc_s = make_idesc(BF, kBMq, kBNk, false);
+            const uint32_t idesc_o = make_idesc(BF, kBMq, HD, true);
+            const uint32_t q_base = smem_u32(sq), k_base = smem_u32(sk), v_base = smem_u32(sv), p_base = smem_u32(sp);
+            bool ok = mbar_wait(smem_u32(&q_full), 0u, &g_fa_error_word);
+            auto issue_s = [&](int j) {
+                const int buf = j & 1;
+                if (!ok || s_abort) return;
+                ok = mbar_wait(smem_u32(&s_free[buf]), (uint32_t(j >> 1) & 1u) ^ 1u, &g_fa_error_word) &&
+                     mbar_wait(smem_u32(&k_full), uint32_t(j) & 1u, &g_fa_error_word);
+                if (!ok) return;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    tc_mma(tmem + uint32_t(buf) * S_COLS, smem_desc_sw128(q_base + (kk >> 2) * Q_BLOCK + (kk & 3) * 32),
+                           smem_desc_sw128(k_base + (kk >> 2) * KV_BLOCK + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
+                tc_commit(smem_u32(&k_empty));
+                tc_commit(smem_u32(&s_full[buf]));
+            };
+            issue_s(0);
+            for (int j = 0; j < nt && ok && !s_abort; ++j) {
+                if (j + 1 < nt) issue_s(j + 1);
+                if (!ok) break;
+                ok = mbar_wait(smem_u32(&p_full), uint32_t(j) & 1u, &g_fa_error_word) &&
+                     mbar_wait(smem_u32(&v_full), uint32_t(j) & 1u, &g_fa_error_word);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int part = 0; part < NP; ++part)
+#pragma unroll
+                    for (int kk = 0; kk < kBNk / 16; ++kk)
+                        tc_mma(tmem + O_COL, smem_desc_sw128(p_base + part * P_BLOCK + kk * 32),
+                               smem_desc_sw128_mn(v_base + kk * 2048, KV_BLOCK), idesc_o,
+                               (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(smem_u32(&v_empty));
+                tc_commit(smem_u32(&o_done));
+            }
+            if (!ok) s_abort = 1;
+        }
+    } else {
+        // ---- softmax: one query row per thread ----
+        const int quarter = warp & 3;               // TMEM lanes this warp may access
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+        const int64_t qi = q0 + row;
+        const int64_t posQ = a.Sk - a.Sq + qi;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt && ok; ++j) {
+            const int buf = j & 1;
+            ok = warp_wait(smem_u32(&s_full[buf]), uint32_t(j >> 1) & 1u, lane) && !s_abort;
+            if (!ok) break;
+            tc_fence_after();
+            float s[kBNk];
+#pragma unroll
+            for (int c = 0; c < kBNk / 32; ++c) tmem_ld32(tmem + uint32_t(buf) * S_COLS + uint32_t(c * 32) + lane_off, s + c * 32);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&s_free[buf]));
+            const int64_t key0 = (t_lo + j) * kBNk;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBNk; ++c) {
+                const int64_t key = key0 + c;
+                const bool allowed = key < a.Sk && (a.mask_kind == 2 || (key <= posQ && (a.mask_kind != 1 || posQ - key < a.window)));
+                s[c] = allowed ? s[c] * a.c : -INFINITY;
+                mx = fmaxf(mx, s[c]);
+            }
+            // lazy rescale: keep the old max unless the new one exceeds it by 2^8
+            const float m_new = fmaxf(m_used, mx);
+            float factor = 1.f;
+            if (m_new > m_used + kRescaleLog2) {  // also when m_used is -inf and the tile has a key
+                factor = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                m_used = m_new;
+                l *= factor;
+            }
+            float lsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < kBNk; ++c) {
+                s[c] = m_used == -INFINITY ? 0.f : exp2f(s[c] - m_used);
+                lsum += s[c];
+            }
+            l += lsum;
+            // P's buffer is free and O is settled once PV(j-1) has completed.
+            if (j > 0) {
+                ok = warp_wait(smem_u32(&o_done), uint32_t(j - 1) & 1u, lane) && !s_abort;
+                if (!ok) break;
+                tc_fence_after();
+                // O rows that were accumulated under the old max (factor 0: O
+                // is zero there, nothing to do)
+                if (__any_sync(0xffffffffu, factor != 1.f && factor != 0.f)) {
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(tmem + O_COL + uint32_t(c * 32) + lane_off, o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] *= (factor == 0.f ? 1.f : factor);
+                        tmem_st32(tmem + O_COL + uint32_t(c * 32) + lane_off, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // P row -> shared memory, K-major with 128-byte swizzle (A operand);
+            // bf16: the hi part, then lo = p - hi in the second block
+#pragma unroll
+            for (int part = 0; part < NP; ++part) {
+#pragma unroll
+                for (int c8 = 0; c8 < kBNk / 8; ++c8) {
+                    float e[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float pv = s[c8 * 8 + i];
+                        e[i] = part == 0 ? pv : pv - Elem<IT>::round(pv);
+                    }
+                    const uint4 w = make_uint4(pack2<IT>(e[0], e[1]), pack2<IT>(e[2], e[3]), pack2<IT>(e[4], e[5]),
+                                               pack2<IT>(e[6], e[7]));
+                    *reinterpret_cast<uint4*>(sp + part * P_BLOCK + row * 128 + ((c8 ^ (row & 7)) << 4)) = w;
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&p_full));
+        }
+        if (nt > 0 && ok) {
+            ok = warp_wait(smem_u32(&o_done), uint32_t(nt - 1) & 1u, lane) && !s_abort;
+            tc_fence_after();
+        }
+        if (!ok) s_abort = 1;
+        // ---- O / l -> out ----
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        const bool valid = qi < a.Sq;
+        const int64_t obase = ((int64_t(b) * a.Nq + hq) * a.Sq + qi) * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            if (nt > 0 && ok) {
+                tmem_ld32(tmem + O_COL + uint32_t(c * 32) + lane_off, o);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[e] = 0.f;
+            }
+            if (valid) {
+                if constexpr (Elem<OT>::bytes == 4) {
+                    float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + c * 32);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        d4[e] = make_float4(o[4 * e] * inv, o[4 * e + 1] * inv, o[4 * e + 2] * inv, o[4 * e + 3] * inv);
+                } else {
+                    uint4* d4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + obase + c * 32);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        d4[e] = make_uint4(pack2<OT>(o[8 * e] * inv, o[8 * e + 1] * inv),
+                                           pack2<OT>(o[8 * e + 2] * inv, o[8 * e + 3] * inv),
+                                           pack2<OT>(o[8 * e + 4] * inv, o[8 * e + 5] * inv),
+                                           pack2<OT>(o[8 * e + 6] * inv, o[8 * e + 7] * inv));
+                }
+            }
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// 3-D map [heads*batch, S, HD] (16-bit), box = 64 x rows x 1, 128-byte swizzle.
+bool make_map_3d(CUtensorMap* map, const void* base, int dtype, int64_t S, int64_t HD, int64_t planes, int rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {cuuint64_t(HD), cuuint64_t(S), cuuint64_t(planes)};
+    cuuint64_t strides[2] = {cuuint64_t(HD) * 2, cuuint64_t(S) * HD * 2};
+    cuuint32_t box[3] = {64, cuuint32_t(rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dtype == PC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int HD>
+constexpr size_t fa_smem() {
+    return size_t(kBMq) * HD * 2 + 2 * size_t(kBNk) * HD * 2 + 2 * size_t(kBMq) * kBNk * 2 + 1024;
+}
+
+template <int HD, class IT, class OT>
+cudaError_t run_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaArgs& fa, cudaStream_t s) {
+    auto kern = fa_tcgen05_kernel<HD, IT, OT>;
+    constexpr size_t smem = fa_smem<HD>();
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = allow_smem(kern, smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    dim3 grid(unsigned(fa.n_qtiles), unsigned(fa.Nq), unsigned(fa.B));
+    return launch_k(kern, grid, dim3(kFaThreads), smem, s, mq, mk, mv, fa);
+}
+
+template <int HD, class IT>
+cudaError_t run_fa_o(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FaArgs& fa,
+                     int out_dtype, cudaStream_t s) {
+    if (out_dtype == PC_F32) return run_fa<HD, IT, TF32>(mq, mk, mv, fa, s);
+    return run_fa<HD, IT, IT>(mq, mk, mv, fa, s);
+}
+
+}  // namespace
+
+// Served: q, k, v all bf16 or all f16; out f32 or the input type; head dim
+// 128 or 256; 16-byte aligned bases; grid dimensions in range; Sq >= 32
+// (shorter queries stay on the plain kernel, as FlashAttention.route does).
+bool fa_tcgen05_supports(const FlashAttention& p) {
+    const bool types = (p.q_dtype == PC_BF16 || p.q_dtype == PC_F16) && p.kv_dtype == p.q_dtype &&
+                       (p.out_dtype == PC_F32 || p.out_dtype == p.q_dtype);
+    return types && (p.Hd == 128 || p.Hd == 256) && p.Sq >= 32 && p.Sk >= 1 && aligned16(p.q) && aligned16(p.k) &&
+           aligned16(p.v) && aligned16(p.out) && p.Nq <= 65535 && p.B <= 65535 &&
+           (p.Sq + kBMq - 1) / kBMq < (int64_t(1) << 31) && p.Sk < (int64_t(1) << 31) && p.Sq < (int64_t(1) << 31) &&
+           encode_fn() != nullptr;
+}
+
+cudaError_t flash_attention_tcgen05(const FlashAttention& p, cudaStream_t s) {
+    CUtensorMap mq, mk, mv;
+    if (!make_map_3d(&mq, p.q, p.q_dtype, p.Sq, p.Hd, p.B * p.Nq, kBMq) ||
+        !make_map_3d(&mk, p.k, p.kv_dtype, p.Sk, p.Hd, p.B * p.Nkv, kBNk) ||
+        !make_map_3d(&mv, p.v, p.kv_dtype, p.Sk, p.Hd, p.B * p.Nkv, kBNk))
+        return cudaErrorInvalidValue;
+    FaArgs fa{};
+    fa.out = p.out;
+    fa.Sq = p.Sq;
+    fa.Sk = p.Sk;
+    fa.B = int(p.B);
+    fa.Nq = int(p.Nq);
+    fa.Nkv = int(p.Nkv);
+    fa.c = p.scale * kLog2e;
+    fa.mask_kind = p.mask_kind;
+    fa.window = p.window;
+    fa.n_qtiles = int((p.Sq + kBMq - 1) / kBMq);
+    if (p.q_dtype == PC_BF16)
+        return p.Hd == 128 ? run_fa_o<128, TBF16>(mq, mk, mv, fa, p.out_dtype, s)
+                           : run_fa_o<256, TBF16>(mq, mk, mv, fa, p.out_dtype, s);
+    return p.Hd == 128 ? run_fa_o<128, TF16>(mq, mk, mv, fa, p.out_dtype, s)
+                       : run_fa_o<256, TF16>(mq, mk, mv, fa, p.out_dtype, s);
+}
+
+uint32_t read_and_clear_fa_errors() {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fa_error_word, sizeof(v)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (v) cudaMemcpyToSymbol(g_fa_error_word, &zero, sizeof(zero));
+    return v;
+}
+
+namespace {
+RegisterFunctions reg_fa_tc({
+    {"flash_attention_tc_bf16", reinterpret_cast<const void*>(fa_tcgen05_kernel<256, TBF16, TBF16>)},
+    {"flash_attention_tc_f16", reinterpret_cast<const void*>(fa_tcgen05_kernel<256, TF16, TF16>)},
+});
+}  // namespace
+
+}  // namespace launch
+}  // namespace popcorn

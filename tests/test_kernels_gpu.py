@@ -437,6 +437,51 @@ def test_prefill_attention(pc, enc, dt, odt, mask, window, B, Nq, Nkv, Sq, Sk, H
     assert_close(from_dev(out, odt), exp, odt, what="prefill FA")
 
 
+@pytest.mark.parametrize("dt,odt", [("bf16", "bf16"), ("bf16", "f32"), ("f16", "f16")])
+@pytest.mark.parametrize("mask,window", [("causal", -1), ("bidirectional", -1), ("sliding", 100)])
+@pytest.mark.parametrize("B,Nq,Nkv,Sq,Sk,Hd", [(2, 4, 2, 300, 300, 128), (1, 2, 1, 64, 500, 256),
+                                             (1, 3, 3, 200, 129, 128), (1, 2, 1, 256, 256, 256)])
+def test_prefill_attention_tcgen05(pc, enc, dt, odt, mask, window, B, Nq, Nkv, Sq, Sk, Hd):
+    """The tensor-core path (Sq >= 32, 16-bit, Hd 128/256): ragged query and key
+    tiles, Sk > Sq and Sk < Sq (rows with no key give zeros), GQA 1/2/3."""
+    rng = np.random.default_rng(Sq * 11 + Sk + Hd)
+    q = rand(rng, (B, Nq, Sq, Hd), dt)
+    k = rand(rng, (B, Nkv, Sk, Hd), dt)
+    v = rand(rng, (B, Nkv, Sk, Hd), dt)
+    scale = 1.0 / np.sqrt(Hd)
+    exp = oracle.flash_attention(q, dt, k, v, dt, odt, scale, mask=mask, window=window)
+    out = empty_dev((B, Nq, Sq, Hd), odt)
+    m = {"causal": pc.AttentionMask.causal, "bidirectional": pc.AttentionMask.bidirectional}.get(mask)
+    if m is None:
+        m = pc.AttentionMask.causal_sliding_window(window)
+    kern = pc.Kernels.FlashAttention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), into=out, scale=scale, mask=m)
+    assert kern.function_names == ["flash_attention_tc_bf16"]
+    run(enc, kern)
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 prefill FA")
+    assert pc.device_error_check(0) == 0
+
+
+def test_prefill_attention_tcgen05_config4(pc, enc):
+    """BASELINE config 4 attention (B 4, 8 Q / 4 KV heads, S 2048, Hd 256,
+    bf16, causal) on the GPU; four (batch, head) planes checked against the
+    oracle."""
+    B, Nq, Nkv, S, Hd = 4, 8, 4, 2048, 256
+    g = torch.Generator(device="cuda").manual_seed(44)
+    q = torch.randn(B, Nq, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Nkv, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Nkv, S, Hd, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(B, Nq, S, Hd, device="cuda", dtype=torch.bfloat16)
+    run(enc, pc.Kernels.FlashAttention(q, k, v, into=out, scale=1.0 / 16, mask=pc.AttentionMask.causal))
+    for b, hq in ((0, 0), (1, 3), (2, 6), (3, 7)):
+        hkv = hq * Nkv // Nq
+        qs = from_dev(q[b:b + 1, hq:hq + 1].contiguous(), "bf16")
+        ks = from_dev(k[b:b + 1, hkv:hkv + 1].contiguous(), "bf16")
+        vs = from_dev(v[b:b + 1, hkv:hkv + 1].contiguous(), "bf16")
+        exp = oracle.flash_attention(qs, "bf16", ks, vs, "bf16", "bf16", 1.0 / 16, mask="causal")
+        assert_close(from_dev(out[b:b + 1, hq:hq + 1].contiguous(), "bf16"), exp, "bf16",
+                     what="config-4 FA b%d h%d" % (b, hq))
+
+
 def test_no_device_errors_recorded(pc):
     assert pc.device_error_check(0) == 0
 
