@@ -64,6 +64,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     return false;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded spin for latency-critical hand-offs: polls without suspending
+// (about 2^26 polls, seconds) so a completed phase is seen at once. On
+// give-up it sets bit 0 of *err and returns false.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned int* err) {
+    for (uint32_t i = 0; i < (1u << 26); ++i)
+        if (mbar_test_wait(bar, parity)) return true;
+    atomicOr(err, 1u);
+    return false;
+}
+
 // Pulls this CTA's share (part `part` of `nparts`) of [ptr, ptr+bytes) into
 // L2, in pieces of at most 64 KB. Ranges are trimmed to 16-byte boundaries.
 __device__ __forceinline__ void prefetch_share_l2(const void* ptr, uint64_t bytes, int part, int nparts) {

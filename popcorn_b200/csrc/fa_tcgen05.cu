@@ -14,15 +14,22 @@
 // fp32-accumulation tolerance of the reference semantics.
 //
 // One CTA per (128-query tile, query head, batch), heaviest causal tiles
-// first. Warp 0 lane 0 loads Q once and then the K and V tile of every
-// 64-key step; warp 1 lane 0 issues the MMAs: S(j+1) = Q.K(j+1)^T into the
-// other of two S accumulators while the softmax warps work on S(j), then
-// O += P(j).V(j). Warps 2-5 own one query row per thread (TMEM lane): they
+// first. Warp 0 lane 0 loads Q once and then the K and V tiles of every
+// 64-key step into two-stage rings, each tile as soon as its stage frees;
+// warp 1 lane 0 issues the MMAs, whichever group is ready first: S(j+1) =
+// Q.K(j+1)^T into the other of two S accumulators while the softmax warps
+// work on S(j), and O += P(j).V(j). Warps 2-5 own one query row per thread (TMEM lane): they
 // read S, mask, keep the running max and sum, write P to shared memory in
 // the MMA's swizzled K-major layout, and rescale O in tensor memory only
 // when the running max grows by more than 2^8 (P stays <= 256; the final
 // O / l is exact for any max used consistently). TMEM: S0, S1 (64 columns
 // each) and O (Hd columns) in one 512-column allocation.
+//
+// Softmax per step: ex2.approx, one select per key only on tiles that cross
+// a row's mask edge, P packed with cvt.rn.{bf16,f16}x2. Measured (config 4:
+// B 4, 8 Q / 4 KV heads, S 2048, Hd 256, causal, bf16): 147 us = 467
+// TFLOP/s. The remaining limit is the K/V load latency (~2.5 us) against a
+// two-stage ring: at Hd 256 shared memory holds no third stage.
 //
 // Every mbarrier wait is bounded; on give-up the CTA sets the error word,
 // skips its remaining work, frees its tensor memory and leaves.
@@ -36,6 +43,18 @@
 namespace popcorn {
 
 __device__ unsigned int g_fa_error_word;
+
+#ifdef PC_FA_TRACE
+// Development-only: per CTA globaltimer at start / end and its step count.
+__device__ unsigned long long g_fa_trace[4096 * 3];
+__device__ unsigned long long g_fa_steps[8][64];  // one CTA: per step event times
+#define FA_STEP(ev, j) do { if (lin == 0 && (j) < 64) g_fa_steps[ev][j] = fa_now(); } while (0)
+__device__ __forceinline__ unsigned long long fa_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#endif
 
 namespace launch {
 
@@ -60,10 +79,32 @@ struct FaArgs {
     int n_qtiles;
 };
 
+// 2^x with the hardware's approximate exponential (PTX ex2.approx: relative
+// error ~2^-22, far below P's representation error).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Two floats -> one 32-bit word of two 16-bit values (lo, hi), round to
+// nearest even (P is finite and >= 0: the same result as the bit-level rule).
+template <class T> __device__ __forceinline__ uint32_t cvt_pair(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t cvt_pair<TBF16>(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+template <> __device__ __forceinline__ uint32_t cvt_pair<TF16>(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
 // Warp-uniform bounded wait: lane 0 waits, the warp learns the outcome.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int lane) {
     int ok = 1;
-    if (lane == 0) ok = mbar_wait(bar, parity, &g_fa_error_word) ? 1 : 0;
+    if (lane == 0) ok = mbar_wait_spin(bar, parity, &g_fa_error_word) ? 1 : 0;
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -80,16 +121,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     constexpr bool BF = IT::code == TBF16::code;
     constexpr int NP = BF ? 2 : 1;  // P parts: bf16 hi + lo, or one f16
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t q_full, k_full, k_empty, v_full, v_empty, s_full[2], s_free[2], p_full, o_done;
+    __shared__ __align__(8) uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full,
+        o_done;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
 
     pdl_launch_dependents();
     unsigned char* sq =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* sk = sq + Q_BYTES;
-    unsigned char* sv = sk + KV_BYTES;
-    unsigned char* sp = sv + KV_BYTES;
+    unsigned char* sk = sq + Q_BYTES;      // two K stages
+    unsigned char* sv = sk + 2 * KV_BYTES; // two V stages
+    unsigned char* sp = sv + 2 * KV_BYTES;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // This CTA's query tile (heaviest causal tiles first), head and batch.
@@ -110,14 +152,23 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (kmin > 0) t_lo = kmin / kBNk;
     }
     const int nt = t_hi > t_lo ? int(t_hi - t_lo) : 0;
+#ifndef PC_FA_TRACE
+#define FA_STEP(ev, j) ((void)0)
+#else
+    const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (threadIdx.x == 0 && lin < 4096) {
+        g_fa_trace[lin * 3] = fa_now();
+        g_fa_trace[lin * 3 + 2] = unsigned(nt);
+    }
+#endif
 
     if (tid == 0) {
         mbar_init(smem_u32(&q_full), 1);
-        mbar_init(smem_u32(&k_full), 1);
-        mbar_init(smem_u32(&k_empty), 1);
-        mbar_init(smem_u32(&v_full), 1);
-        mbar_init(smem_u32(&v_empty), 1);
         for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&k_full[i]), 1);
+            mbar_init(smem_u32(&k_empty[i]), 1);
+            mbar_init(smem_u32(&v_full[i]), 1);
+            mbar_init(smem_u32(&v_empty[i]), 1);
             mbar_init(smem_u32(&s_full[i]), 1);
             mbar_init(smem_u32(&s_free[i]), 4);
         }
@@ -142,33 +193,47 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int at = 0; at < ATOMS; ++at)
                 tma_load_3d(smem_u32(sq + at * Q_BLOCK), &map_q, at * 64, int(q0), zq, smem_u32(&q_full));
             int kf = 0, vf = 0;  // K and V tiles issued
-            for (int j = 0; j < nt && !s_abort; ++j) {
-                const int key0 = int((t_lo + j) * kBNk);
-                const uint32_t ph = (uint32_t(j) & 1u) ^ 1u;
-                if (!mbar_wait(smem_u32(&k_empty), ph, &g_fa_error_word)) {
-                    s_abort = 1;
-                    break;
-                }
-                mbar_expect_tx(smem_u32(&k_full), KV_BYTES);
+            uint32_t idle = 0;
+            // K and V tiles are issued independently, each as soon as its stage frees.
+            while ((kf < nt || vf < nt) && !s_abort) {
+                bool progressed = false;
+                if (kf < nt && (kf == 0 || kf - vf < 2) &&
+                    mbar_test_wait(smem_u32(&k_empty[kf & 1]), (uint32_t(kf >> 1) & 1u) ^ 1u)) {
+                    const int st = kf & 1;
+                    mbar_expect_tx(smem_u32(&k_full[st]), KV_BYTES);
 #pragma unroll
-                for (int at = 0; at < ATOMS; ++at)
-                    tma_load_3d(smem_u32(sk + at * KV_BLOCK), &map_k, at * 64, key0, zkv, smem_u32(&k_full));
-                ++kf;
-                if (!mbar_wait(smem_u32(&v_empty), ph, &g_fa_error_word)) {
-                    s_abort = 1;
-                    break;
+                    for (int at = 0; at < ATOMS; ++at)
+                        tma_load_3d(smem_u32(sk + st * KV_BYTES + at * KV_BLOCK), &map_k, at * 64,
+                                    int((t_lo + kf) * kBNk), zkv, smem_u32(&k_full[st]));
+                    FA_STEP(0, kf);
+                    ++kf;
+                    progressed = true;
                 }
-                mbar_expect_tx(smem_u32(&v_full), KV_BYTES);
+                if (vf < kf && mbar_test_wait(smem_u32(&v_empty[vf & 1]), (uint32_t(vf >> 1) & 1u) ^ 1u)) {
+                    const int st = vf & 1;
+                    mbar_expect_tx(smem_u32(&v_full[st]), KV_BYTES);
 #pragma unroll
-                for (int at = 0; at < ATOMS; ++at)
-                    tma_load_3d(smem_u32(sv + at * KV_BLOCK), &map_v, at * 64, key0, zkv, smem_u32(&v_full));
-                ++vf;
+                    for (int at = 0; at < ATOMS; ++at)
+                        tma_load_3d(smem_u32(sv + st * KV_BYTES + at * KV_BLOCK), &map_v, at * 64,
+                                    int((t_lo + vf) * kBNk), zkv, smem_u32(&v_full[st]));
+                    FA_STEP(1, vf);
+                    ++vf;
+                    progressed = true;
+                }
+                if (progressed) {
+                    idle = 0;
+                } else if (++idle > (1u << 26)) {  // bounded: about seconds of polling
+                    atomicOr(&g_fa_error_word, 1u);
+                    s_abort = 1;
+                }
             }
             if (s_abort) {
                 // leave no copy in flight: wait (bounded) for the last ones issued
-                mbar_wait(smem_u32(&q_full), 0u, &g_fa_error_word);
-                if (kf > 0) mbar_wait(smem_u32(&k_full), uint32_t(kf - 1) & 1u, &g_fa_error_word);
-                if (vf > 0) mbar_wait(smem_u32(&v_full), uint32_t(vf - 1) & 1u, &g_fa_error_word);
+                mbar_wait_spin(smem_u32(&q_full), 0u, &g_fa_error_word);
+                for (int i = kf - 2 < 0 ? 0 : kf - 2; i < kf; ++i)
+                    mbar_wait_spin(smem_u32(&k_full[i & 1]), uint32_t(i >> 1) & 1u, &g_fa_error_word);
+                for (int i = vf - 2 < 0 ? 0 : vf - 2; i < vf; ++i)
+                    mbar_wait_spin(smem_u32(&v_full[i & 1]), uint32_t(i >> 1) & 1u, &g_fa_error_word);
             }
         }
     } else if (warp == 1) {
@@ -177,38 +242,59 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             const uint32_t idesc_s = make_idesc(BF, kBMq, kBNk, false);
             const uint32_t idesc_o = make_idesc(BF, kBMq, HD, true);
             const uint32_t q_base = smem_u32(sq), k_base = smem_u32(sk), v_base = smem_u32(sv), p_base = smem_u32(sp);
-            bool ok = mbar_wait(smem_u32(&q_full), 0u, &g_fa_error_word);
-            auto issue_s = [&](int j) {
-                const int buf = j & 1;
-                if (!ok || s_abort) return;
-                ok = mbar_wait(smem_u32(&s_free[buf]), (uint32_t(j >> 1) & 1u) ^ 1u, &g_fa_error_word) &&
-                     mbar_wait(smem_u32(&k_full), uint32_t(j) & 1u, &g_fa_error_word);
-                if (!ok) return;
-                tc_fence_after();
+            bool ok = mbar_wait_spin(smem_u32(&q_full), 0u, &g_fa_error_word);
+            // Issue whichever MMA group is ready: S(ns) once its K tile has
+            // landed and its accumulator is free, O += P(np).V(np) once P and V
+            // are there, so neither waits behind the other's operands.
+            int ns = 0, np = 0;
+            uint32_t idle = 0;
+            while (ok && np < nt && !s_abort) {
+                bool progressed = false;
+                if (ns < nt && ns <= np + 1) {
+                    const int buf = ns & 1;
+                    if (mbar_test_wait(smem_u32(&s_free[buf]), (uint32_t(ns >> 1) & 1u) ^ 1u) &&
+                        mbar_test_wait(smem_u32(&k_full[buf]), uint32_t(ns >> 1) & 1u)) {
+                        tc_fence_after();
+                        const uint32_t kb = k_base + buf * KV_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk)
-                    tc_mma(tmem + uint32_t(buf) * S_COLS, smem_desc_sw128(q_base + (kk >> 2) * Q_BLOCK + (kk & 3) * 32),
-                           smem_desc_sw128(k_base + (kk >> 2) * KV_BLOCK + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
-                tc_commit(smem_u32(&k_empty));
-                tc_commit(smem_u32(&s_full[buf]));
-            };
-            issue_s(0);
-            for (int j = 0; j < nt && ok && !s_abort; ++j) {
-                if (j + 1 < nt) issue_s(j + 1);
-                if (!ok) break;
-                ok = mbar_wait(smem_u32(&p_full), uint32_t(j) & 1u, &g_fa_error_word) &&
-                     mbar_wait(smem_u32(&v_full), uint32_t(j) & 1u, &g_fa_error_word);
-                if (!ok) break;
-                tc_fence_after();
+                        for (int kk = 0; kk < HD / 16; ++kk)
+                            tc_mma(tmem + uint32_t(buf) * S_COLS,
+                                   smem_desc_sw128(q_base + (kk >> 2) * Q_BLOCK + (kk & 3) * 32),
+                                   smem_desc_sw128(kb + (kk >> 2) * KV_BLOCK + (kk & 3) * 32), idesc_s,
+                                   kk > 0 ? 1u : 0u);
+                        tc_commit(smem_u32(&k_empty[buf]));
+                        FA_STEP(2, ns);
+                        tc_commit(smem_u32(&s_full[buf]));
+                        ++ns;
+                        progressed = true;
+                    }
+                }
+                if (np < ns) {
+                    const int vs = np & 1;
+                    if (mbar_test_wait(smem_u32(&p_full), uint32_t(np) & 1u) &&
+                        mbar_test_wait(smem_u32(&v_full[vs]), uint32_t(np >> 1) & 1u)) {
+                        tc_fence_after();
+                        const uint32_t vb = v_base + vs * KV_BYTES;
 #pragma unroll
-                for (int part = 0; part < NP; ++part)
+                        for (int part = 0; part < NP; ++part)
 #pragma unroll
-                    for (int kk = 0; kk < kBNk / 16; ++kk)
-                        tc_mma(tmem + O_COL, smem_desc_sw128(p_base + part * P_BLOCK + kk * 32),
-                               smem_desc_sw128_mn(v_base + kk * 2048, KV_BLOCK), idesc_o,
-                               (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(smem_u32(&v_empty));
-                tc_commit(smem_u32(&o_done));
+                            for (int kk = 0; kk < kBNk / 16; ++kk)
+                                tc_mma(tmem + O_COL, smem_desc_sw128(p_base + part * P_BLOCK + kk * 32),
+                                       smem_desc_sw128_mn(vb + kk * 2048, KV_BLOCK), idesc_o,
+                                       (np > 0 || part > 0 || kk > 0) ? 1u : 0u);
+                        tc_commit(smem_u32(&v_empty[vs]));
+                        FA_STEP(3, np);
+                        tc_commit(smem_u32(&o_done));
+                        ++np;
+                        progressed = true;
+                    }
+                }
+                if (progressed) {
+                    idle = 0;
+                } else if (++idle > (1u << 26)) {  // bounded: about seconds of polling
+                    atomicOr(&g_fa_error_word, 1u);
+                    ok = false;
+                }
             }
             if (!ok) s_abort = 1;
         }
@@ -225,6 +311,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             const int buf = j & 1;
             ok = warp_wait(smem_u32(&s_full[buf]), uint32_t(j >> 1) & 1u, lane) && !s_abort;
             if (!ok) break;
+            if (warp == 2 && lane == 0) FA_STEP(4, j);
             tc_fence_after();
             float s[kBNk];
 #pragma unroll
@@ -232,27 +319,42 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&s_free[buf]));
+            // allowed keys of this row: [key_lo, key_hi), as offsets into this tile
             const int64_t key0 = (t_lo + j) * kBNk;
+            int64_t hi = a.mask_kind == 2 ? a.Sk : (posQ + 1 < a.Sk ? posQ + 1 : a.Sk);
+            int64_t lo = a.mask_kind == 1 ? posQ - a.window + 1 : 0;
+            hi -= key0;
+            lo -= key0;
+            const int chi = hi < 0 ? 0 : (hi > kBNk ? kBNk : int(hi));
+            const int clo = lo < 0 ? 0 : (lo > kBNk ? kBNk : int(lo));
             float mx = -INFINITY;
+            if (__all_sync(0xffffffffu, clo == 0 && chi == kBNk)) {
+                // no key of this tile is masked for any row of the warp
 #pragma unroll
-            for (int c = 0; c < kBNk; ++c) {
-                const int64_t key = key0 + c;
-                const bool allowed = key < a.Sk && (a.mask_kind == 2 || (key <= posQ && (a.mask_kind != 1 || posQ - key < a.window)));
-                s[c] = allowed ? s[c] * a.c : -INFINITY;
-                mx = fmaxf(mx, s[c]);
+                for (int c = 0; c < kBNk; ++c) {
+                    s[c] *= a.c;
+                    mx = fmaxf(mx, s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < kBNk; ++c) {
+                    s[c] = (c >= clo && c < chi) ? s[c] * a.c : -INFINITY;
+                    mx = fmaxf(mx, s[c]);
+                }
             }
             // lazy rescale: keep the old max unless the new one exceeds it by 2^8
             const float m_new = fmaxf(m_used, mx);
             float factor = 1.f;
             if (m_new > m_used + kRescaleLog2) {  // also when m_used is -inf and the tile has a key
-                factor = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+                factor = m_used == -INFINITY ? 0.f : ex2(m_used - m_new);
                 m_used = m_new;
                 l *= factor;
             }
             float lsum = 0.f;
+            const float mu = m_used == -INFINITY ? 0.f : m_used;  // all s are -inf then: ex2 gives 0
 #pragma unroll
             for (int c = 0; c < kBNk; ++c) {
-                s[c] = m_used == -INFINITY ? 0.f : exp2f(s[c] - m_used);
+                s[c] = ex2(s[c] - mu);
                 lsum += s[c];
             }
             l += lsum;
@@ -260,6 +362,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             if (j > 0) {
                 ok = warp_wait(smem_u32(&o_done), uint32_t(j - 1) & 1u, lane) && !s_abort;
                 if (!ok) break;
+                if (warp == 2 && lane == 0) FA_STEP(5, j);
                 tc_fence_after();
                 // O rows that were accumulated under the old max (factor 0: O
                 // is zero there, nothing to do)
@@ -278,24 +381,28 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             // P row -> shared memory, K-major with 128-byte swizzle (A operand);
             // bf16: the hi part, then lo = p - hi in the second block
 #pragma unroll
-            for (int part = 0; part < NP; ++part) {
+            for (int c8 = 0; c8 < kBNk / 8; ++c8) {
+                uint32_t h[4];
 #pragma unroll
-                for (int c8 = 0; c8 < kBNk / 8; ++c8) {
-                    float e[8];
+                for (int i = 0; i < 4; ++i) h[i] = cvt_pair<IT>(s[c8 * 8 + 2 * i], s[c8 * 8 + 2 * i + 1]);
+                const uint32_t off = row * 128 + ((c8 ^ (row & 7)) << 4);
+                *reinterpret_cast<uint4*>(sp + off) = make_uint4(h[0], h[1], h[2], h[3]);
+                if constexpr (NP == 2) {
+                    // lo = p - hi (exact in fp32), rounded again
+                    uint32_t w[4];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float pv = s[c8 * 8 + i];
-                        e[i] = part == 0 ? pv : pv - Elem<IT>::round(pv);
+                    for (int i = 0; i < 4; ++i) {
+                        const float h0 = __uint_as_float(h[i] << 16), h1 = __uint_as_float(h[i] & 0xffff0000u);
+                        w[i] = cvt_pair<IT>(s[c8 * 8 + 2 * i] - h0, s[c8 * 8 + 2 * i + 1] - h1);
                     }
-                    const uint4 w = make_uint4(pack2<IT>(e[0], e[1]), pack2<IT>(e[2], e[3]), pack2<IT>(e[4], e[5]),
-                                               pack2<IT>(e[6], e[7]));
-                    *reinterpret_cast<uint4*>(sp + part * P_BLOCK + row * 128 + ((c8 ^ (row & 7)) << 4)) = w;
+                    *reinterpret_cast<uint4*>(sp + P_BLOCK + off) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&p_full));
+            if (warp == 2 && lane == 0) FA_STEP(6, j);
         }
         if (nt > 0 && ok) {
             ok = warp_wait(smem_u32(&o_done), uint32_t(nt - 1) & 1u, lane) && !s_abort;
@@ -337,6 +444,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+#ifdef PC_FA_TRACE
+    if (threadIdx.x == 0 && lin < 4096) g_fa_trace[lin * 3 + 1] = fa_now();
+#endif
 }
 
 // 3-D map [heads*batch, S, HD] (16-bit), box = 64 x rows x 1, 128-byte swizzle.
@@ -356,7 +466,7 @@ bool make_map_3d(CUtensorMap* map, const void* base, int dtype, int64_t S, int64
 
 template <int HD>
 constexpr size_t fa_smem() {
-    return size_t(kBMq) * HD * 2 + 2 * size_t(kBNk) * HD * 2 + 2 * size_t(kBMq) * kBNk * 2 + 1024;
+    return size_t(kBMq) * HD * 2 + 4 * size_t(kBNk) * HD * 2 + 2 * size_t(kBMq) * kBNk * 2 + 1024;
 }
 
 template <int HD, class IT, class OT>
@@ -411,6 +521,7 @@ cudaError_t flash_attention_tcgen05(const FlashAttention& p, cudaStream_t s) {
     fa.mask_kind = p.mask_kind;
     fa.window = p.window;
     fa.n_qtiles = int((p.Sq + kBMq - 1) / kBMq);
+
     if (p.q_dtype == PC_BF16)
         return p.Hd == 128 ? run_fa_o<128, TBF16>(mq, mk, mv, fa, p.out_dtype, s)
                            : run_fa_o<256, TBF16>(mq, mk, mv, fa, p.out_dtype, s);
@@ -437,3 +548,12 @@ RegisterFunctions reg_fa_tc({
 
 }  // namespace launch
 }  // namespace popcorn
+
+#ifdef PC_FA_TRACE
+extern "C" __attribute__((visibility("default"))) int pc_debug_fa_trace(unsigned long long* host) {
+    return int(cudaMemcpyFromSymbol(host, popcorn::g_fa_trace, sizeof(popcorn::g_fa_trace)));
+}
+extern "C" __attribute__((visibility("default"))) int pc_debug_fa_steps(unsigned long long* host) {
+    return int(cudaMemcpyFromSymbol(host, popcorn::g_fa_steps, sizeof(popcorn::g_fa_steps)));
+}
+#endif
