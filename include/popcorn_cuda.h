@@ -287,6 +287,29 @@ PC_API int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_we
                                     const pc_tensor* k_cache, const pc_tensor* v_cache, int64_t offset,
                                     const pc_tensor* position, pc_kernel** kernel);
 
+/* ---- batched-decode helpers (extensions; each equals a reference op
+ * sequence) ------------------------------------------------------------ */
+
+/* Splits qkv [B, (Nq+2*Nkv)*Hd] (ONE Matmul against the concatenated
+ * [W_q; W_k; W_v]) into q_out [B,Nq,1,Hd] and the new key / value rows,
+ * written to k_cache / v_cache [B,Nkv,Smax,Hd] at `offset` (or at the int32
+ * held by `position` on the device when given) exactly as KVCacheWrite
+ * stores them (KVCacheWrite.metal:17-26). Same dtype everywhere; a bit-exact
+ * copy. Hd * element size must be a multiple of 16 bytes. */
+PC_API int pc_kernel_qkv_scatter(const pc_tensor* qkv, const pc_tensor* q_out, const pc_tensor* k_cache,
+                                 const pc_tensor* v_cache, int64_t offset, const pc_tensor* position,
+                                 pc_kernel** kernel);
+/* out [rows,F] = round(act(g)) * u for gate_up [rows,2F] (g = columns 0..F-1,
+ * u = F..2F-1: ONE Matmul against [W_gate; W_up]) — GeluTanh (or SiLU) then
+ * Mul (GeluTanh.metal:6-35, Mul.metal:7-25). */
+PC_API int pc_kernel_gated_activation(const pc_tensor* gate_up, int32_t activation, const pc_tensor* out,
+                                      pc_kernel** kernel);
+/* sum_out = a + b (Add.metal), then norm_out = RMSNorm(sum_out, norm_weight,
+ * eps, add_one) (RMSNorm.metal:7-42) over the last axis; both stored. */
+PC_API int pc_kernel_add_rmsnorm(const pc_tensor* a, const pc_tensor* b, const pc_tensor* norm_weight, float eps,
+                                 int32_t add_one_to_weight, const pc_tensor* sum_out, const pc_tensor* norm_out,
+                                 pc_kernel** kernel);
+
 /* ---- fused decode step (extension) ---------------------------------------- */
 
 /* One decode layer's weights and KV caches (device pointers). Weights are

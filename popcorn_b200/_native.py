@@ -113,6 +113,9 @@ def _declare(L):
         "pc_kernel_gated_mlp": ([T, T, F, I32, T, T, I32, T, PP], I),
         "pc_kernel_matmul_residual": ([T, T, T, T, PP], I),
         "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
+        "pc_kernel_qkv_scatter": ([T, T, T, T, I64, T, PP], I),
+        "pc_kernel_gated_activation": ([T, I32, T, PP], I),
+        "pc_kernel_add_rmsnorm": ([T, T, T, F, I32, T, T, PP], I),
         "pc_flash_decoding_noalloc": ([T, T, T, T, T, F, M, P], I),
         "pc_flash_decoding_noalloc_capacity": ([], ctypes.c_size_t),
         "pc_decode_stack_workspace_bytes": ([ctypes.POINTER(pc_decode_stack_desc), ctypes.POINTER(ctypes.c_uint64)], I),

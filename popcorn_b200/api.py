@@ -521,6 +521,30 @@ class Kernels:
                              keep=_keep(x, norm_weight, w_qkv, q_out, k_cache, v_cache, position))
 
 
+    class QKVScatter(Kernel):
+        """Extension: q and the new K/V rows out of one fused QKV Matmul."""
+
+        def __init__(self, qkv, q_out, k_cache, v_cache, offset=0, position=None):
+            super().__init__(N.lib().pc_kernel_qkv_scatter, _tc(qkv), _tc(q_out), _tc(k_cache), _tc(v_cache),
+                             int(offset), _tc(position), keep=_keep(qkv, q_out, k_cache, v_cache, position))
+
+    class GatedActivation(Kernel):
+        """Extension: round(act(gate)) * up out of one fused gate/up Matmul."""
+        GELU_TANH, SILU = 0, 1
+
+        def __init__(self, gate_up, into, activation=0):
+            super().__init__(N.lib().pc_kernel_gated_activation, _tc(gate_up), int(activation), _tc(into),
+                             keep=_keep(gate_up, into))
+
+    class AddRMSNorm(Kernel):
+        """Extension: Add then RMSNorm; both results stored."""
+
+        def __init__(self, a, b, norm_weight, sum_out, norm_out, eps=1e-6, add_one_to_weight=False):
+            super().__init__(N.lib().pc_kernel_add_rmsnorm, _tc(a), _tc(b), _tc(norm_weight), ctypes.c_float(eps),
+                             int(add_one_to_weight), _tc(sum_out), _tc(norm_out),
+                             keep=_keep(a, b, norm_weight, sum_out, norm_out))
+
+
 class DecodeStackKernel(Kernel):
     """Extension: a whole batch-1 decode step through a layer stack as one
     persistent kernel (pc_kernel_decode_stack). `desc` is a filled

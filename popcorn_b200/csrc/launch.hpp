@@ -158,6 +158,32 @@ struct FlashAttention {
 cudaError_t flash_attention(const FlashAttention& p, cudaStream_t stream);
 bool flash_attention_uses_tensor_cores(const FlashAttention& p);
 
+// Batched-decode helpers (batched.cu).
+struct QKVScatter {
+    const void* qkv;  // [B, (Nq + 2 Nkv) * Hd]
+    void* q;          // [B, Nq, 1, Hd]
+    void* k_cache;    // [B, Nkv, Smax, Hd]
+    void* v_cache;
+    int dtype;
+    int64_t B, Nq, Nkv, Hd, Smax, offset;
+    const int32_t* pos_dev;  // when set, the position is read on the device
+};
+cudaError_t qkv_scatter(const QKVScatter& p, cudaStream_t stream);
+cudaError_t gated_activation(const void* gate_up, void* out, int dtype, int64_t rows, int64_t F, int act,
+                             cudaStream_t stream);
+struct AddRMSNorm {
+    const void* a;
+    const void* b;
+    void* sum_out;
+    void* norm_out;
+    const float* weight;
+    int dtype;
+    int64_t rows, H;
+    float eps;
+    int add_one;
+};
+cudaError_t add_rmsnorm(const AddRMSNorm& p, cudaStream_t stream);
+
 // One persistent kernel for a batch-1 decode step through a layer stack
 // (decode_step.cu). `layers` points to device memory.
 struct DecodeLayer {

@@ -541,6 +541,133 @@ std::unique_ptr<Kernel> make_qkv(const Tensor& x, const Tensor* nw, float eps, b
 }
 
 // ---------------------------------------------------------------------------
+// Batched-decode helpers (batched.cu)
+// ---------------------------------------------------------------------------
+inline bool aligned16_ptr(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+class QKVScatterKernel : public Kernel {
+public:
+    QKVScatterKernel(Tensor qkv, Tensor q, Tensor kc, Tensor vc, int64_t offset, const Tensor* pos)
+        : qkv_(qkv), q_(q), kc_(kc), vc_(vc) {
+        const int dt = qkv.dtype();
+        if (!is_float(dt) || q.dtype() != dt || kc.dtype() != dt || vc.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "QKVScatter needs one float dtype for qkv, q and caches.");
+        if (qkv.rank() != 2 || q.rank() != 4 || kc.rank() != 4 || !kc.same_shape(vc))
+            fail(PC_ERR_TENSOR_INVALID_RANK, "QKVScatter wants qkv [B,(Nq+2Nkv)*Hd], q [B,Nq,1,Hd], caches [B,Nkv,Smax,Hd].");
+        const int64_t B = q[0], Nq = q[1], Hd = q[3], Nkv = kc[1], Smax = kc[2];
+        if (q[2] != 1 || kc[0] != B || kc[3] != Hd || qkv[0] != B || qkv[1] != (Nq + 2 * Nkv) * Hd)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKVScatter shapes disagree: qkv " + qkv.shape_string() + ", q " +
+                                                   q.shape_string() + ", cache " + kc.shape_string() + ".");
+        const int es = dtype_stride(dt);
+        if ((Hd * es) % 16 != 0 || !aligned16_ptr(qkv.data()) || !aligned16_ptr(q.data()) ||
+            !aligned16_ptr(kc.data()) || !aligned16_ptr(vc.data()))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKVScatter needs Hd rows of a multiple of 16 bytes, 16-byte aligned.");
+        if (!pos && (offset < 0 || offset >= Smax))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache write offset " + std::to_string(offset) +
+                                                   " outside cache length " + std::to_string(Smax) + ".");
+        if (pos) {
+            if (pos->dtype() != PC_I32 || pos->element_count() < 1)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "position must be int32 [1].");
+            pos_ = *pos;
+            has_pos_ = true;
+        }
+        p_ = launch::QKVScatter{qkv.data(), q.data(), kc.data(), vc.data(), dt, B, Nq, Nkv, Hd, Smax, offset,
+                                pos ? static_cast<const int32_t*>(pos->data()) : nullptr};
+        function_names_ = "qkv_scatter";
+    }
+    const char* name() const override { return "QKVScatter"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> b = {{qkv_, PC_ACCESS_READ}, {q_, PC_ACCESS_WRITE}, {kc_, PC_ACCESS_WRITE},
+                                  {vc_, PC_ACCESS_WRITE}};
+        if (has_pos_) b.push_back({pos_, PC_ACCESS_READ});
+        return b;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::QKVScatter p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::qkv_scatter(p, s); });
+    }
+
+private:
+    Tensor qkv_, q_, kc_, vc_, pos_;
+    bool has_pos_ = false;
+    launch::QKVScatter p_{};
+};
+
+class GatedActivationKernel : public Kernel {
+public:
+    GatedActivationKernel(Tensor gu, int act, Tensor out) : gu_(gu), out_(out), act_(act) {
+        const int dt = gu.dtype();
+        if (!is_float(dt) || out.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "GatedActivation needs one float dtype.");
+        if (act != PC_ACT_GELU_TANH && act != PC_ACT_SILU)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "unknown activation.");
+        if (gu.rank() != 2 || out.rank() != 2 || out[0] != gu[0] || gu[1] != 2 * out[1])
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "GatedActivation wants gate_up [rows,2F] and out [rows,F]; got " +
+                                                   gu.shape_string() + ", " + out.shape_string() + ".");
+        rows_ = out[0];
+        F_ = out[1];
+        function_names_ = dt == PC_F32 ? "gated_activation" : std::string("gated_activation_") + dt_tag(dt);
+    }
+    const char* name() const override { return "GatedActivation"; }
+    std::vector<Binding> tensors() const override { return {{gu_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}}; }
+    void encode(KernelCommandEncoder& enc) const override {
+        const void* gu = gu_.data();
+        void* o = out_.data();
+        const int dt = gu_.dtype(), act = act_;
+        const int64_t rows = rows_, F = F_;
+        enc.dispatch(function_names_, tensors(),
+                     [=](cudaStream_t s) { return launch::gated_activation(gu, o, dt, rows, F, act, s); });
+    }
+
+private:
+    Tensor gu_, out_;
+    int act_;
+    int64_t rows_ = 0, F_ = 0;
+};
+
+class AddRMSNormKernel : public Kernel {
+public:
+    AddRMSNormKernel(Tensor a, Tensor b, const Tensor* w, float eps, bool add_one, Tensor sum, Tensor norm)
+        : a_(a), b_(b), sum_(sum), norm_(norm) {
+        const int dt = a.dtype();
+        if (!is_float(dt) || b.dtype() != dt || sum.dtype() != dt || norm.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "AddRMSNorm needs one float dtype.");
+        if (!a.same_shape(b) || !a.same_shape(sum) || !a.same_shape(norm) || a.rank() < 1)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "AddRMSNorm shapes must match; got " + a.shape_string() + ", " +
+                                                   b.shape_string() + ".");
+        const int64_t H = a[a.rank() - 1];
+        if (H <= 0) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "AddRMSNorm hidden size must be >= 1.");
+        if (w) {
+            if (w->dtype() != PC_F32)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32.");
+            require_elements(*w, H, "AddRMSNorm weight");
+            w_ = *w;
+            has_w_ = true;
+        }
+        p_ = launch::AddRMSNorm{a.data(), b.data(), sum.data(), norm.data(),
+                                w ? static_cast<const float*>(w->data()) : nullptr, dt, a.element_count() / H, H, eps,
+                                add_one ? 1 : 0};
+        function_names_ = dt == PC_F32 ? "add_rmsnorm" : std::string("add_rmsnorm_") + dt_tag(dt);
+    }
+    const char* name() const override { return "AddRMSNorm"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{a_, PC_ACCESS_READ}, {b_, PC_ACCESS_READ}, {sum_, PC_ACCESS_WRITE},
+                                  {norm_, PC_ACCESS_WRITE}};
+        if (has_w_) v.push_back({w_, PC_ACCESS_READ});
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::AddRMSNorm p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::add_rmsnorm(p, s); });
+    }
+
+private:
+    Tensor a_, b_, sum_, norm_, w_;
+    bool has_w_ = false;
+    launch::AddRMSNorm p_{};
+};
+
+// ---------------------------------------------------------------------------
 // Fused decode step (decode_step.cu)
 // ---------------------------------------------------------------------------
 launch::DecodeStep make_step(const pc_decode_stack_desc* d) {
@@ -923,6 +1050,40 @@ int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, f
     return wrap(make_qkv(tensor_arg(x, "x"), norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
                          tensor_arg(w_qkv, "w_qkv"), tensor_arg(q_out, "q_out"), tensor_arg(k_cache, "k_cache"),
                          tensor_arg(v_cache, "v_cache"), offset, position ? &pos : nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_qkv_scatter(const pc_tensor* qkv, const pc_tensor* q_out, const pc_tensor* k_cache,
+                          const pc_tensor* v_cache, int64_t offset, const pc_tensor* position, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor pos;
+    if (position) pos = tensor_arg(position, "position");
+    return wrap(std::make_unique<QKVScatterKernel>(tensor_arg(qkv, "qkv"), tensor_arg(q_out, "q_out"),
+                                                   tensor_arg(k_cache, "k_cache"), tensor_arg(v_cache, "v_cache"),
+                                                   offset, position ? &pos : nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_gated_activation(const pc_tensor* gate_up, int32_t activation, const pc_tensor* out,
+                               pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<GatedActivationKernel>(tensor_arg(gate_up, "gate_up"), activation,
+                                                        tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_add_rmsnorm(const pc_tensor* a, const pc_tensor* b, const pc_tensor* norm_weight, float eps,
+                          int32_t add_one_to_weight, const pc_tensor* sum_out, const pc_tensor* norm_out,
+                          pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(std::make_unique<AddRMSNormKernel>(tensor_arg(a, "a"), tensor_arg(b, "b"),
+                                                   norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
+                                                   tensor_arg(sum_out, "sum_out"), tensor_arg(norm_out, "norm_out")),
                 kernel);
     PC_GUARD_END
 }

@@ -79,6 +79,14 @@ class TPDecodeModel:
     and the LM head; all_reduce(t) is called on each partial sum (NCCL in the
     benchmark). The position (fixed at ctx - 1, every sequence attends to
     ctx keys) makes each step the same work as a real step at that context.
+
+    Per layer (10 launches + 2 all-reduces): one Matmul against the
+    concatenated [W_q; W_k; W_v] and a QKVScatter (q out, K/V rows into the
+    caches); ragged FlashDecoding; o_proj; all-reduce; AddRMSNorm (residual
+    add + MLP norm); one Matmul against [W_gate; W_up] and a GatedActivation;
+    down_proj; all-reduce; AddRMSNorm (residual add + the next layer's
+    attention norm, or the final norm). Each fused op rounds where the
+    unfused reference sequence stores.
     """
 
     def __init__(self, library, shape, rank=0, world=1, seed=0, device=0):
@@ -91,7 +99,7 @@ class TPDecodeModel:
         dt = {"bf16": torch.bfloat16, "f16": torch.float16}[s.dtype]
         g = torch.Generator(device=dev)
         g.manual_seed(seed * 1000003 + rank)
-        nq, nkv, f = s.Nq // world, s.Nkv // world, s.F // world
+        self.nq, self.nkv, self.f = nq, nkv, f = s.Nq // world, s.Nkv // world, s.F // world
 
         def w(*shape_, std=0.02):
             return (torch.randn(*shape_, device=dev, generator=g) * std).to(dt)
@@ -101,8 +109,12 @@ class TPDecodeModel:
             self.layers.append({
                 "attn_norm": (torch.randn(s.H, device=dev, generator=g) * 0.1).float(),
                 "mlp_norm": (torch.randn(s.H, device=dev, generator=g) * 0.1).float(),
-                "w_q": w(nq * s.Hd, s.H), "w_k": w(nkv * s.Hd, s.H), "w_v": w(nkv * s.Hd, s.H),
-                "w_o": w(s.H, nq * s.Hd), "w_gate": w(f, s.H), "w_up": w(f, s.H), "w_down": w(s.H, f),
+                # rows: this rank's q heads, then its K heads, then its V heads
+                "w_qkv": w((nq + 2 * nkv) * s.Hd, s.H),
+                "w_o": w(s.H, nq * s.Hd),
+                # rows: this rank's gate slice, then its up slice
+                "w_gu": w(2 * f, s.H),
+                "w_down": w(s.H, f),
                 "k_cache": w(s.B, nkv, s.ctx, s.Hd, std=1.0), "v_cache": w(s.B, nkv, s.ctx, s.Hd, std=1.0),
             })
         self.final_norm = (torch.randn(s.H, device=dev, generator=g) * 0.1).float()
@@ -112,12 +124,11 @@ class TPDecodeModel:
         self.xn = torch.zeros_like(self.x)
         self.h = torch.zeros_like(self.x)
         self.o = torch.zeros_like(self.x)
+        self.qkv = torch.zeros(B, (nq + 2 * nkv) * s.Hd, device=dev, dtype=dt)
         self.q = torch.zeros(B, nq, 1, s.Hd, device=dev, dtype=dt)
-        self.k = torch.zeros(B, nkv, 1, s.Hd, device=dev, dtype=dt)
-        self.v = torch.zeros(B, nkv, 1, s.Hd, device=dev, dtype=dt)
         self.attn = torch.zeros(B, nq, 1, s.Hd, device=dev, dtype=dt)
-        self.gate = torch.zeros(B, f, device=dev, dtype=dt)
-        self.up = torch.zeros(B, f, device=dev, dtype=dt)
+        self.gu = torch.zeros(B, 2 * f, device=dev, dtype=dt)
+        self.act = torch.zeros(B, f, device=dev, dtype=dt)
         self.logits = torch.zeros(B, s.V // world, device=dev, dtype=dt)
         self.lens = torch.full((B,), s.ctx, device=dev, dtype=torch.int32)
         self.scratch = FixedScratch(64 << 20, device)
@@ -129,30 +140,22 @@ class TPDecodeModel:
         if self._ks is not None:
             return self._ks
         s, K = self.s, Kernels
-        nq = s.Nq // self.world
-        ks = []
-        for w in self.layers:
-            ks += [K.RMSNorm(self.x, w["attn_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True),
-                   K.Matmul(self.xn, w["w_q"], into=self.q.view(s.B, -1), transpose_b=True),
-                   K.Matmul(self.xn, w["w_k"], into=self.k.view(s.B, -1), transpose_b=True),
-                   K.Matmul(self.xn, w["w_v"], into=self.v.view(s.B, -1), transpose_b=True),
-                   K.KVCacheWrite(self.k, w["k_cache"], offset=s.ctx - 1),
-                   K.KVCacheWrite(self.v, w["v_cache"], offset=s.ctx - 1),
+        ks = [K.RMSNorm(self.x, self.layers[0]["attn_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True)]
+        for i, w in enumerate(self.layers):
+            nxt_norm = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.final_norm
+            ks += [K.Matmul(self.xn, w["w_qkv"], into=self.qkv, transpose_b=True),
+                   K.QKVScatter(self.qkv, self.q, w["k_cache"], w["v_cache"], offset=s.ctx - 1),
                    K.FlashDecodingRagged(self.q, w["k_cache"], w["v_cache"], self.lens, into=self.attn,
                                          scale=s.scale, mask=AttentionMask.causal),
-                   K.Matmul(self.attn.view(s.B, nq * s.Hd), w["w_o"], into=self.o, transpose_b=True),
+                   K.Matmul(self.attn.view(s.B, self.nq * s.Hd), w["w_o"], into=self.o, transpose_b=True),
                    None,
-                   K.Add(self.x, self.o, into=self.h),
-                   K.RMSNorm(self.h, w["mlp_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True),
-                   K.Matmul(self.xn, w["w_gate"], into=self.gate, transpose_b=True),
-                   K.Matmul(self.xn, w["w_up"], into=self.up, transpose_b=True),
-                   K.GeluTanh(self.gate, into=self.gate),
-                   K.Mul(self.gate, self.up, into=self.gate),
-                   K.Matmul(self.gate, w["w_down"], into=self.o, transpose_b=True),
+                   K.AddRMSNorm(self.x, self.o, w["mlp_norm"], self.h, self.xn, eps=s.eps, add_one_to_weight=True),
+                   K.Matmul(self.xn, w["w_gu"], into=self.gu, transpose_b=True),
+                   K.GatedActivation(self.gu, self.act),
+                   K.Matmul(self.act, w["w_down"], into=self.o, transpose_b=True),
                    None,
-                   K.Add(self.h, self.o, into=self.x)]
-        ks += [K.RMSNorm(self.x, self.final_norm, into=self.xn, eps=s.eps, add_one_to_weight=True),
-               K.Matmul(self.xn, self.lm_head, into=self.logits, transpose_b=True)]
+                   K.AddRMSNorm(self.h, self.o, nxt_norm, self.x, self.xn, eps=s.eps, add_one_to_weight=True)]
+        ks += [K.Matmul(self.xn, self.lm_head, into=self.logits, transpose_b=True)]
         self._ks = ks
         return ks
 
