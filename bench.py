@@ -335,6 +335,14 @@ def run_tp(args):
     hbm_gbs, _, peak_kind = peaks()
     shape = TPShape(layers=args.tp_layers)
     model = TPDecodeModel(pc.KernelLibrary(local), shape, rank=rank, world=world, seed=5, device=local)
+    if args.allreduce == "peer":
+        def all_gather(blob):
+            if world == 1:
+                return [blob]
+            out = [None] * world
+            dist.all_gather_object(out, blob)
+            return out
+        model.use_peer_allreduce(all_gather)
     stream = torch.cuda.Stream(device=local)
 
     def all_reduce(t):
@@ -378,7 +386,7 @@ def run_tp(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV)",
             "config": {"workload": "config5: 9B-shape decode, %d layers, vocab 256000, batch 32, KV ctx 8192"
                                    % shape.L, "global_batch": shape.B, "seq_len": shape.ctx,
-                       "parallelism": "tp%d" % world,
+                       "parallelism": "tp%d" % world, "allreduce": args.allreduce,
                        "l2": "inputs larger than L2"},
             "per_rank_hbm_gbs": per_rank_bytes / (ms * 1e-3) / 1e9,
             "per_rank_frac_of_measured_hbm": per_rank_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, "peak_kind": peak_kind,
@@ -410,6 +418,8 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill"])
     ap.add_argument("--tp-layers", type=int, default=42)
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tp9b: one-shot all-reduce over peer memory fused with Add + RMSNorm, or NCCL")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="config-2 stack depth (26 for the bench line; fewer for small profiling captures)")
     args = ap.parse_args()

@@ -310,6 +310,40 @@ PC_API int pc_kernel_add_rmsnorm(const pc_tensor* a, const pc_tensor* b, const p
                                  int32_t add_one_to_weight, const pc_tensor* sum_out, const pc_tensor* norm_out,
                                  pc_kernel** kernel);
 
+/* ---- tensor parallelism over peer memory (extension) ---------------------- */
+
+/* CUDA IPC of a pc_buffer_alloc allocation (64-byte opaque handle), for one
+ * process per GPU on one node. pc_ipc_open_handle maps a peer's allocation
+ * into this process (peer access enabled lazily); pc_ipc_close_handle
+ * unmaps it. */
+PC_API int pc_ipc_get_handle(const void* ptr, uint8_t* handle64);
+PC_API int pc_ipc_open_handle(const uint8_t* handle64, void** ptr);
+PC_API int pc_ipc_close_handle(void* ptr);
+
+/* The ranks of one tensor-parallel group as seen by this process: for every
+ * rank, its two partial-sum buffers ([rows, H] of the activation dtype, at
+ * least rows * H elements) and its control block (5 x uint32, zero-filled
+ * once before first use); this rank's own pointers at index `rank`, the
+ * peers' opened with pc_ipc_open_handle. */
+#define PC_MAX_PEERS 8
+typedef struct pc_peer_group {
+    int32_t world, rank;
+    void* partial[PC_MAX_PEERS][2];
+    uint32_t* control[PC_MAX_PEERS];
+} pc_peer_group;
+/* All-reduce (sum) of partial buffer `buffer` (0 or 1) across the group,
+ * then sum_out = residual + that sum, then norm_out = RMSNorm(sum_out,
+ * norm_weight, eps, add_one) — the NCCL all-reduce -> Add (Add.metal) ->
+ * RMSNorm (RMSNorm.metal) sequence in one kernel. The ranks' partials are
+ * read over peer memory (NVLink) once each rank has published its own;
+ * every wait is bounded (device error word bit 3 on give-up). Every rank
+ * must issue the same sequence of calls; a rank's buffer b is rewritten
+ * only after its next call on the other buffer. residual / sum_out /
+ * norm_out [rows, H], bf16 or f16, H a multiple of 8 and at most 8192. */
+PC_API int pc_kernel_allreduce_add_rmsnorm(const pc_peer_group* group, int32_t buffer, const pc_tensor* residual,
+                                           const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                                           const pc_tensor* sum_out, const pc_tensor* norm_out, pc_kernel** kernel);
+
 /* ---- fused decode step (extension) ---------------------------------------- */
 
 /* One decode layer's weights and KV caches (device pointers). Weights are

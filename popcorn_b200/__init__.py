@@ -6,9 +6,9 @@ reference's Swift surface in Python over that ABI; ``decode`` composes the
 decode layer and stack used by the benchmark.
 """
 from .api import (Access, AttentionMask, DataType, FixedScratch, Kernel, KernelCommandEncoder, KernelLibrary,
-                  KernelScratchAllocator, Kernels, PopcornError, ScratchPool, ScratchSpec, Tensor,
+                  KernelScratchAllocator, Kernels, PeerGroup, PopcornError, ScratchPool, ScratchSpec, Tensor,
                   device_error_check)
 
 __all__ = ["Access", "AttentionMask", "DataType", "FixedScratch", "Kernel", "KernelCommandEncoder", "KernelLibrary",
-           "KernelScratchAllocator", "Kernels", "PopcornError", "ScratchPool", "ScratchSpec", "Tensor",
+           "KernelScratchAllocator", "Kernels", "PeerGroup", "PopcornError", "ScratchPool", "ScratchSpec", "Tensor",
            "device_error_check"]

@@ -45,6 +45,15 @@ class pc_scratch_allocator(ctypes.Structure):
 _lib = None
 
 
+MAX_PEERS = 8
+
+
+class pc_peer_group(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("partial", (ctypes.c_void_p * 2) * MAX_PEERS),
+                ("control", ctypes.POINTER(ctypes.c_uint32) * MAX_PEERS)]
+
+
 def lib():
     """Loads the CUDA library once; raises ImportError if it is missing."""
     global _lib
@@ -114,6 +123,10 @@ def _declare(L):
         "pc_kernel_matmul_residual": ([T, T, T, T, PP], I),
         "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
         "pc_kernel_qkv_scatter": ([T, T, T, T, I64, T, PP], I),
+        "pc_ipc_get_handle": ([P, ctypes.POINTER(ctypes.c_uint8)], I),
+        "pc_ipc_open_handle": ([ctypes.POINTER(ctypes.c_uint8), PP], I),
+        "pc_ipc_close_handle": ([P], I),
+        "pc_kernel_allreduce_add_rmsnorm": ([ctypes.POINTER(pc_peer_group), I32, T, T, F, I32, T, T, PP], I),
         "pc_kernel_gated_activation": ([T, I32, T, PP], I),
         "pc_kernel_add_rmsnorm": ([T, T, T, F, I32, T, T, PP], I),
         "pc_flash_decoding_noalloc": ([T, T, T, T, T, F, M, P], I),

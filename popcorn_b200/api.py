@@ -545,6 +545,80 @@ class Kernels:
                              keep=_keep(a, b, norm_weight, sum_out, norm_out))
 
 
+    class AllReduceAddRMSNorm(Kernel):
+        """Extension: all-reduce (sum) of a PeerGroup partial buffer over peer
+        memory, then Add(residual) and RMSNorm, in one kernel."""
+
+        def __init__(self, group, buffer, residual, norm_weight, sum_out, norm_out, eps=1e-6,
+                     add_one_to_weight=False):
+            super().__init__(N.lib().pc_kernel_allreduce_add_rmsnorm, ctypes.byref(group.c), int(buffer),
+                             _tc(residual), _tc(norm_weight), ctypes.c_float(eps), int(add_one_to_weight),
+                             _tc(sum_out), _tc(norm_out), keep=_keep(group, residual, norm_weight, sum_out, norm_out))
+
+
+class PeerGroup:
+    """The tensor-parallel ranks' partial-sum buffers and control blocks,
+    shared through CUDA IPC (one process per GPU on one node).
+
+    Each rank allocates two [rows, cols] partial buffers of `dtype` and a
+    zero-filled control block, and `all_gather(bytes) -> [bytes per rank]`
+    (e.g. torch.distributed.all_gather_object) exchanges their IPC handles;
+    the peers' buffers are then opened in this process. `partial(b)` is this
+    rank's buffer b as a Tensor: the Matmul that produces the partial sum
+    writes into it."""
+
+    def __init__(self, device, world, rank, rows, cols, dtype, all_gather):
+        if world > N.MAX_PEERS:
+            raise PopcornError(PopcornError.tensorShapeMismatch, "at most %d ranks" % N.MAX_PEERS)
+        L = N.lib()
+        self.device, self.world, self.rank, self.rows, self.cols = device, world, rank, rows, cols
+        self.dtype = DataType[dtype] if isinstance(dtype, str) else DataType(dtype)
+        nbytes = rows * cols * L.pc_dtype_stride(int(self.dtype))
+        own = []
+        for _ in range(3):
+            p = ctypes.c_void_p()
+            _check(L.pc_buffer_alloc(device, nbytes if len(own) < 2 else 64, ctypes.byref(p)))
+            own.append(p.value)
+        zeros = (ctypes.c_uint8 * 64)()
+        _check(L.pc_memcpy_htod_async(own[2], ctypes.cast(zeros, ctypes.c_void_p), 64, None))
+        _check(L.pc_stream_synchronize(None))
+        self._own = own
+        handles = []
+        for p in own:
+            h = (ctypes.c_uint8 * 64)()
+            _check(L.pc_ipc_get_handle(p, h))
+            handles.append(bytes(h))
+        gathered = all_gather(b"".join(handles))
+        self._opened = []
+        g = N.pc_peer_group()
+        g.world, g.rank = world, rank
+        for r in range(world):
+            if r == rank:
+                ptrs = own
+            else:
+                ptrs = []
+                blob = gathered[r]
+                for i in range(3):
+                    h = (ctypes.c_uint8 * 64).from_buffer_copy(blob[64 * i:64 * (i + 1)])
+                    p = ctypes.c_void_p()
+                    _check(L.pc_ipc_open_handle(h, ctypes.byref(p)))
+                    ptrs.append(p.value)
+                    self._opened.append(p.value)
+            g.partial[r][0] = ptrs[0]
+            g.partial[r][1] = ptrs[1]
+            g.control[r] = ctypes.cast(ptrs[2], ctypes.POINTER(ctypes.c_uint32))
+        self.c = g
+
+    def partial(self, b):
+        return Tensor(self._own[b], (self.rows, self.cols), self.dtype, owner=self)
+
+    def close(self):
+        L = N.lib()
+        for p in self._opened:
+            L.pc_ipc_close_handle(p)
+        self._opened = []
+
+
 class DecodeStackKernel(Kernel):
     """Extension: a whole batch-1 decode step through a layer stack as one
     persistent kernel (pc_kernel_decode_stack). `desc` is a filled

@@ -786,6 +786,7 @@ RegisterFunctions reg_fd({
 uint32_t read_and_clear_gemv_errors();
 uint32_t read_and_clear_gemm_errors();
 uint32_t read_and_clear_fa_errors();
+uint32_t read_and_clear_allreduce_errors();
 uint32_t read_and_clear_step_errors();
 
 }  // namespace launch
@@ -801,7 +802,7 @@ extern "C" int pc_device_error_check(int device, uint32_t* flags) {
     cudaDeviceSynchronize();
     *flags = popcorn::launch::read_and_clear_fd_errors() | popcorn::launch::read_and_clear_gemv_errors() |
              popcorn::launch::read_and_clear_gemm_errors() | popcorn::launch::read_and_clear_step_errors() |
-             popcorn::launch::read_and_clear_fa_errors();
+             popcorn::launch::read_and_clear_fa_errors() | popcorn::launch::read_and_clear_allreduce_errors();
     cudaSetDevice(prev);
     return PC_OK;
 }

@@ -184,6 +184,25 @@ struct AddRMSNorm {
 };
 cudaError_t add_rmsnorm(const AddRMSNorm& p, cudaStream_t stream);
 
+// One-shot all-reduce of tensor-parallel partial sums over peer memory,
+// fused with the residual add and RMSNorm (allreduce.cu).
+constexpr int kMaxPeers = 8;
+struct PeerAllReduce {
+    const void* partial[kMaxPeers][2];  // each rank's two partial buffers, as mapped here
+    unsigned int* ctl[kMaxPeers];       // each rank's control block: flag[2], epoch[2], CTA count
+    int rank, world, buffer;
+    const void* residual;
+    void* sum_out;
+    void* norm_out;
+    const float* weight;
+    int dtype;
+    int64_t rows, H;
+    float eps;
+    int add_one;
+};
+bool peer_allreduce_supports(const PeerAllReduce& p);
+cudaError_t peer_allreduce_add_rmsnorm(const PeerAllReduce& p, cudaStream_t stream);
+
 // One persistent kernel for a batch-1 decode step through a layer stack
 // (decode_step.cu). `layers` points to device memory.
 struct DecodeLayer {

@@ -668,6 +668,71 @@ private:
 };
 
 // ---------------------------------------------------------------------------
+// All-reduce + Add + RMSNorm over peer memory (allreduce.cu)
+// ---------------------------------------------------------------------------
+class PeerAllReduceKernel : public Kernel {
+public:
+    PeerAllReduceKernel(const pc_peer_group* g, int buffer, Tensor res, const Tensor* w, float eps, bool add_one,
+                        Tensor sum, Tensor norm)
+        : res_(res), sum_(sum), norm_(norm) {
+        if (!g) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group is null.");
+        const int dt = res.dtype();
+        if ((dt != PC_BF16 && dt != PC_F16) || sum.dtype() != dt || norm.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "peer all-reduce serves bf16 or f16.");
+        if (!res.same_shape(sum) || !res.same_shape(norm) || res.rank() < 1)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "residual, sum and norm outputs must have one shape.");
+        if (g->world < 1 || g->world > PC_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group: bad world / rank.");
+        launch::PeerAllReduce p{};
+        for (int r = 0; r < g->world; ++r) {
+            if (!g->partial[r][0] || !g->partial[r][1] || !g->control[r])
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group: missing buffer of rank " + std::to_string(r) + ".");
+            p.partial[r][0] = g->partial[r][0];
+            p.partial[r][1] = g->partial[r][1];
+            p.ctl[r] = g->control[r];
+        }
+        const int64_t H = res[res.rank() - 1];
+        if (w) {
+            if (w->dtype() != PC_F32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32.");
+            require_elements(*w, H, "all-reduce norm weight");
+            w_ = *w;
+            has_w_ = true;
+        }
+        p.rank = g->rank;
+        p.world = g->world;
+        p.buffer = buffer;
+        p.residual = res.data();
+        p.sum_out = sum.data();
+        p.norm_out = norm.data();
+        p.weight = w ? static_cast<const float*>(w->data()) : nullptr;
+        p.dtype = dt;
+        p.rows = res.element_count() / H;
+        p.H = H;
+        p.eps = eps;
+        p.add_one = add_one ? 1 : 0;
+        if (!launch::peer_allreduce_supports(p))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer all-reduce: H must be a multiple of 8 and <= 8192, buffer 0 or 1.");
+        p_ = p;
+        function_names_ = dt == PC_BF16 ? "allreduce_add_rmsnorm_bf16" : "allreduce_add_rmsnorm_f16";
+    }
+    const char* name() const override { return "AllReduceAddRMSNorm"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{res_, PC_ACCESS_READ}, {sum_, PC_ACCESS_WRITE}, {norm_, PC_ACCESS_WRITE}};
+        if (has_w_) v.push_back({w_, PC_ACCESS_READ});
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::PeerAllReduce p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::peer_allreduce_add_rmsnorm(p, s); });
+    }
+
+private:
+    Tensor res_, sum_, norm_, w_;
+    bool has_w_ = false;
+    launch::PeerAllReduce p_{};
+};
+
+// ---------------------------------------------------------------------------
 // Fused decode step (decode_step.cu)
 // ---------------------------------------------------------------------------
 launch::DecodeStep make_step(const pc_decode_stack_desc* d) {
@@ -1084,6 +1149,19 @@ int pc_kernel_add_rmsnorm(const pc_tensor* a, const pc_tensor* b, const pc_tenso
     return wrap(std::make_unique<AddRMSNormKernel>(tensor_arg(a, "a"), tensor_arg(b, "b"),
                                                    norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
                                                    tensor_arg(sum_out, "sum_out"), tensor_arg(norm_out, "norm_out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_allreduce_add_rmsnorm(const pc_peer_group* group, int32_t buffer, const pc_tensor* residual,
+                                    const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                                    const pc_tensor* sum_out, const pc_tensor* norm_out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(std::make_unique<PeerAllReduceKernel>(group, buffer, tensor_arg(residual, "residual"),
+                                                      norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
+                                                      tensor_arg(sum_out, "sum_out"), tensor_arg(norm_out, "norm_out")),
                 kernel);
     PC_GUARD_END
 }

@@ -300,6 +300,31 @@ int pc_buffer_alloc(int device, size_t bytes, void** ptr) {
     PC_GUARD_END
 }
 
+int pc_ipc_get_handle(const void* ptr, uint8_t* handle64) {
+    PC_GUARD_BEGIN
+    if (!ptr || !handle64) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "null pointer.");
+    cudaIpcMemHandle_t h;
+    check_cuda(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+    memcpy(handle64, &h, 64);
+    PC_GUARD_END
+}
+
+int pc_ipc_open_handle(const uint8_t* handle64, void** ptr) {
+    PC_GUARD_BEGIN
+    if (!ptr || !handle64) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "null pointer.");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, 64);
+    check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    PC_GUARD_END
+}
+
+int pc_ipc_close_handle(void* ptr) {
+    PC_GUARD_BEGIN
+    check_cuda(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+    PC_GUARD_END
+}
+
 int pc_buffer_free(void* ptr) {
     PC_GUARD_BEGIN
     check_cuda(cudaFree(ptr), "cudaFree");

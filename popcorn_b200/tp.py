@@ -20,7 +20,7 @@ Every computation is a popcorn_b200 kernel (Matmul on the tcgen05 tensor
 cores for M = 32, RMSNorm, KVCacheWrite, ragged FlashDecoding, GeluTanh,
 Mul, Add); torch provides device memory, streams and the collective.
 """
-from .api import AttentionMask, FixedScratch, KernelCommandEncoder, Kernels
+from .api import AttentionMask, FixedScratch, KernelCommandEncoder, Kernels, PeerGroup
 
 
 class TPShape:
@@ -80,7 +80,8 @@ class TPDecodeModel:
     benchmark). The position (fixed at ctx - 1, every sequence attends to
     ctx keys) makes each step the same work as a real step at that context.
 
-    Per layer (10 launches + 2 all-reduces): one Matmul against the
+    Per layer (10 launches + 2 all-reduces, or 10 launches with the peer
+    all-reduce fused into the add + norm): one Matmul against the
     concatenated [W_q; W_k; W_v] and a QKVScatter (q out, K/V rows into the
     caches); ragged FlashDecoding; o_proj; all-reduce; AddRMSNorm (residual
     add + MLP norm); one Matmul against [W_gate; W_up] and a GatedActivation;
@@ -132,6 +133,17 @@ class TPDecodeModel:
         self.logits = torch.zeros(B, s.V // world, device=dev, dtype=dt)
         self.lens = torch.full((B,), s.ctx, device=dev, dtype=torch.int32)
         self.scratch = FixedScratch(64 << 20, device)
+        self.device = device
+        self.peer = None
+        self._ks = None
+
+    def use_peer_allreduce(self, all_gather):
+        """Switches the two all-reduces per layer from the caller's collective
+        to the one-shot peer-memory kernel fused with Add + RMSNorm
+        (Kernels.AllReduceAddRMSNorm). `all_gather(bytes) -> [bytes]` exchanges
+        the IPC handles once (every rank calls this together)."""
+        s = self.s
+        self.peer = PeerGroup(self.device, self.world, self.rank, s.B, s.H, s.dtype, all_gather)
         self._ks = None
 
     def kernels(self):
@@ -140,6 +152,16 @@ class TPDecodeModel:
         if self._ks is not None:
             return self._ks
         s, K = self.s, Kernels
+        peer = self.peer
+        o_a = peer.partial(0) if peer else self.o  # o_proj partial sum
+        o_b = peer.partial(1) if peer else self.o  # down_proj partial sum
+
+        def reduce_add_norm(buf, part, residual, weight, sum_out):
+            if peer:
+                return [K.AllReduceAddRMSNorm(peer, buf, residual, weight, sum_out, self.xn, eps=s.eps,
+                                              add_one_to_weight=True)]
+            return [None, K.AddRMSNorm(residual, part, weight, sum_out, self.xn, eps=s.eps, add_one_to_weight=True)]
+
         ks = [K.RMSNorm(self.x, self.layers[0]["attn_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True)]
         for i, w in enumerate(self.layers):
             nxt_norm = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.final_norm
@@ -147,14 +169,12 @@ class TPDecodeModel:
                    K.QKVScatter(self.qkv, self.q, w["k_cache"], w["v_cache"], offset=s.ctx - 1),
                    K.FlashDecodingRagged(self.q, w["k_cache"], w["v_cache"], self.lens, into=self.attn,
                                          scale=s.scale, mask=AttentionMask.causal),
-                   K.Matmul(self.attn.view(s.B, self.nq * s.Hd), w["w_o"], into=self.o, transpose_b=True),
-                   None,
-                   K.AddRMSNorm(self.x, self.o, w["mlp_norm"], self.h, self.xn, eps=s.eps, add_one_to_weight=True),
-                   K.Matmul(self.xn, w["w_gu"], into=self.gu, transpose_b=True),
+                   K.Matmul(self.attn.view(s.B, self.nq * s.Hd), w["w_o"], into=o_a, transpose_b=True)]
+            ks += reduce_add_norm(0, o_a, self.x, w["mlp_norm"], self.h)
+            ks += [K.Matmul(self.xn, w["w_gu"], into=self.gu, transpose_b=True),
                    K.GatedActivation(self.gu, self.act),
-                   K.Matmul(self.act, w["w_down"], into=self.o, transpose_b=True),
-                   None,
-                   K.AddRMSNorm(self.h, self.o, nxt_norm, self.x, self.xn, eps=s.eps, add_one_to_weight=True)]
+                   K.Matmul(self.act, w["w_down"], into=o_b, transpose_b=True)]
+            ks += reduce_add_norm(1, o_b, self.h, nxt_norm, self.x)
         ks += [K.Matmul(self.xn, self.lm_head, into=self.logits, transpose_b=True)]
         self._ks = ks
         return ks

@@ -138,3 +138,59 @@ def test_tp_model_one_rank_matches_oracle(pc):
     assert_chain_close(oracle.to_f32(from_dev(m.logits, dt), dt), oracle.to_f32(exp, dt), dt, what="logits",
                        ulps=16, rel=1e-2)
     assert pc.device_error_check(0) == 0
+
+
+def _fill(pc, tensor, host):
+    """Copies a host array into a raw library Tensor."""
+    import ctypes
+    from popcorn_b200 import _native as N
+    a = np.ascontiguousarray(host)
+    L = N.lib()
+    assert L.pc_memcpy_htod_async(tensor.data_ptr, a.ctypes.data_as(ctypes.c_void_p), a.nbytes, None) == 0
+    assert L.pc_stream_synchronize(None) == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_peer_allreduce_world1(pc, enc, dt):
+    """One rank: the all-reduce is the partial itself; then Add and RMSNorm.
+    Repeated calls on both buffers check the epoch protocol."""
+    rng = np.random.default_rng(12)
+    rows, H = 4, 3584
+    g = pc.PeerGroup(0, 1, 0, rows, H, dt, lambda b: [b])
+    w = (rng.standard_normal(H) * 0.1).astype(np.float32)
+    wd = torch.from_numpy(w).cuda()
+    for it in range(3):
+        for buf in (0, 1):
+            part = rand(rng, (rows, H), dt)
+            res = rand(rng, (rows, H), dt)
+            _fill(pc, g.partial(buf), part)
+            s_out, n_out = empty_dev((rows, H), dt), empty_dev((rows, H), dt)
+            run(enc, pc.Kernels.AllReduceAddRMSNorm(g, buf, to_dev(res, dt), wd, s_out, n_out, eps=1e-6,
+                                                    add_one_to_weight=True))
+            s_exp = oracle.add(res, part, dt)
+            assert np.array_equal(from_dev(s_out, dt), s_exp), (it, buf)
+            assert_close(from_dev(n_out, dt), oracle.rmsnorm(s_exp, dt, w, eps=1e-6, add_one=True), dt, what="norm")
+    assert pc.device_error_check(0) == 0
+    g.close()
+
+
+def test_tp_model_one_rank_peer_allreduce(pc):
+    """The TP model with the fused peer all-reduce (one rank) against the
+    oracle step, as test_tp_model_one_rank_matches_oracle."""
+    from popcorn_b200.tp import TPDecodeModel, TPShape
+    dt = "bf16"
+    shape = TPShape(hidden=512, q_heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=2048, layers=2, batch=4,
+                    ctx=96, dtype=dt)
+    m = TPDecodeModel(pc.KernelLibrary(0), shape, seed=3)
+    m.use_peer_allreduce(lambda b: [b])
+    m.x.normal_(generator=torch.Generator(device="cuda").manual_seed(1))
+    host = {"x": from_dev(m.x, dt), "final_norm": m.final_norm.cpu().numpy(), "lm_head": from_dev(m.lm_head, dt),
+            "layers": [{k: (v.cpu().numpy() if v.dtype == torch.float32 else from_dev(v, dt)) for k, v in w.items()}
+                       for w in m.layers]}
+    enc = m.encoder()
+    m.step(enc, lambda t: pytest.fail("no collective on the peer path"))
+    torch.cuda.synchronize()
+    exp = _oracle_step(m, host, dt)
+    assert_chain_close(oracle.to_f32(from_dev(m.logits, dt), dt), oracle.to_f32(exp, dt), dt, what="logits",
+                       ulps=16, rel=1e-2)
+    assert pc.device_error_check(0) == 0
