@@ -494,16 +494,17 @@ def main():
 
         # ---- end to end through the C ABI with host buffers ----
         H = shape.H
-        host_in = torch.empty(H, dtype=torch.float16).pin_memory()
-        host_in.normal_()
-        host_pos = torch.tensor([pos, pos + 1], dtype=torch.int32).pin_memory()
+        # the step's inputs as laid out in stack.io: x (f16), then [pos, pos + 1]
+        io_bytes = stack.io_pos_offset + 8
+        host_io = torch.zeros(io_bytes, dtype=torch.uint8).pin_memory()
+        host_io[:H * 2].view(torch.float16).normal_()
+        host_io[stack.io_pos_offset:io_bytes].view(torch.int32).copy_(torch.tensor([pos, pos + 1], dtype=torch.int32))
         host_out = torch.empty(H, dtype=torch.float16).pin_memory()
         L = N.lib()
         sptr = torch.cuda.current_stream().cuda_stream
 
         def e2e_step():
-            L.pc_memcpy_htod_async(stack.x.data_ptr(), host_in.data_ptr(), H * 2, sptr)
-            L.pc_memcpy_htod_async(stack.pos_state.data_ptr(), host_pos.data_ptr(), 8, sptr)
+            L.pc_memcpy_htod_async(stack.io.data_ptr(), host_io.data_ptr(), io_bytes, sptr)
             graph.replay()
             L.pc_memcpy_dtoh_async(host_out.data_ptr(), stack.out.data_ptr(), H * 2, sptr)
 
@@ -615,7 +616,7 @@ def main():
         "fused_step": {"kernel": "decode_step_f16 (one persistent launch per token, all 26 layers)",
                        "ms_per_step": fused_ms, "tok_s": 1000.0 / fused_ms,
                        "step_hbm_gbs": bytes_step / (fused_ms * 1e-3) / 1e9, "device_error_word": fused_err},
-        "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": H * 2 + 8, "d2h_bytes_per_step": H * 2,
+        "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": H * 2,
                 "path": "pc_memcpy_htod_async (pinned host) -> graph of C-ABI kernels -> pc_memcpy_dtoh_async"},
         "gpu_launches": launches_per_step * args.steps,
         "launches_per_step": launches_per_step,

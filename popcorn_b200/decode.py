@@ -101,14 +101,20 @@ class DecodeStack:
         s = shape
         tdt = _torch_dtype(s.dtype)
         dev = "cuda:%d" % device
-        self.x = torch.zeros(1, s.H, dtype=tdt, device=dev)
+        # One device block holds the step's inputs: the hidden state x, then
+        # the position state [pos, pos + 1] (int32) at a 16-byte boundary,
+        # so a caller feeds a step with a single host-to-device copy.
+        esz = torch.tensor([], dtype=tdt).element_size()
+        self.io_pos_offset = (s.H * esz + 15) // 16 * 16
+        self.io = torch.zeros(self.io_pos_offset + 16, dtype=torch.uint8, device=dev)
+        self.x = self.io[:s.H * esz].view(tdt).view(1, s.H)
         self.x2 = torch.zeros(1, s.H, dtype=tdt, device=dev)
         self.h = torch.zeros(1, s.H, dtype=tdt, device=dev)
         self.q = torch.zeros(1, s.Nq, 1, s.Hd, dtype=tdt, device=dev)
         self.attn = torch.zeros(1, s.Nq, 1, s.Hd, dtype=tdt, device=dev)
         self.act = torch.zeros(1, s.F, dtype=tdt, device=dev)
         # device-resident position state: [pos, pos + 1]
-        self.pos_state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.pos_state = self.io[self.io_pos_offset:self.io_pos_offset + 8].view(torch.int32)
         # scratch for the decode attention partials (reused by every layer)
         self.scratch = FixedScratch(64 << 20, device)
         self.l2_prefetch = l2_prefetch
