@@ -59,6 +59,9 @@ struct GemmArgs {
     int swap;             // 1: MMA rows are C columns (C^T = B A^T)
     int tma_store;        // 1: C tiles leave through map_c
     int b_mn;             // 1: B is [K, N] (not transposed): MN-major tiles
+    int ksplit;           // K partitions per output tile (1: none)
+    float* ws;            // ksplit > 1: fp32 partial tiles [tiles][ksplit][BN][128]
+    unsigned int* cnt;    // ksplit > 1: arrivals per tile (zero before the launch; left zero)
 };
 
 // Persistent form: one CTA per SM walks output tiles t = blockIdx.x,
@@ -84,6 +87,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tfull[2], tempty[2];
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
+    __shared__ int s_last;
 
     pdl_launch_dependents();
     unsigned char* smem =
@@ -93,6 +97,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     const int ktiles = int((g.K + kBK - 1) / kBK);
     const int ntm = int((g.M + kBM - 1) / kBM), ntn = int((g.N + BN - 1) / BN);
     const int ntiles = ntm * ntn;
+    // Work units: (output tile, K partition). With split-K the partitions of
+    // a tile run on different CTAs; the last to finish sums them in order.
+    const int ks = g.ksplit;
+    const int kps = (ktiles + ks - 1) / ks;  // K tiles per partition
+    const int nunits = ntiles * ks;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -118,9 +127,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         if (lane == 0) {
             // ---- TMA producer ----
             int it = 0;
-            for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+            for (int u = blockIdx.x; u < nunits && !s_abort; u += gridDim.x) {
+                const int t = u / ks, kt0 = (u % ks) * kps;
+                const int kt1 = kt0 + kps < ktiles ? kt0 + kps : ktiles;
                 const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * BN;
-                for (int kt = 0; kt < ktiles; ++kt, ++it) {
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = uint32_t(it / kStages) & 1u;
                     if (s_abort || !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, &g_gemm_error_word)) {
@@ -147,7 +158,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             // ---- MMA issuer ----
             const uint32_t idesc = make_idesc(!g.in_f16, kBM, BN, g.b_mn != 0);
             int it = 0, lt = 0;
-            for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, ++lt) {
+            for (int u = blockIdx.x; u < nunits && !s_abort; u += gridDim.x, ++lt) {
+                const int kt0 = (u % ks) * kps;
+                const int kt1 = kt0 + kps < ktiles ? kt0 + kps : ktiles;
                 const int acc = lt & 1;
                 if (!mbar_wait(smem_u32(&tempty[acc]), (uint32_t(lt >> 1) & 1u) ^ 1u, &g_gemm_error_word)) {
                     s_abort = 1;
@@ -155,7 +168,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(acc) * ACC_COLS;
-                for (int kt = 0; kt < ktiles; ++kt, ++it) {
+                for (int kt = kt0; kt < kt1; ++kt, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = uint32_t(it / kStages) & 1u;
                     if (s_abort || !mbar_wait(smem_u32(&full[s]), ph, &g_gemm_error_word)) {
@@ -171,7 +184,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                         // swizzled row; MN-major: 16 K-rows (2048 B) further
                         const uint64_t bd = g.b_mn ? smem_desc_sw128_mn(b_base + kk * 2048, kBK * 128)
                                                    : smem_desc_sw128(b_base + kk * 32);
-                        tc_mma(d, smem_desc_sw128(a_base + kk * 32), bd, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma(d, smem_desc_sw128(a_base + kk * 32), bd, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&empty[s]));
                 }
@@ -183,7 +196,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         unsigned char* wbuf = staging + size_t(warp - 2) * BOX;
         int lt = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+        for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
+            const int t = u / ks;
             const int m0 = (t / ntn) * kBM, n0 = (t % ntn) * BN;
             const int acc = lt & 1;
             if (s_abort || !mbar_wait(smem_u32(&tfull[acc]), uint32_t(lt >> 1) & 1u, &g_gemm_error_word)) {
@@ -193,6 +207,51 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             tc_fence_after();
             const uint32_t src = tmem + uint32_t(acc) * ACC_COLS + (uint32_t(q * 32) << 16);
             const int64_t gr = int64_t(m0) + q * 32 + lane;
+            if (ks > 1) {
+                // fp32 partial tile -> workspace, column-major (lanes = rows: coalesced)
+                float* wt = g.ws + (size_t(t) * ks + (u % ks)) * size_t(BN) * kBM;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(src + uint32_t(c0), v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) wt[size_t(c0 + j) * kBM + q * 32 + lane] = v[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+                // the last partition of this tile to arrive sums all of them in order
+                named_sync(1, kEpiWarps * 32);
+                if (warp == 2 && lane == 0) {
+                    __threadfence();
+                    s_last = atomicAdd(&g.cnt[t], 1u) == unsigned(ks) - 1;
+                }
+                named_sync(1, kEpiWarps * 32);
+                if (s_last) {
+                    __threadfence();
+                    const float* w0 = g.ws + size_t(t) * ks * size_t(BN) * kBM;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < BN; c0 += 32) {
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+                        for (int sp = 0; sp < ks; ++sp) {
+                            const float* wp = w0 + size_t(sp) * BN * kBM;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] += __ldcg(wp + size_t(c0 + j) * kBM + q * 32 + lane);
+                        }
+                        if (gr < g.M) {
+                            // swapped problem: MMA row = output column gr
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + c0 + j < g.N) Elem<CT>::store(g.c, int64_t(n0 + c0 + j) * g.ldc + gr, v[j]);
+                        }
+                    }
+                    named_sync(1, kEpiWarps * 32);
+                    if (warp == 2 && lane == 0) g.cnt[t] = 0u;  // every partition has arrived
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
@@ -305,9 +364,9 @@ cudaError_t launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    const int64_t tiles = ((g.N + BN - 1) / BN) * ((g.M + kBM - 1) / kBM);
+    const int64_t units = ((g.N + BN - 1) / BN) * ((g.M + kBM - 1) / kBM) * g.ksplit;
     const int sms = current_sm_count();
-    dim3 grid(unsigned(tiles < sms ? tiles : sms));
+    dim3 grid(unsigned(units < sms ? units : sms));
     return launch_k(kern, grid, dim3(kPersistThreads), smem, s, ma, mb, mc, g);
 }
 
@@ -337,6 +396,35 @@ bool tcgen05_supports(const Matmul& p) {
            aligned16(p.b) && p.M < (int64_t(1) << 31) && p.N < (int64_t(1) << 31) && encode_fn() != nullptr;
 }
 
+// Split-K for skinny (swapped) problems: a batched-decode GEMM has few
+// 128-row weight tiles (e.g. 8 for N = 1024), so whole-K tiles would stream
+// the weights from a handful of SMs. Partitions of >= 4 K tiles are added
+// until the (tile, partition) units cover the SMs. Returns the partition
+// count (1: no split) and the output-tile count and width.
+static int ksplit_plan(const Matmul& p, int64_t* tiles_out, int* bn_out) {
+    if (p.M > 64) return 1;
+    const int bn = p.M <= 32 ? 32 : 64;
+    const int64_t tiles = ((p.N + kBM - 1) / kBM) * ((p.M + bn - 1) / bn);
+    const int64_t ktiles = (p.K + kBK - 1) / kBK;
+    const int sms = current_sm_count();
+    if (tiles_out) *tiles_out = tiles;
+    if (bn_out) *bn_out = bn;
+    if (tiles * 2 > sms || ktiles < 8) return 1;
+    int64_t ks = (sms + tiles - 1) / tiles;
+    if (ks > ktiles / 4) ks = ktiles / 4;
+    if (ks <= 1) return 1;
+    const int64_t kps = (ktiles + ks - 1) / ks;
+    return int((ktiles + kps - 1) / kps);  // no empty partition
+}
+
+size_t matmul_tcgen05_workspace(const Matmul& p) {
+    int64_t tiles = 0;
+    int bn = 0;
+    const int ks = ksplit_plan(p, &tiles, &bn);
+    if (ks <= 1) return 0;
+    return size_t(tiles) * ks * bn * kBM * 4 + size_t(tiles) * 4;
+}
+
 cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
     // Skinny M: swap so the weight rows fill the 128-row MMA side.
     const bool swap = p.M <= 64;
@@ -359,6 +447,19 @@ cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
     g.tma_store = (!swap && (p.N * ces) % 16 == 0 && aligned16(p.c) && make_out_map(&mc, p.c, p.c_dtype, p.M, p.N))
                       ? 1 : 0;
     if (!g.tma_store) mc = ma;  // unused
+    g.ksplit = 1;
+    if (p.workspace) {
+        int64_t tiles = 0;
+        const int ks = ksplit_plan(p, &tiles, nullptr);
+        if (ks > 1) {
+            g.ksplit = ks;
+            g.ws = static_cast<float*>(p.workspace);
+            g.cnt = reinterpret_cast<unsigned int*>(static_cast<char*>(p.workspace) +
+                                                    size_t(tiles) * ks * bn * kBM * 4);
+            cudaError_t e = cudaMemsetAsync(g.cnt, 0, size_t(tiles) * 4, s);
+            if (e != cudaSuccess) return e;
+        }
+    }
     switch (p.c_dtype) {
     case PC_F32: return launch_ct<TF32>(ma, mb, mc, bn, g, s);
     case PC_BF16: return launch_ct<TBF16>(ma, mb, mc, bn, g, s);

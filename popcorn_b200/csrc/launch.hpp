@@ -95,10 +95,12 @@ struct Matmul {
     int c_dtype;
     int64_t M, K, N;
     int transpose_b;
+    void* workspace = nullptr;  // tcgen05 split-K partials (matmul_tcgen05_workspace bytes) or null
 };
 cudaError_t matmul(const Matmul& p, cudaStream_t stream);
 // True when the tcgen05 tensor-core GEMM serves this problem.
 bool matmul_uses_tensor_cores(const Matmul& p);
+size_t matmul_tcgen05_workspace(const Matmul& p);
 
 // Elementwise: GeluTanh / SiLU (unary) and Mul / Add (binary).
 enum class Unary : int { kGeluTanh = 0, kSilu = 1 };

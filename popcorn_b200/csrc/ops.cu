@@ -322,7 +322,22 @@ public:
             return;
         }
         launch::Matmul p = params();
-        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::matmul(p, s); });
+        // (an encoder without a scratch allocator runs the unsplit GEMM)
+        const size_t ws =
+            enc.has_scratch() && launch::matmul_uses_tensor_cores(p) ? launch::matmul_tcgen05_workspace(p) : 0;
+        if (ws == 0) {
+            enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::matmul(p, s); });
+            return;
+        }
+        // split-K partials of a skinny tensor-core GEMM come from the scratch allocator
+        std::vector<ScratchSpec> specs = {{{int64_t(ws)}, PC_U8}};
+        enc.with_temporaries(specs, [&](const std::vector<Tensor>& t) {
+            launch::Matmul q = p;
+            q.workspace = t[0].data();
+            std::vector<Binding> b = tensors();
+            b.push_back({t[0], PC_ACCESS_READ_WRITE});
+            enc.dispatch(function_names_, b, [q](cudaStream_t s) { return launch::matmul(q, s); });
+        });
     }
 
 private:

@@ -132,6 +132,7 @@ public:
     void with_temporaries(const std::vector<ScratchSpec>& specs,
                           const std::function<void(const std::vector<Tensor>&)>& body);
 
+    bool has_scratch() const { return has_scratch_; }
     int64_t barrier_count() const { return barriers_; }
     int64_t dispatch_count() const { return dispatches_; }
     void set_hook(pc_dispatch_hook hook, void* ctx) { hook_ = hook; hook_ctx_ = ctx; }
