@@ -344,6 +344,18 @@ PC_API int pc_kernel_allreduce_add_rmsnorm(const pc_peer_group* group, int32_t b
                                            const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
                                            const pc_tensor* sum_out, const pc_tensor* norm_out, pc_kernel** kernel);
 
+/* Matmul + all-reduce + Add + RMSNorm in ONE kernel: the tensor-core GEMM of
+ * a [M,K] by w [N,K] (transposeB; M <= 64, bf16 or f16) writes its output
+ * tiles into this rank's partial buffer `buffer`; when the rank's last tile
+ * is stored it publishes the partial, and the same kernel then sums every
+ * rank's rows over peer memory and applies Add(residual) and RMSNorm as
+ * pc_kernel_allreduce_add_rmsnorm does (residual / outputs [M, N]). */
+PC_API int pc_kernel_matmul_allreduce_add_rmsnorm(const pc_tensor* a, const pc_tensor* w, const pc_peer_group* group,
+                                                  int32_t buffer, const pc_tensor* residual,
+                                                  const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                                                  const pc_tensor* sum_out, const pc_tensor* norm_out,
+                                                  pc_kernel** kernel);
+
 /* ---- fused decode step (extension) ---------------------------------------- */
 
 /* One decode layer's weights and KV caches (device pointers). Weights are

@@ -127,6 +127,8 @@ def _declare(L):
         "pc_ipc_open_handle": ([ctypes.POINTER(ctypes.c_uint8), PP], I),
         "pc_ipc_close_handle": ([P], I),
         "pc_kernel_allreduce_add_rmsnorm": ([ctypes.POINTER(pc_peer_group), I32, T, T, F, I32, T, T, PP], I),
+        "pc_kernel_matmul_allreduce_add_rmsnorm": ([T, T, ctypes.POINTER(pc_peer_group), I32, T, T, F, I32, T, T, PP],
+                                                   I),
         "pc_kernel_gated_activation": ([T, I32, T, PP], I),
         "pc_kernel_add_rmsnorm": ([T, T, T, F, I32, T, T, PP], I),
         "pc_flash_decoding_noalloc": ([T, T, T, T, T, F, M, P], I),

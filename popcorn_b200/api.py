@@ -556,6 +556,21 @@ class Kernels:
                              _tc(sum_out), _tc(norm_out), keep=_keep(group, residual, norm_weight, sum_out, norm_out))
 
 
+class _MatmulAllReduceAddRMSNorm(Kernel):
+    """Extension: Matmul (a . w^T, M <= 64, tensor cores) into this rank's
+    PeerGroup partial buffer, then the all-reduce + Add + RMSNorm, in ONE
+    kernel."""
+
+    def __init__(self, a, w, group, buffer, residual, norm_weight, sum_out, norm_out, eps=1e-6,
+                 add_one_to_weight=False):
+        super().__init__(N.lib().pc_kernel_matmul_allreduce_add_rmsnorm, _tc(a), _tc(w), ctypes.byref(group.c),
+                         int(buffer), _tc(residual), _tc(norm_weight), ctypes.c_float(eps), int(add_one_to_weight),
+                         _tc(sum_out), _tc(norm_out), keep=_keep(a, w, group, residual, norm_weight, sum_out, norm_out))
+
+
+Kernels.MatmulAllReduceAddRMSNorm = _MatmulAllReduceAddRMSNorm
+
+
 class PeerGroup:
     """The tensor-parallel ranks' partial-sum buffers and control blocks,
     shared through CUDA IPC (one process per GPU on one node).

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "dtype.cuh"
 #include "launch.hpp"
+#include "peer_reduce.cuh"
 #include "popcorn.hpp"
 
 namespace popcorn {
@@ -37,137 +38,36 @@ namespace launch {
 
 namespace {
 
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint4 ld_volatile16(const void* p) {
-    uint4 v;
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p)
-                 : "memory");
-    return v;
-}
-
 constexpr int kArThreads = 256;
-constexpr int kArVec = 8;        // 16-bit elements per 16-byte chunk
-constexpr int kArMaxChunks = 4;  // chunks per thread: rows up to 8192 elements
 
 template <class T>
 __global__ void __launch_bounds__(kArThreads) allreduce_add_rmsnorm_kernel(const PeerAllReduce p) {
     pdl_wait();
     __shared__ float red[kArThreads / 32];
-    __shared__ float s_scale;
     __shared__ int s_ok;
     __shared__ unsigned int s_epoch;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int b = p.buffer;
-    unsigned int* my_ctl = p.ctl[p.rank];  // [0..1] flags, [2..3] epochs, [4] CTA count
+    unsigned int* my_ctl = p.ctl[p.rank];
     if (tid == 0) {
-        const unsigned int e = my_ctl[2 + b] + 1u;
+        const unsigned int e = my_ctl[kCtlEpoch + b] + 1u;
         s_epoch = e;
         if (blockIdx.x == 0) {
+            // this rank's partial was written by the preceding kernel
             __threadfence_system();
-            st_release_sys(&my_ctl[b], e);
+            pr_st_release_sys(&my_ctl[kCtlFlag + b], e);
         }
-        // wait for every rank's partial of this call
-        int ok = 1;
-        for (int r = 0; r < p.world && ok; ++r) {
-            long i = 0;
-            while (ld_acquire_sys(&p.ctl[r][b]) < e) {
-                if (++i > (1l << 22)) {
-                    atomicOr(&g_allreduce_error_word, 8u);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        s_ok = ok;
+        s_ok = pr_wait_peers(p, e, &g_allreduce_error_word) ? 1 : 0;
     }
     __syncthreads();
-    const int64_t row = blockIdx.x;
-    const int64_t H = p.H;
-    const int nchunks = int(H / kArVec);
-    float acc[kArMaxChunks][kArVec];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < kArMaxChunks; ++j) {
-        const int c = tid + j * kArThreads;
-        if (c >= nchunks) continue;
-        float o[kArVec];
-#pragma unroll
-        for (int e = 0; e < kArVec; ++e) o[e] = 0.f;
-        if (s_ok) {
-            for (int r = 0; r < p.world; ++r) {
-                const uint4 w = ld_volatile16(static_cast<const char*>(p.partial[r][b]) + (row * H + int64_t(c) * kArVec) * 2);
-                float f[kArVec];
-                unpack8<T>(w, f);
-#pragma unroll
-                for (int e = 0; e < kArVec; ++e) o[e] += f[e];
-            }
-        }
-        const uint4 rw = *reinterpret_cast<const uint4*>(static_cast<const char*>(p.residual) + (row * H + int64_t(c) * kArVec) * 2);
-        float res[kArVec];
-        unpack8<T>(rw, res);
-#pragma unroll
-        for (int e = 0; e < kArVec; ++e) {
-            const float s = Elem<T>::round(res[e] + Elem<T>::round(o[e]));
-            acc[j][e] = s;
-            ss += s * s;
-        }
-        uint4 so;
-        so.x = pack2<T>(acc[j][0], acc[j][1]);
-        so.y = pack2<T>(acc[j][2], acc[j][3]);
-        so.z = pack2<T>(acc[j][4], acc[j][5]);
-        so.w = pack2<T>(acc[j][6], acc[j][7]);
-        *reinterpret_cast<uint4*>(static_cast<char*>(p.sum_out) + (row * H + int64_t(c) * kArVec) * 2) = so;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (warp == 0) {
-        float v = lane < kArThreads / 32 ? red[lane] : 0.f;
-        v = warp_sum(v);
-        if (lane == 0) s_scale = rsqrtf(v / float(H) + p.eps);
-    }
-    __syncthreads();
-    const float scale = s_scale;
-#pragma unroll
-    for (int j = 0; j < kArMaxChunks; ++j) {
-        const int c = tid + j * kArThreads;
-        if (c >= nchunks) continue;
-        float v[kArVec];
-#pragma unroll
-        for (int e = 0; e < kArVec; ++e) {
-            float x = acc[j][e] * scale;
-            if (p.weight) {
-                float w = p.weight[c * kArVec + e];
-                if (p.add_one) w = 1.0f + w;
-                x *= w;
-            }
-            v[e] = x;
-        }
-        uint4 no;
-        no.x = pack2<T>(v[0], v[1]);
-        no.y = pack2<T>(v[2], v[3]);
-        no.z = pack2<T>(v[4], v[5]);
-        no.w = pack2<T>(v[6], v[7]);
-        *reinterpret_cast<uint4*>(static_cast<char*>(p.norm_out) + (row * H + int64_t(c) * kArVec) * 2) = no;
-    }
+    pr_reduce_row<T, kArThreads>(p, blockIdx.x, s_ok != 0, tid, red, [] { __syncthreads(); });
     // the last CTA out advances this rank's epoch for buffer b
-    __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const unsigned int done = atomicAdd(&my_ctl[4], 1u);
+        const unsigned int done = atomicAdd(&my_ctl[kCtlExit], 1u);
         if (done == gridDim.x - 1) {
-            my_ctl[4] = 0u;
-            my_ctl[2 + b] = s_epoch;
+            my_ctl[kCtlExit] = 0u;
+            my_ctl[kCtlEpoch + b] = s_epoch;
             __threadfence();
         }
     }
@@ -176,7 +76,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_add_rmsnorm_kernel(const
 }  // namespace
 
 bool peer_allreduce_supports(const PeerAllReduce& p) {
-    return (p.dtype == PC_BF16 || p.dtype == PC_F16) && p.H % kArVec == 0 && p.H <= kArVec * kArMaxChunks * kArThreads &&
+    return (p.dtype == PC_BF16 || p.dtype == PC_F16) && p.H % kPrVec == 0 && p.H <= 8192 &&
            p.world >= 1 && p.world <= kMaxPeers && p.rank >= 0 && p.rank < p.world && (p.buffer == 0 || p.buffer == 1);
 }
 

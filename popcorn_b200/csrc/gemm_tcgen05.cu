@@ -35,6 +35,7 @@
 #include "tcgen05.cuh"
 #include "dtype.cuh"
 #include "launch.hpp"
+#include "peer_reduce.cuh"
 #include "popcorn.hpp"
 
 namespace popcorn {
@@ -62,6 +63,8 @@ struct GemmArgs {
     int ksplit;           // K partitions per output tile (1: none)
     float* ws;            // ksplit > 1: fp32 partial tiles [tiles][ksplit][BN][128]
     unsigned int* cnt;    // ksplit > 1: arrivals per tile (zero before the launch; left zero)
+    int fuse_ar;          // 1: C is this rank's peer partial buffer; all-reduce + Add + RMSNorm follow
+    PeerAllReduce ar;
 };
 
 // Persistent form: one CTA per SM walks output tiles t = blockIdx.x,
@@ -88,6 +91,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
     __shared__ int s_last;
+    __shared__ unsigned int s_ar_epoch;
+    __shared__ int s_ar_ok;
+    __shared__ float s_red[kEpiWarps];
 
     pdl_launch_dependents();
     unsigned char* smem =
@@ -194,6 +200,22 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     } else {
         // ---- epilogue warps ----
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        unsigned int* own_ctl = g.fuse_ar ? g.ar.ctl[g.ar.rank] : nullptr;
+        // A finished output tile of this rank's partial; the last one publishes
+        // the partial to the peers (system-scope release of this call's epoch).
+        auto tile_done = [&]() {
+            __threadfence();
+            const unsigned int old = atomicAdd(&own_ctl[kCtlTiles + g.ar.buffer], 1u);
+            if (old == unsigned(ntiles) - 1) {
+                own_ctl[kCtlTiles + g.ar.buffer] = 0u;
+                __threadfence_system();
+                pr_st_release_sys(&own_ctl[kCtlFlag + g.ar.buffer], s_ar_epoch);
+            }
+        };
+        if (g.fuse_ar) {
+            if (warp == 2 && lane == 0) s_ar_epoch = own_ctl[kCtlEpoch + g.ar.buffer] + 1u;
+            named_sync(1, kEpiWarps * 32);
+        }
         unsigned char* wbuf = staging + size_t(warp - 2) * BOX;
         int lt = 0;
         for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++lt) {
@@ -248,7 +270,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                         }
                     }
                     named_sync(1, kEpiWarps * 32);
-                    if (warp == 2 && lane == 0) g.cnt[t] = 0u;  // every partition has arrived
+                    if (warp == 2 && lane == 0) {
+                        g.cnt[t] = 0u;  // every partition has arrived
+                        if (g.fuse_ar) tile_done();
+                    }
                 }
                 continue;
             }
@@ -294,13 +319,38 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+            if (g.fuse_ar) {
+                named_sync(1, kEpiWarps * 32);  // all rows of the tile stored
+                if (warp == 2 && lane == 0) tile_done();
+            }
         }
         if (g.tma_store && lane == 0) bulk_wait_read<0>();
+        if (g.fuse_ar) {
+            // all-reduce of the rows, then Add + RMSNorm (rows spread over the CTAs)
+            if (warp == 2 && lane == 0) s_ar_ok = pr_wait_peers(g.ar, s_ar_epoch, &g_gemm_error_word) ? 1 : 0;
+            named_sync(1, kEpiWarps * 32);
+            const bool ok = s_ar_ok != 0 && !s_abort;
+            if constexpr (sizeof(typename CT::storage) == 2) {  // 16-bit partials only
+                for (int64_t r = blockIdx.x; r < g.ar.rows; r += gridDim.x)
+                    pr_reduce_row<CT, kEpiWarps * 32>(g.ar, r, ok, tid - 64, s_red,
+                                                       [] { named_sync(1, kEpiWarps * 32); });
+            }
+        }
     }
     __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+    if (g.fuse_ar && tid == 0) {
+        // the last CTA out records this call's epoch for the buffer
+        unsigned int* own_ctl = g.ar.ctl[g.ar.rank];
+        __threadfence();
+        if (atomicAdd(&own_ctl[kCtlExit], 1u) == gridDim.x - 1) {
+            own_ctl[kCtlExit] = 0u;
+            own_ctl[kCtlEpoch + g.ar.buffer] = s_ar_epoch;
+            __threadfence();
+        }
+    }
 }
 
 // ---- host: tensor maps ----------------------------------------------------------
@@ -425,7 +475,27 @@ size_t matmul_tcgen05_workspace(const Matmul& p) {
     return size_t(tiles) * ks * bn * kBM * 4 + size_t(tiles) * 4;
 }
 
-cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
+static cudaError_t matmul_tcgen05_impl(const Matmul& p, const PeerAllReduce* ar, cudaStream_t s);
+
+cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) { return matmul_tcgen05_impl(p, nullptr, s); }
+
+// The skinny (swapped) form serves any 1 <= M <= 64: rows past M are the
+// TMA's zero fill and are never stored.
+bool tcgen05_supports_skinny(const Matmul& p) {
+    Matmul q = p;
+    q.M = 16;
+    return p.M >= 1 && p.M <= 64 && p.transpose_b && tcgen05_supports(q);
+}
+
+// The skinny GEMM writing this rank's partial (p.c = its peer buffer), then
+// the all-reduce + Add + RMSNorm of `ar` in the same kernel.
+cudaError_t matmul_tcgen05_allreduce(const Matmul& p, const PeerAllReduce& ar, cudaStream_t s) {
+    if (p.M > 64 || p.c_dtype != p.a_dtype || !peer_allreduce_supports(ar) || ar.rows != p.M || ar.H != p.N)
+        return cudaErrorInvalidValue;
+    return matmul_tcgen05_impl(p, &ar, s);
+}
+
+static cudaError_t matmul_tcgen05_impl(const Matmul& p, const PeerAllReduce* ar, cudaStream_t s) {
     // Skinny M: swap so the weight rows fill the 128-row MMA side.
     const bool swap = p.M <= 64;
     GemmArgs g{};
@@ -448,6 +518,10 @@ cudaError_t matmul_tcgen05(const Matmul& p, cudaStream_t s) {
                       ? 1 : 0;
     if (!g.tma_store) mc = ma;  // unused
     g.ksplit = 1;
+    if (ar) {
+        g.fuse_ar = 1;
+        g.ar = *ar;
+    }
     if (p.workspace) {
         int64_t tiles = 0;
         const int ks = ksplit_plan(p, &tiles, nullptr);

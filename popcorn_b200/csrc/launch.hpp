@@ -203,6 +203,11 @@ struct PeerAllReduce {
     int add_one;
 };
 bool peer_allreduce_supports(const PeerAllReduce& p);
+// tcgen05 skinny GEMM (M <= 64, transposeB) whose output is this rank's
+// partial buffer, followed in the same kernel by the all-reduce + Add +
+// RMSNorm of `ar` (rows = M, H = N).
+cudaError_t matmul_tcgen05_allreduce(const Matmul& p, const PeerAllReduce& ar, cudaStream_t stream);
+bool tcgen05_supports_skinny(const Matmul& p);
 cudaError_t peer_allreduce_add_rmsnorm(const PeerAllReduce& p, cudaStream_t stream);
 
 // One persistent kernel for a batch-1 decode step through a layer stack

@@ -747,6 +747,101 @@ private:
     launch::PeerAllReduce p_{};
 };
 
+// The peer all-reduce parameters from a group descriptor (validated).
+launch::PeerAllReduce peer_params(const pc_peer_group* g, int buffer, const Tensor& res, const Tensor* w, float eps,
+                                  bool add_one, const Tensor& sum, const Tensor& norm) {
+    if (!g) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group is null.");
+    const int dt = res.dtype();
+    if ((dt != PC_BF16 && dt != PC_F16) || sum.dtype() != dt || norm.dtype() != dt)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "peer all-reduce serves bf16 or f16.");
+    if (!res.same_shape(sum) || !res.same_shape(norm) || res.rank() < 1)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "residual, sum and norm outputs must have one shape.");
+    if (g->world < 1 || g->world > PC_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group: bad world / rank.");
+    launch::PeerAllReduce p{};
+    for (int r = 0; r < g->world; ++r) {
+        if (!g->partial[r][0] || !g->partial[r][1] || !g->control[r])
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer group: missing buffer of rank " + std::to_string(r) + ".");
+        p.partial[r][0] = g->partial[r][0];
+        p.partial[r][1] = g->partial[r][1];
+        p.ctl[r] = g->control[r];
+    }
+    const int64_t H = res[res.rank() - 1];
+    if (w) {
+        if (w->dtype() != PC_F32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32.");
+        require_elements(*w, H, "all-reduce norm weight");
+    }
+    p.rank = g->rank;
+    p.world = g->world;
+    p.buffer = buffer;
+    p.residual = res.data();
+    p.sum_out = sum.data();
+    p.norm_out = norm.data();
+    p.weight = w ? static_cast<const float*>(w->data()) : nullptr;
+    p.dtype = dt;
+    p.rows = res.element_count() / H;
+    p.H = H;
+    p.eps = eps;
+    p.add_one = add_one ? 1 : 0;
+    if (!launch::peer_allreduce_supports(p))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "peer all-reduce: H must be a multiple of 8 and <= 8192, buffer 0 or 1.");
+    return p;
+}
+
+class MatmulAllReduceKernel : public Kernel {
+public:
+    MatmulAllReduceKernel(Tensor a, Tensor w, const pc_peer_group* g, int buffer, Tensor res, const Tensor* nw,
+                          float eps, bool add_one, Tensor sum, Tensor norm)
+        : a_(a), w_(w), res_(res), sum_(sum), norm_(norm) {
+        ar_ = peer_params(g, buffer, res, nw, eps, add_one, sum, norm);
+        if (nw) {
+            nw_ = *nw;
+            has_nw_ = true;
+        }
+        if (a.rank() != 2 || w.rank() != 2 || a[1] != w[1] || ar_.rows != a[0] || ar_.H != w[0])
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "MatmulAllReduce wants a [M,K], w [N,K], residual [M,N]; got a " +
+                                                   a.shape_string() + ", w " + w.shape_string() + ".");
+        if (a.dtype() != res.dtype() || w.dtype() != a.dtype())
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "MatmulAllReduce needs one 16-bit dtype.");
+        mm_ = launch::Matmul{a.data(), a.dtype(), w.data(), w.dtype(), const_cast<void*>(ar_.partial[ar_.rank][buffer]),
+                             a.dtype(), a[0], a[1], w[0], 1};
+        if (!launch::tcgen05_supports_skinny(mm_))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "MatmulAllReduce serves the tensor-core GEMM with M <= 64, K % 8 == 0.");
+        function_names_ = "matmul_tc_bf16_tb";
+    }
+    const char* name() const override { return "MatmulAllReduceAddRMSNorm"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{a_, PC_ACCESS_READ}, {w_, PC_ACCESS_READ}, {res_, PC_ACCESS_READ},
+                                  {sum_, PC_ACCESS_WRITE}, {norm_, PC_ACCESS_WRITE}};
+        if (has_nw_) v.push_back({nw_, PC_ACCESS_READ});
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::Matmul p = mm_;
+        launch::PeerAllReduce ar = ar_;
+        const size_t ws = enc.has_scratch() ? launch::matmul_tcgen05_workspace(p) : 0;
+        if (ws == 0) {
+            enc.dispatch(function_names_, tensors(),
+                         [p, ar](cudaStream_t s) { return launch::matmul_tcgen05_allreduce(p, ar, s); });
+            return;
+        }
+        std::vector<ScratchSpec> specs = {{{int64_t(ws)}, PC_U8}};
+        enc.with_temporaries(specs, [&](const std::vector<Tensor>& t) {
+            launch::Matmul q = p;
+            q.workspace = t[0].data();
+            std::vector<Binding> b = tensors();
+            b.push_back({t[0], PC_ACCESS_READ_WRITE});
+            enc.dispatch(function_names_, b, [q, ar](cudaStream_t s) { return launch::matmul_tcgen05_allreduce(q, ar, s); });
+        });
+    }
+
+private:
+    Tensor a_, w_, res_, sum_, norm_, nw_;
+    bool has_nw_ = false;
+    launch::Matmul mm_{};
+    launch::PeerAllReduce ar_{};
+};
+
 // ---------------------------------------------------------------------------
 // Fused decode step (decode_step.cu)
 // ---------------------------------------------------------------------------
@@ -1177,6 +1272,21 @@ int pc_kernel_allreduce_add_rmsnorm(const pc_peer_group* group, int32_t buffer, 
     return wrap(std::make_unique<PeerAllReduceKernel>(group, buffer, tensor_arg(residual, "residual"),
                                                       norm_weight ? &nw : nullptr, eps, add_one_to_weight != 0,
                                                       tensor_arg(sum_out, "sum_out"), tensor_arg(norm_out, "norm_out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_matmul_allreduce_add_rmsnorm(const pc_tensor* a, const pc_tensor* w, const pc_peer_group* group,
+                                           int32_t buffer, const pc_tensor* residual, const pc_tensor* norm_weight,
+                                           float eps, int32_t add_one_to_weight, const pc_tensor* sum_out,
+                                           const pc_tensor* norm_out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(std::make_unique<MatmulAllReduceKernel>(tensor_arg(a, "a"), tensor_arg(w, "w"), group, buffer,
+                                                        tensor_arg(residual, "residual"), norm_weight ? &nw : nullptr,
+                                                        eps, add_one_to_weight != 0, tensor_arg(sum_out, "sum_out"),
+                                                        tensor_arg(norm_out, "norm_out")),
                 kernel);
     PC_GUARD_END
 }

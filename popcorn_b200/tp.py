@@ -137,13 +137,14 @@ class TPDecodeModel:
         self.peer = None
         self._ks = None
 
-    def use_peer_allreduce(self, all_gather):
+    def use_peer_allreduce(self, all_gather, fuse_gemm=True):
         """Switches the two all-reduces per layer from the caller's collective
         to the one-shot peer-memory kernel fused with Add + RMSNorm
         (Kernels.AllReduceAddRMSNorm). `all_gather(bytes) -> [bytes]` exchanges
         the IPC handles once (every rank calls this together)."""
         s = self.s
         self.peer = PeerGroup(self.device, self.world, self.rank, s.B, s.H, s.dtype, all_gather)
+        self.fuse_gemm = fuse_gemm
         self._ks = None
 
     def kernels(self):
@@ -156,11 +157,20 @@ class TPDecodeModel:
         o_a = peer.partial(0) if peer else self.o  # o_proj partial sum
         o_b = peer.partial(1) if peer else self.o  # down_proj partial sum
 
-        def reduce_add_norm(buf, part, residual, weight, sum_out):
+        fuse = peer is not None and getattr(self, "fuse_gemm", False) and s.B <= 64
+
+        def gemm_reduce_add_norm(a, w, buf, part, residual, weight, sum_out):
+            """The partial-sum GEMM and its all-reduce + Add + RMSNorm: one
+            kernel (fused), GEMM + peer kernel, or GEMM + collective + AddRMSNorm."""
+            if fuse:
+                return [K.MatmulAllReduceAddRMSNorm(a, w, peer, buf, residual, weight, sum_out, self.xn, eps=s.eps,
+                                                    add_one_to_weight=True)]
+            ks = [K.Matmul(a, w, into=part, transpose_b=True)]
             if peer:
-                return [K.AllReduceAddRMSNorm(peer, buf, residual, weight, sum_out, self.xn, eps=s.eps,
-                                              add_one_to_weight=True)]
-            return [None, K.AddRMSNorm(residual, part, weight, sum_out, self.xn, eps=s.eps, add_one_to_weight=True)]
+                return ks + [K.AllReduceAddRMSNorm(peer, buf, residual, weight, sum_out, self.xn, eps=s.eps,
+                                                   add_one_to_weight=True)]
+            return ks + [None, K.AddRMSNorm(residual, part, weight, sum_out, self.xn, eps=s.eps,
+                                            add_one_to_weight=True)]
 
         ks = [K.RMSNorm(self.x, self.layers[0]["attn_norm"], into=self.xn, eps=s.eps, add_one_to_weight=True)]
         for i, w in enumerate(self.layers):
@@ -168,13 +178,12 @@ class TPDecodeModel:
             ks += [K.Matmul(self.xn, w["w_qkv"], into=self.qkv, transpose_b=True),
                    K.QKVScatter(self.qkv, self.q, w["k_cache"], w["v_cache"], offset=s.ctx - 1),
                    K.FlashDecodingRagged(self.q, w["k_cache"], w["v_cache"], self.lens, into=self.attn,
-                                         scale=s.scale, mask=AttentionMask.causal),
-                   K.Matmul(self.attn.view(s.B, self.nq * s.Hd), w["w_o"], into=o_a, transpose_b=True)]
-            ks += reduce_add_norm(0, o_a, self.x, w["mlp_norm"], self.h)
+                                         scale=s.scale, mask=AttentionMask.causal)]
+            ks += gemm_reduce_add_norm(self.attn.view(s.B, self.nq * s.Hd), w["w_o"], 0, o_a, self.x, w["mlp_norm"],
+                                       self.h)
             ks += [K.Matmul(self.xn, w["w_gu"], into=self.gu, transpose_b=True),
-                   K.GatedActivation(self.gu, self.act),
-                   K.Matmul(self.act, w["w_down"], into=o_b, transpose_b=True)]
-            ks += reduce_add_norm(1, o_b, self.h, nxt_norm, self.x)
+                   K.GatedActivation(self.gu, self.act)]
+            ks += gemm_reduce_add_norm(self.act, w["w_down"], 1, o_b, self.h, nxt_norm, self.x)
         ks += [K.Matmul(self.xn, self.lm_head, into=self.logits, transpose_b=True)]
         self._ks = ks
         return ks

@@ -174,20 +174,24 @@ def test_peer_allreduce_world1(pc, enc, dt):
     g.close()
 
 
-def test_tp_model_one_rank_peer_allreduce(pc):
-    """The TP model with the fused peer all-reduce (one rank) against the
-    oracle step, as test_tp_model_one_rank_matches_oracle."""
+@pytest.mark.parametrize("fuse_gemm", [False, True])
+def test_tp_model_one_rank_peer_allreduce(pc, fuse_gemm):
+    """The TP model with the peer all-reduce (one rank) against the oracle
+    step, as test_tp_model_one_rank_matches_oracle: the all-reduce as its own
+    kernel after the GEMM, or fused into the GEMM (one kernel)."""
     from popcorn_b200.tp import TPDecodeModel, TPShape
     dt = "bf16"
     shape = TPShape(hidden=512, q_heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=2048, layers=2, batch=4,
                     ctx=96, dtype=dt)
     m = TPDecodeModel(pc.KernelLibrary(0), shape, seed=3)
-    m.use_peer_allreduce(lambda b: [b])
+    m.use_peer_allreduce(lambda b: [b], fuse_gemm=fuse_gemm)
     m.x.normal_(generator=torch.Generator(device="cuda").manual_seed(1))
     host = {"x": from_dev(m.x, dt), "final_norm": m.final_norm.cpu().numpy(), "lm_head": from_dev(m.lm_head, dt),
             "layers": [{k: (v.cpu().numpy() if v.dtype == torch.float32 else from_dev(v, dt)) for k, v in w.items()}
                        for w in m.layers]}
     enc = m.encoder()
+    names = [k.name for k in m.kernels() if k is not None]
+    assert ("MatmulAllReduceAddRMSNorm" in names) == fuse_gemm
     m.step(enc, lambda t: pytest.fail("no collective on the peer path"))
     torch.cuda.synchronize()
     exp = _oracle_step(m, host, dt)
