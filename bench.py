@@ -335,14 +335,14 @@ def run_tp(args):
     hbm_gbs, _, peak_kind = peaks()
     shape = TPShape(layers=args.tp_layers)
     model = TPDecodeModel(pc.KernelLibrary(local), shape, rank=rank, world=world, seed=5, device=local)
-    if args.allreduce in ("peer", "peer-separate"):
+    if args.allreduce in ("peer", "peer-fused"):
         def all_gather(blob):
             if world == 1:
                 return [blob]
             out = [None] * world
             dist.all_gather_object(out, blob)
             return out
-        model.use_peer_allreduce(all_gather, fuse_gemm=args.allreduce == "peer")
+        model.use_peer_allreduce(all_gather, fuse_gemm=args.allreduce == "peer-fused")
     stream = torch.cuda.Stream(device=local)
 
     def all_reduce(t):
@@ -418,9 +418,9 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill"])
     ap.add_argument("--tp-layers", type=int, default=42)
-    ap.add_argument("--allreduce", default="peer", choices=["peer", "peer-separate", "nccl"],
-                    help="tp9b: all-reduce over peer memory fused into the o_proj / down GEMM with Add + RMSNorm "
-                         "(peer), the same as a separate kernel after the GEMM (peer-separate), or NCCL")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "peer-fused", "nccl"],
+                    help="tp9b: all-reduce over peer memory with Add + RMSNorm as one kernel after the GEMM "
+                         "(peer), the same fused into the o_proj / down GEMM (peer-fused), or NCCL")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="config-2 stack depth (26 for the bench line; fewer for small profiling captures)")
     args = ap.parse_args()

@@ -19,6 +19,8 @@
 // shared memory, split into two float4 planes (elements 0-3 / 4-7 of every
 // 16-byte chunk) so a warp's x reads are conflict-free. Rows whose length
 // is not a multiple of 16 bytes use a plain one-warp-per-row kernel.
+#include <cstdlib>
+
 #include "async.cuh"
 #include "common.cuh"
 #include "dtype.cuh"
@@ -346,7 +348,21 @@ cudaError_t run_scalar(const Gemv& p, cudaStream_t s) {
     return launch_k(kern, dim3(unsigned(grid)), dim3(kThreads), smem, s, p);
 }
 
-constexpr size_t kTmaSmemBudget = 200 * 1024;
+constexpr size_t kTmaSmemBudget = 200 * 1024;  // upper bound (the attribute set once per kernel)
+
+// Shared memory a CTA may use for its ring and activation planes.
+// POPCORN_GEMV_SMEM_KB overrides the default (tuning).
+size_t gemv_smem_budget() {
+    static size_t b = [] {
+        size_t v = kTmaSmemBudget;
+        if (const char* e = getenv("POPCORN_GEMV_SMEM_KB")) {
+            const long kb = atol(e);
+            if (kb >= 32 && size_t(kb) * 1024 <= kTmaSmemBudget) v = size_t(kb) * 1024;
+        }
+        return v;
+    }();
+    return b;
+}
 
 bool make_plan(const Gemv& p, GemvPlan& g) {
     const int es = dtype_stride(p.w_dtype);
@@ -362,8 +378,9 @@ bool make_plan(const Gemv& p, GemvPlan& g) {
     g.ntiles = int((p.N + 7) / 8);
     g.stage_bytes = int(8 * kc * es);
     size_t xbytes = size_t(K) * 4;
-    if (xbytes + 2 * size_t(g.stage_bytes) > kTmaSmemBudget) return false;
-    g.stages = int((kTmaSmemBudget - xbytes) / g.stage_bytes);
+    const size_t budget = gemv_smem_budget();
+    if (xbytes + 2 * size_t(g.stage_bytes) > budget) return false;
+    g.stages = int((budget - xbytes) / g.stage_bytes);
     if (g.stages > 8) g.stages = 8;
     return g.stages >= 2;
 }

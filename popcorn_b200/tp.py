@@ -137,11 +137,15 @@ class TPDecodeModel:
         self.peer = None
         self._ks = None
 
-    def use_peer_allreduce(self, all_gather, fuse_gemm=True):
+    def use_peer_allreduce(self, all_gather, fuse_gemm=False):
         """Switches the two all-reduces per layer from the caller's collective
         to the one-shot peer-memory kernel fused with Add + RMSNorm
         (Kernels.AllReduceAddRMSNorm). `all_gather(bytes) -> [bytes]` exchanges
-        the IPC handles once (every rank calls this together)."""
+        the IPC handles once (every rank calls this together). With
+        fuse_gemm the o_proj / down GEMM and the all-reduce are one kernel
+        (Kernels.MatmulAllReduceAddRMSNorm); at batch 32 that measured slower
+        (TP2 2145 vs 2229 tok/s: the GEMM's grid waits on the peers instead
+        of letting the next kernel start), so it is off by default."""
         s = self.s
         self.peer = PeerGroup(self.device, self.world, self.rank, s.B, s.H, s.dtype, all_gather)
         self.fuse_gemm = fuse_gemm

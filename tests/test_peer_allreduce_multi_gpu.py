@@ -73,7 +73,7 @@ def _worker(rank, world, port, out_dir):
     m.step(enc2, lambda t: dist.all_reduce(t))
     torch.cuda.synchronize()
     nccl_logits = m.logits.float().cpu().numpy()
-    m.use_peer_allreduce(all_gather)
+    m.use_peer_allreduce(all_gather, fuse_gemm=True)
     m.x.copy_(x0)
     m.step(enc2, lambda t: None)
     torch.cuda.synchronize()
