@@ -250,6 +250,12 @@ PC_API int pc_kernel_gelu_tanh(const pc_tensor* x, const pc_tensor* out, pc_kern
 PC_API int pc_kernel_mul(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel);
 /* Kernels.Add(_:_:into:), Add.swift. */
 PC_API int pc_kernel_add(const pc_tensor* a, const pc_tensor* b, const pc_tensor* out, pc_kernel** kernel);
+/* Kernels.Argmax(_:indices:axis:), Argmax.swift:24-37 (axis -1 only): int32
+ * index of the largest element of each row, ties to the lowest index, NaN
+ * never wins (Argmax.metal:7-76). x f32 (reference); f16 / bf16 are an
+ * extension (compared as their exact f32 values). Long rows use caller
+ * scratch for their partial winners. */
+PC_API int pc_kernel_argmax(const pc_tensor* x, const pc_tensor* indices, int32_t axis, pc_kernel** kernel);
 /* Extension: SiLU, silu(g) = g / (1 + exp(-g)) (no reference kernel). */
 PC_API int pc_kernel_silu(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel);
 

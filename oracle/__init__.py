@@ -42,6 +42,7 @@ def _declare(L):
         "or_rmsnorm": [P, I, P, P, I, L64, L64, F, I, I],
         "or_matvec_nk": [P, I, P, I, P, I, L64, L64],
         "or_matmul": [P, I, P, I, P, I, L64, L64, L64, I],
+        "or_argmax": [P, I, L64, L64, P],
         "or_gelu_tanh": [P, I, P, I, L64],
         "or_silu": [P, I, P, I, L64],
         "or_mul": [P, P, P, I, L64],
@@ -163,6 +164,17 @@ def add(a, b, dt):
     a, b = _c(a), _c(b)
     out = np.empty(a.shape, dtype=NP[dt])
     lib().or_add(_p(a), _p(b), _p(out), DT[dt], a.size)
+    return out
+
+
+def argmax(x, dt):
+    """Argmax.metal:5-76 over the last axis: int32 index per row (ties -> the
+    lowest index; NaN never wins; a row of NaN gives 0x7fffffff for n >= 32)."""
+    x = _c(x)
+    N = x.shape[-1]
+    rows = x.size // N
+    out = np.empty(x.shape[:-1], dtype=np.int32)
+    lib().or_argmax(_p(x), DT[dt], rows, N, _p(out))
     return out
 
 

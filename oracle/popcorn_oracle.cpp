@@ -16,6 +16,8 @@
 //   or_matmul              Sources/Popcorn/Kernels/Matmul.metal:7-27
 //   or_gelu_tanh           Sources/Popcorn/Kernels/GeluTanh.metal:6-35
 //   or_mul / or_add        Sources/Popcorn/Kernels/Mul.metal:7-25, Add.metal:7-25
+//   or_argmax              Sources/Popcorn/Kernels/Argmax.metal:5-76, routing
+//                          Argmax.swift:21 (n >= 32 -> argmax_row)
 //   or_flash_decoding      Sources/Popcorn/Kernels/FlashDecoding.metal:29-231
 //                          with P = 8 from Kernels/FlashDecoding.swift:77
 //   or_flash_attention     Sources/Popcorn/Kernels/FlashAttention.metal:31-162
@@ -263,6 +265,39 @@ void or_mul(const void* a, const void* b, void* out, int dt, int64_t n) {
 
 void or_add(const void* a, const void* b, void* out, int dt, int64_t n) {
     for (int64_t i = 0; i < n; ++i) store(out, dt, i, load(a, dt, i) + load(b, dt, i));
+}
+
+// Argmax.metal:7-9: a candidate wins on a larger value, or an equal value at
+// a lower index (NaN never wins: both comparisons are false).
+static bool argmax_better(float cv, int32_t ci, float bv, int32_t bi) { return cv > bv || (cv == bv && ci < bi); }
+
+// Per row of x [rows, N]: n < 32 follows `argmax` (:11-27, starts from
+// element 0), n >= 32 follows `argmax_row` (:29-76, starts from (-inf,
+// 0x7fffffff)); the reduction order of argmax_row does not change the result
+// because the order relation above is total on non-NaN values.
+void or_argmax(const void* x, int dt, int64_t rows, int64_t N, int32_t* out) {
+    for (int64_t r = 0; r < rows; ++r) {
+        float bv;
+        int32_t bi;
+        int64_t i0;
+        if (N < 32) {
+            bv = load(x, dt, r * N);
+            bi = 0;
+            i0 = 1;
+        } else {
+            bv = -INFINITY;
+            bi = 0x7fffffff;
+            i0 = 0;
+        }
+        for (int64_t i = i0; i < N; ++i) {
+            const float v = load(x, dt, r * N + i);
+            if (argmax_better(v, int32_t(i), bv, bi)) {
+                bv = v;
+                bi = int32_t(i);
+            }
+        }
+        out[r] = bi;
+    }
 }
 
 // FlashDecoding.metal:29-174 (partial) + :182-231 (reduce), Sq = 1.

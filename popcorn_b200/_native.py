@@ -123,6 +123,7 @@ def _declare(L):
         "pc_kernel_matmul_residual": ([T, T, T, T, PP], I),
         "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
         "pc_kernel_qkv_scatter": ([T, T, T, T, I64, T, PP], I),
+        "pc_kernel_argmax": ([T, T, I32, PP], I),
         "pc_ipc_get_handle": ([P, ctypes.POINTER(ctypes.c_uint8)], I),
         "pc_ipc_open_handle": ([ctypes.POINTER(ctypes.c_uint8), PP], I),
         "pc_ipc_close_handle": ([P], I),

@@ -521,6 +521,12 @@ class Kernels:
                              keep=_keep(x, norm_weight, w_qkv, q_out, k_cache, v_cache, position))
 
 
+    class Argmax(Kernel):
+        """Kernels.Argmax(_:indices:axis:) (Argmax.swift:24-37)."""
+
+        def __init__(self, x, indices, axis=-1):
+            super().__init__(N.lib().pc_kernel_argmax, _tc(x), _tc(indices), int(axis), keep=_keep(x, indices))
+
     class QKVScatter(Kernel):
         """Extension: q and the new K/V rows out of one fused QKV Matmul."""
 

@@ -186,6 +186,20 @@ struct AddRMSNorm {
 };
 cudaError_t add_rmsnorm(const AddRMSNorm& p, cudaStream_t stream);
 
+// Kernels.Argmax (argmax.cu).
+struct Argmax {
+    const void* x;  // [rows, N]
+    int dtype;
+    int32_t* out;   // [rows]
+    int64_t rows, N;
+    int chunks;     // two-pass form when > 1 (argmax_plan)
+    int64_t chunk;
+    float* part_v;  // [rows * chunks] scratch of the two-pass form
+    int32_t* part_i;
+};
+void argmax_plan(Argmax& p, int sm_count);
+cudaError_t argmax(const Argmax& p, cudaStream_t stream);
+
 // One-shot all-reduce of tensor-parallel partial sums over peer memory,
 // fused with the residual add and RMSNorm (allreduce.cu).
 constexpr int kMaxPeers = 8;

@@ -556,6 +556,57 @@ std::unique_ptr<Kernel> make_qkv(const Tensor& x, const Tensor* nw, float eps, b
 }
 
 // ---------------------------------------------------------------------------
+// Kernels.Argmax (Argmax.swift)
+// ---------------------------------------------------------------------------
+class ArgmaxKernel : public Kernel {
+public:
+    ArgmaxKernel(Tensor x, Tensor idx, int axis) : x_(x), idx_(idx) {
+        const int rank = x.rank();
+        const int ax = axis < 0 ? rank + axis : axis;
+        // Argmax.swift:25-29
+        if (rank < 1 || ax != rank - 1)
+            fail(PC_ERR_TENSOR_INVALID_AXIS, "Argmax axis " + std::to_string(axis) + " is invalid for rank " +
+                                                 std::to_string(rank) + ".");
+        if (!is_float(x.dtype()))
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Argmax input must be f32 (f16 / bf16 extension).");
+        if (idx.dtype() != PC_I32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "Argmax indices must be int32.");
+        const int64_t N = x[ax];
+        const int64_t rows = N > 0 ? x.element_count() / N : 0;
+        // Argmax.swift:31-35
+        if (idx.element_count() != rows)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Argmax indices must contain " + std::to_string(rows) +
+                                                   " elements; got " + std::to_string(idx.element_count()) + ".");
+        if (N > int64_t(0x7fffffff)) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Argmax row longer than int32 indices.");
+        p_ = launch::Argmax{x.data(), x.dtype(), static_cast<int32_t*>(idx.data()), rows, N, 1, N, nullptr, nullptr};
+        function_names_ = N < 32 ? "argmax" : "argmax_row";  // Argmax.swift:21
+    }
+    const char* name() const override { return "Argmax"; }
+    std::vector<Binding> tensors() const override { return {{x_, PC_ACCESS_READ}, {idx_, PC_ACCESS_WRITE}}; }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::Argmax p = p_;
+        if (p.N >= 32 && enc.has_scratch()) launch::argmax_plan(p, enc.sm_count());
+        if (p.chunks <= 1) {
+            enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::argmax(p, s); });
+            return;
+        }
+        std::vector<ScratchSpec> specs = {{{p.rows * p.chunks}, PC_F32}, {{p.rows * p.chunks}, PC_I32}};
+        enc.with_temporaries(specs, [&](const std::vector<Tensor>& t) {
+            launch::Argmax q = p;
+            q.part_v = static_cast<float*>(t[0].data());
+            q.part_i = static_cast<int32_t*>(t[1].data());
+            std::vector<Binding> b = tensors();
+            b.push_back({t[0], PC_ACCESS_READ_WRITE});
+            b.push_back({t[1], PC_ACCESS_READ_WRITE});
+            enc.dispatch(function_names_, b, [q](cudaStream_t s) { return launch::argmax(q, s); });
+        });
+    }
+
+private:
+    Tensor x_, idx_;
+    launch::Argmax p_{};
+};
+
+// ---------------------------------------------------------------------------
 // Batched-decode helpers (batched.cu)
 // ---------------------------------------------------------------------------
 inline bool aligned16_ptr(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -1226,6 +1277,12 @@ int pc_kernel_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, f
                          tensor_arg(w_qkv, "w_qkv"), tensor_arg(q_out, "q_out"), tensor_arg(k_cache, "k_cache"),
                          tensor_arg(v_cache, "v_cache"), offset, position ? &pos : nullptr),
                 kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_argmax(const pc_tensor* x, const pc_tensor* indices, int32_t axis, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<ArgmaxKernel>(tensor_arg(x, "x"), tensor_arg(indices, "indices"), axis), kernel);
     PC_GUARD_END
 }
 

@@ -90,10 +90,14 @@ class DecodeStack:
     output on exit (it ping-pongs through two buffers).
     """
 
-    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False):
+    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False, vocab=0):
+        """vocab > 0 adds the step's tail: the final RMSNorm fused into the LM
+        head GEMV (tied embedding [vocab, H]) into `logits`, then Argmax into
+        `token` (int32) — the greedy next token (Argmax.metal)."""
         import torch
         self.shape = shape
         self.library = library
+        self.vocab = vocab
         self.device = device
         g = torch.Generator(device="cuda:%d" % device)
         g.manual_seed(seed)
@@ -119,6 +123,11 @@ class DecodeStack:
         self.scratch = FixedScratch(64 << 20, device)
         self.l2_prefetch = l2_prefetch
         self.fused = fused
+        if vocab:
+            self.final_norm = (torch.randn(s.H, generator=g, device=dev) * 0.1).float()
+            self.lm_head = (torch.randn(vocab, s.H, generator=g, device=dev, dtype=torch.float32) * 0.02).to(tdt)
+            self.logits = torch.zeros(1, vocab, dtype=tdt, device=dev)
+            self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self._kernels = None
 
     def kernels(self):
@@ -145,6 +154,7 @@ class DecodeStack:
         if self.l2_prefetch:
             self._chain_prefetch(ks)
         self.out = cur
+        ks += self._tail_kernels()
         self._kernels = ks
         return ks
 
@@ -170,8 +180,17 @@ class DecodeStack:
         desc.workspace_bytes = nbytes
         k = DecodeStackKernel(desc, keep=(self._layer_table, self._workspace))
         self.out = self.x if len(self.layers) % 2 == 0 else self.x2
-        self._kernels = [k]
+        self._kernels = [k] + self._tail_kernels()
         return self._kernels
+
+    def _tail_kernels(self):
+        """Final RMSNorm + LM head GEMV + Argmax (when vocab > 0)."""
+        if not self.vocab:
+            return []
+        s = self.shape
+        return [Kernels.RMSNormMatmul(self.out, self.final_norm, self.lm_head, into=self.logits, eps=s.eps,
+                                      add_one_to_weight=True),
+                Kernels.Argmax(self.logits, self.token)]
 
     # Bytes of the next operand each kernel pulls into L2 once its own loads
     # are issued (an L2 of 126 MB holds these comfortably).
@@ -209,7 +228,8 @@ class DecodeStack:
         return self.out
 
     def algorithmic_bytes_per_step(self, ctx):
-        return len(self.layers) * self.shape.bytes_per_token(ctx)
+        lm = self.vocab * self.shape.H * _nbytes(self.x) // self.x.numel() if self.vocab else 0
+        return len(self.layers) * self.shape.bytes_per_token(ctx) + lm
 
 
 def _nbytes(t):

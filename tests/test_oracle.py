@@ -168,3 +168,23 @@ def test_flash_decoding_partials_layout():
     assert np.all(pL[0, 0, :3] == 1.0) and np.all(pL[0, 0, 3:] == 0.0)
     assert np.all(np.isneginf(pM[0, 0, 3:]))
     assert np.allclose(out, 1.0)
+
+
+def test_argmax_kat(kats):
+    k = kats["argmax"]
+    x = np.array(k["x"], np.float32).reshape(k["shape"])
+    assert oracle.argmax(x, "f32").tolist() == k["expected"]
+
+
+def test_argmax_rules():
+    """Argmax.metal:7-76: ties -> lowest index; NaN never wins; n >= 32 starts
+    from (-inf, 0x7fffffff), n < 32 from element 0."""
+    x = np.zeros((4, 40), np.float32)
+    x[0, [3, 17, 30]] = 5.0                      # tie: lowest index
+    x[1] = np.nan
+    x[1, 22] = -np.inf                           # only non-NaN value
+    x[2] = np.nan                                # nothing wins
+    x[3] = -np.inf                               # all -inf: lowest index
+    assert oracle.argmax(x, "f32").tolist() == [3, 22, 0x7fffffff, 0]
+    y = np.array([[np.nan, 1.0, 2.0]], np.float32)  # n < 32: element 0 (NaN) is never beaten
+    assert oracle.argmax(y, "f32").tolist() == [0]
