@@ -549,6 +549,29 @@ def main():
             kern_us[name] = a_ev.elapsed_time(b_ev) * 1000.0 / reps / n_layers
             del g_role
 
+        # ---- the step's tail at Gemma-2 vocabulary size: final RMSNorm fused into
+        # the LM head GEMV (256000 x 2304, 1.18 GB) + Argmax, from its own graph ----
+        tail = DecodeStack(lib, shape, 1, seed=99 + rank, device=local, vocab=256000)
+        tail.set_position(pos)
+        tail.x.normal_()
+        tail_ks = tail.kernels()[-2:]
+        g_t = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_t, stream=stream):
+            enc.encode(*tail_ks)
+        for _ in range(3):
+            g_t.replay()
+        torch.cuda.synchronize()
+        t0e = torch.cuda.Event(enable_timing=True)
+        t1e = torch.cuda.Event(enable_timing=True)
+        t0e.record(stream)
+        for _ in range(10):
+            g_t.replay()
+        t1e.record(stream)
+        torch.cuda.synchronize()
+        tail_us = t0e.elapsed_time(t1e) * 100.0
+        tail_bytes = 256000 * shape.H * 2 + 256000 * 2
+        del g_t, tail
+
         # ---- the same step as one persistent kernel (DecodeStack(fused=True)) ----
         fused = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, fused=True)
         fused.set_position(pos)
@@ -614,6 +637,9 @@ def main():
         "flash_decode": {"kernel": "flash_decoding_f16 (partial + combine)", "achieved_gbs": fd["gbs"],
                          "frac_of_measured_hbm": fd["frac_of_measured_hbm"], "bytes_per_launch": fd["bytes"]},
         "kernels": kernels,
+        "lm_head_argmax": {"kernels": "RMSNorm + LM head GEMV (vocab 256000) + Argmax", "us": tail_us,
+                           "bytes": tail_bytes, "gbs": tail_bytes / (tail_us * 1e-6) / 1e9,
+                           "frac_of_measured_hbm": tail_bytes / (tail_us * 1e-6) / 1e9 / hbm_gbs},
         "fused_step": {"kernel": "decode_step_f16 (one persistent launch per token, all 26 layers)",
                        "ms_per_step": fused_ms, "tok_s": 1000.0 / fused_ms,
                        "step_hbm_gbs": bytes_step / (fused_ms * 1e-3) / 1e9, "device_error_word": fused_err},

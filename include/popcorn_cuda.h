@@ -316,6 +316,32 @@ PC_API int pc_kernel_add_rmsnorm(const pc_tensor* a, const pc_tensor* b, const p
                                  int32_t add_one_to_weight, const pc_tensor* sum_out, const pc_tensor* norm_out,
                                  pc_kernel** kernel);
 
+/* ---- rotary position embedding ------------------------------------------ */
+
+/* Kernels.RopeBuildCosSin (RopeBuildCosSin.swift:31-50, RopeBuildCosSin.metal:
+ * 5-21): cos_out / sin_out [T, Hd/2] f32 = cos / sin(positions[t] *
+ * inv_freq[i]) * attention_scaling; positions int32 [T], inv_freq f32 [Hd/2]. */
+PC_API int pc_kernel_rope_build_cos_sin(const pc_tensor* positions, const pc_tensor* inv_freq,
+                                        const pc_tensor* cos_out, const pc_tensor* sin_out, float attention_scaling,
+                                        pc_kernel** kernel);
+/* Kernels.RopeApply (RopeApply.swift:48-64, RopeApply.metal:6-49): rotate-half
+ * RoPE of x [B, T, Nh, Hd] with tables [T, Hd/2]; (x, tables) dtypes f32/f32,
+ * bf16/bf16, bf16/f32 (reference) and f16/f16, f16/f32 (extension); out has
+ * x's shape and dtype. */
+PC_API int pc_kernel_rope_apply(const pc_tensor* x, const pc_tensor* cos_t, const pc_tensor* sin_t,
+                                const pc_tensor* out, pc_kernel** kernel);
+/* Extension: the decode step's per-head norms and RoPE in place, one launch
+ * for RMSNorm(q, q_norm) -> RopeApply, RMSNorm(k, k_norm) -> RopeApply and
+ * (norm_v != 0) RMSNorm(v) without weight (Gemma4TextInference.swift:352-381),
+ * with the reference's rounding points. q [B, Nq, 1, Hd]; the new key / value
+ * rows are the caches' rows [B, Nkv, Smax, Hd] at the position (offset, or
+ * position int32 [1] on the device when given); tables f32 [R, Hd/2], row 0
+ * when R == 1 else the position's row. */
+PC_API int pc_kernel_qk_norm_rope(const pc_tensor* q, const pc_tensor* k_cache, const pc_tensor* v_cache,
+                                  const pc_tensor* q_norm, const pc_tensor* k_norm, const pc_tensor* cos_t,
+                                  const pc_tensor* sin_t, float eps, int32_t add_one_to_weight, int32_t norm_v,
+                                  int64_t offset, const pc_tensor* position, pc_kernel** kernel);
+
 /* ---- tensor parallelism over peer memory (extension) ---------------------- */
 
 /* CUDA IPC of a pc_buffer_alloc allocation (64-byte opaque handle), for one

@@ -43,6 +43,8 @@ def _declare(L):
         "or_matvec_nk": [P, I, P, I, P, I, L64, L64],
         "or_matmul": [P, I, P, I, P, I, L64, L64, L64, I],
         "or_argmax": [P, I, L64, L64, P],
+        "or_rope_build": [P, P, P, P, L64, L64, F],
+        "or_rope_apply": [P, I, P, P, I, P, I, L64, L64, L64, L64],
         "or_gelu_tanh": [P, I, P, I, L64],
         "or_silu": [P, I, P, I, L64],
         "or_mul": [P, P, P, I, L64],
@@ -164,6 +166,27 @@ def add(a, b, dt):
     a, b = _c(a), _c(b)
     out = np.empty(a.shape, dtype=NP[dt])
     lib().or_add(_p(a), _p(b), _p(out), DT[dt], a.size)
+    return out
+
+
+def rope_build(positions, inv_freq, scaling=1.0):
+    """RopeBuildCosSin.metal:5-21: fp32 cos / sin tables [T, Hd2]."""
+    positions = _c(np.asarray(positions, np.int32))
+    inv_freq = _c(np.asarray(inv_freq, np.float32))
+    T, Hd2 = positions.size, inv_freq.size
+    c = np.empty((T, Hd2), np.float32)
+    s = np.empty((T, Hd2), np.float32)
+    lib().or_rope_build(_p(positions), _p(inv_freq), _p(c), _p(s), T, Hd2, scaling)
+    return c, s
+
+
+def rope_apply(x, xdt, cos, sin, tdt, odt=None):
+    """RopeApply.metal:6-49: x [B, T, Nh, Hd], tables [T, Hd/2]."""
+    x, cos, sin = _c(x), _c(cos), _c(sin)
+    odt = odt or xdt
+    B, T, Nh, Hd = x.shape
+    out = np.empty(x.shape, dtype=NP[odt])
+    lib().or_rope_apply(_p(x), DT[xdt], _p(cos), _p(sin), DT[tdt], _p(out), DT[odt], B, T, Nh, Hd // 2)
     return out
 
 

@@ -16,6 +16,8 @@
 //   or_matmul              Sources/Popcorn/Kernels/Matmul.metal:7-27
 //   or_gelu_tanh           Sources/Popcorn/Kernels/GeluTanh.metal:6-35
 //   or_mul / or_add        Sources/Popcorn/Kernels/Mul.metal:7-25, Add.metal:7-25
+//   or_rope_build          Sources/Popcorn/Kernels/RopeBuildCosSin.metal:5-21
+//   or_rope_apply          Sources/Popcorn/Kernels/RopeApply.metal:6-49
 //   or_argmax              Sources/Popcorn/Kernels/Argmax.metal:5-76, routing
 //                          Argmax.swift:21 (n >= 32 -> argmax_row)
 //   or_flash_decoding      Sources/Popcorn/Kernels/FlashDecoding.metal:29-231
@@ -265,6 +267,37 @@ void or_mul(const void* a, const void* b, void* out, int dt, int64_t n) {
 
 void or_add(const void* a, const void* b, void* out, int dt, int64_t n) {
     for (int64_t i = 0; i < n; ++i) store(out, dt, i, load(a, dt, i) + load(b, dt, i));
+}
+
+// RopeBuildCosSin.metal:13-20: angle = position[t] * inv_freq[i] in fp32;
+// cos / sin tables [T, Hd2] (fp32) times `scaling`.
+void or_rope_build(const int32_t* positions, const float* inv_freq, float* cos_out, float* sin_out, int64_t T,
+                   int64_t Hd2, float scaling) {
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < Hd2; ++i) {
+            const float angle = float(positions[t]) * inv_freq[i];
+            cos_out[t * Hd2 + i] = std::cos(angle) * scaling;
+            sin_out[t * Hd2 + i] = std::sin(angle) * scaling;
+        }
+}
+
+// RopeApply.metal:15-48: x [B, T, Nh, 2*Hd2]; per head the halves
+// x1 = x[:Hd2], x2 = x[Hd2:] become (x1 c - x2 s, x1 s + x2 c) with the
+// tables' row t; fp32 arithmetic, one rounding at each store.
+void or_rope_apply(const void* x, int xdt, const void* cos_t, const void* sin_t, int tdt, void* out, int odt,
+                   int64_t B, int64_t T, int64_t Nh, int64_t Hd2) {
+    const int64_t Hd = 2 * Hd2;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t t = 0; t < T; ++t)
+            for (int64_t h = 0; h < Nh; ++h) {
+                const int64_t base = ((b * T + t) * Nh + h) * Hd;
+                for (int64_t i = 0; i < Hd2; ++i) {
+                    const float x1 = load(x, xdt, base + i), x2 = load(x, xdt, base + Hd2 + i);
+                    const float c = load(cos_t, tdt, t * Hd2 + i), sn = load(sin_t, tdt, t * Hd2 + i);
+                    store(out, odt, base + i, x1 * c - x2 * sn);
+                    store(out, odt, base + Hd2 + i, x1 * sn + x2 * c);
+                }
+            }
 }
 
 // Argmax.metal:7-9: a candidate wins on a larger value, or an equal value at

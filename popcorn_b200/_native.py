@@ -124,6 +124,9 @@ def _declare(L):
         "pc_kernel_qkv_projection": ([T, T, F, I32, T, T, T, T, I64, T, PP], I),
         "pc_kernel_qkv_scatter": ([T, T, T, T, I64, T, PP], I),
         "pc_kernel_argmax": ([T, T, I32, PP], I),
+        "pc_kernel_rope_build_cos_sin": ([T, T, T, T, F, PP], I),
+        "pc_kernel_rope_apply": ([T, T, T, T, PP], I),
+        "pc_kernel_qk_norm_rope": ([T, T, T, T, T, T, T, F, I32, I32, I64, T, PP], I),
         "pc_ipc_get_handle": ([P, ctypes.POINTER(ctypes.c_uint8)], I),
         "pc_ipc_open_handle": ([ctypes.POINTER(ctypes.c_uint8), PP], I),
         "pc_ipc_close_handle": ([P], I),

@@ -527,6 +527,34 @@ class Kernels:
         def __init__(self, x, indices, axis=-1):
             super().__init__(N.lib().pc_kernel_argmax, _tc(x), _tc(indices), int(axis), keep=_keep(x, indices))
 
+    class RopeBuildCosSin(Kernel):
+        """Kernels.RopeBuildCosSin(positions:invFreq:cosOut:sinOut:attentionScaling:)
+        (RopeBuildCosSin.swift:31-50)."""
+
+        def __init__(self, positions, inv_freq, cos_out, sin_out, attention_scaling=1.0):
+            super().__init__(N.lib().pc_kernel_rope_build_cos_sin, _tc(positions), _tc(inv_freq), _tc(cos_out),
+                             _tc(sin_out), ctypes.c_float(attention_scaling),
+                             keep=_keep(positions, inv_freq, cos_out, sin_out))
+
+    class RopeApply(Kernel):
+        """Kernels.RopeApply(_:cos:sin:into:) (RopeApply.swift:48-64)."""
+
+        def __init__(self, x, cos, sin, into):
+            super().__init__(N.lib().pc_kernel_rope_apply, _tc(x), _tc(cos), _tc(sin), _tc(into),
+                             keep=_keep(x, cos, sin, into))
+
+    class QKNormRope(Kernel):
+        """Extension: RMSNorm(q) -> RopeApply, RMSNorm(k) -> RopeApply and
+        RMSNorm(v) (no weight) of one decode step in place, one launch
+        (Gemma4TextInference.swift:352-381)."""
+
+        def __init__(self, q, k_cache, v_cache, q_norm, k_norm, cos, sin, offset=0, position=None, eps=1e-6,
+                     add_one_to_weight=False, norm_v=True):
+            super().__init__(N.lib().pc_kernel_qk_norm_rope, _tc(q), _tc(k_cache), _tc(v_cache), _tc(q_norm),
+                             _tc(k_norm), _tc(cos), _tc(sin), ctypes.c_float(eps), int(add_one_to_weight),
+                             int(norm_v), int(offset), _tc(position),
+                             keep=_keep(q, k_cache, v_cache, q_norm, k_norm, cos, sin, position))
+
     class QKVScatter(Kernel):
         """Extension: q and the new K/V rows out of one fused QKV Matmul."""
 

@@ -186,6 +186,34 @@ struct AddRMSNorm {
 };
 cudaError_t add_rmsnorm(const AddRMSNorm& p, cudaStream_t stream);
 
+// Rotary embedding and the decode step's per-head norms (rope.cu).
+cudaError_t rope_build_cos_sin(const int32_t* positions, const float* inv_freq, float* cos_out, float* sin_out,
+                               int64_t T, int64_t Hd2, float scaling, cudaStream_t stream);
+struct RopeApply {
+    const void* x;  // [B, T, Nh, 2 Hd2]
+    const void* cos_t;  // [T, Hd2]
+    const void* sin_t;
+    void* out;
+    int x_dtype, t_dtype, out_dtype;
+    int64_t B, T, Nh, Hd2;
+};
+cudaError_t rope_apply(const RopeApply& p, cudaStream_t stream);
+struct QKNormRope {
+    void* q;        // [B, Nq, 1, Hd], in place
+    void* k_cache;  // [B, Nkv, Smax, Hd]: the row at the position, in place
+    void* v_cache;
+    const float* q_norm;  // [Hd]
+    const float* k_norm;  // [Hd]
+    const float* cos_t;   // [table_rows, Hd/2] f32; row 0 when table_rows == 1, else the position's row
+    const float* sin_t;
+    int dtype;
+    int64_t B, Nq, Nkv, Hd, Smax, offset, table_rows;
+    const int32_t* pos_dev;  // when set, the position is read on the device
+    float eps;
+    int add_one, norm_v;
+};
+cudaError_t qk_norm_rope(const QKNormRope& p, cudaStream_t stream);
+
 // Kernels.Argmax (argmax.cu).
 struct Argmax {
     const void* x;  // [rows, N]

@@ -734,6 +734,151 @@ private:
 };
 
 // ---------------------------------------------------------------------------
+// Rotary embedding (rope.cu)
+// ---------------------------------------------------------------------------
+class RopeBuildCosSinKernel : public Kernel {
+public:
+    // RopeBuildCosSin.swift:31-50 (shape checks), :8-28 (constants)
+    RopeBuildCosSinKernel(Tensor pos, Tensor inv, Tensor c, Tensor s, float scaling)
+        : pos_(pos), inv_(inv), cos_(c), sin_(s), scaling_(scaling) {
+        if (!c.same_shape(s))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE cos and sin output shapes must match; got " + c.shape_string() +
+                                                   " and " + s.shape_string() + ".");
+        if (c.rank() != 2)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(c.rank()) + ".");
+        T_ = c[0];
+        Hd2_ = c[1];
+        if (pos.element_count() != T_)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE positions count must equal seqLen " + std::to_string(T_) +
+                                                   "; got " + std::to_string(pos.element_count()) + ".");
+        if (inv.element_count() != Hd2_)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE invFreq count must equal halfHeadDim " + std::to_string(Hd2_) +
+                                                   "; got " + std::to_string(inv.element_count()) + ".");
+        if (pos.dtype() != PC_I32 || inv.dtype() != PC_F32 || c.dtype() != PC_F32 || s.dtype() != PC_F32)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RoPE tables: int32 positions, f32 invFreq and tables.");
+        function_names_ = "rope_build_cos_sin";
+    }
+    const char* name() const override { return "RopeBuildCosSin"; }
+    std::vector<Binding> tensors() const override {
+        return {{pos_, PC_ACCESS_READ}, {inv_, PC_ACCESS_READ}, {cos_, PC_ACCESS_WRITE}, {sin_, PC_ACCESS_WRITE}};
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        const int32_t* pos = static_cast<const int32_t*>(pos_.data());
+        const float* inv = static_cast<const float*>(inv_.data());
+        float* c = static_cast<float*>(cos_.data());
+        float* sn = static_cast<float*>(sin_.data());
+        const int64_t T = T_, Hd2 = Hd2_;
+        const float sc = scaling_;
+        enc.dispatch(function_names_, tensors(),
+                     [=](cudaStream_t s) { return launch::rope_build_cos_sin(pos, inv, c, sn, T, Hd2, sc, s); });
+    }
+
+private:
+    Tensor pos_, inv_, cos_, sin_;
+    float scaling_;
+    int64_t T_ = 0, Hd2_ = 0;
+};
+
+class RopeApplyKernel : public Kernel {
+public:
+    // RopeApply.swift:48-64 (shape checks), :19-31 (dtype routing)
+    RopeApplyKernel(Tensor x, Tensor c, Tensor s, Tensor out) : x_(x), cos_(c), sin_(s), out_(out) {
+        if (x.rank() != 4)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 4, got rank " + std::to_string(x.rank()) + ".");
+        if (!x.same_shape(out))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE output shape must match input; got " + out.shape_string() +
+                                                   ", expected " + x.shape_string() + ".");
+        const int64_t Hd = x[3];
+        if (Hd % 2 != 0)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE head dimension must be even; got " + std::to_string(Hd) + ".");
+        if (c.rank() != 2 || s.rank() != 2 || c[0] != x[1] || c[1] != Hd / 2 || !c.same_shape(s))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "RoPE tables must have shape [" + std::to_string(x[1]) + ", " +
+                                                   std::to_string(Hd / 2) + "]; got cos " + c.shape_string() +
+                                                   ", sin " + s.shape_string() + ".");
+        const int xd = x.dtype(), td = c.dtype();
+        const bool ok = s.dtype() == td && out.dtype() == xd &&
+                        ((xd == PC_F32 && td == PC_F32) || (xd == PC_BF16 && (td == PC_BF16 || td == PC_F32)) ||
+                         (xd == PC_F16 && (td == PC_F16 || td == PC_F32)));
+        if (!ok)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, std::string("Unsupported RoPE data type combination: ") +
+                                                               dt_tag(xd) + ", " + dt_tag(td) + ".");
+        p_ = launch::RopeApply{x.data(), c.data(), s.data(), out.data(), xd, td, xd, x[0], x[1], x[2], Hd / 2};
+        if (xd == PC_F32) function_names_ = "rope_apply";
+        else if (td == PC_F32) function_names_ = std::string("rope_apply_f32_tables_") + dt_tag(xd);
+        else function_names_ = std::string("rope_apply_") + dt_tag(xd);
+    }
+    const char* name() const override { return "RopeApply"; }
+    std::vector<Binding> tensors() const override {
+        return {{x_, PC_ACCESS_READ}, {cos_, PC_ACCESS_READ}, {sin_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::RopeApply p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::rope_apply(p, s); });
+    }
+
+private:
+    Tensor x_, cos_, sin_, out_;
+    launch::RopeApply p_{};
+};
+
+// The decode step's RMSNorm(q) -> RopeApply, RMSNorm(k) -> RopeApply,
+// RMSNorm(v) (Gemma4TextInference.swift:352-381) in place, one launch.
+class QKNormRopeKernel : public Kernel {
+public:
+    QKNormRopeKernel(Tensor q, Tensor kc, Tensor vc, Tensor qn, Tensor kn, Tensor c, Tensor s, float eps,
+                     bool add_one, bool norm_v, int64_t offset, const Tensor* pos)
+        : q_(q), kc_(kc), vc_(vc), qn_(qn), kn_(kn), cos_(c), sin_(s) {
+        const int dt = q.dtype();
+        if (!is_float(dt) || kc.dtype() != dt || vc.dtype() != dt)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "QKNormRope needs one float dtype for q and the caches.");
+        if (qn.dtype() != PC_F32 || kn.dtype() != PC_F32 || c.dtype() != PC_F32 || s.dtype() != PC_F32)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "QKNormRope norm weights and tables must be f32.");
+        if (q.rank() != 4 || kc.rank() != 4 || !kc.same_shape(vc) || c.rank() != 2 || !c.same_shape(s))
+            fail(PC_ERR_TENSOR_INVALID_RANK, "QKNormRope wants q [B,Nq,1,Hd], caches [B,Nkv,Smax,Hd], tables [R,Hd/2].");
+        const int64_t B = q[0], Nq = q[1], Hd = q[3], Nkv = kc[1], Smax = kc[2];
+        if (q[2] != 1 || kc[0] != B || kc[3] != Hd || c[1] != Hd / 2)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKNormRope shapes disagree: q " + q.shape_string() + ", cache " +
+                                                   kc.shape_string() + ", table " + c.shape_string() + ".");
+        if (Hd % 2 != 0 || Hd > 2048)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKNormRope head dimension must be even and <= 2048.");
+        require_elements(qn, Hd, "q norm weight");
+        require_elements(kn, Hd, "k norm weight");
+        if (!pos && (offset < 0 || offset >= Smax || (c[0] != 1 && offset >= c[0])))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKNormRope position " + std::to_string(offset) +
+                                                   " outside the cache or the tables.");
+        if (pos) {
+            if (pos->dtype() != PC_I32 || pos->element_count() < 1)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "position must be int32 [1].");
+            pos_ = *pos;
+            has_pos_ = true;
+        }
+        p_ = launch::QKNormRope{q.data(), kc.data(), vc.data(), static_cast<const float*>(qn.data()),
+                                static_cast<const float*>(kn.data()), static_cast<const float*>(c.data()),
+                                static_cast<const float*>(s.data()), dt, B, Nq, Nkv, Hd, Smax, offset, c[0],
+                                pos ? static_cast<const int32_t*>(pos->data()) : nullptr, eps, add_one ? 1 : 0,
+                                norm_v ? 1 : 0};
+        function_names_ = dt == PC_F32 ? "qk_norm_rope" : std::string("qk_norm_rope_") + dt_tag(dt);
+    }
+    const char* name() const override { return "QKNormRope"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> b = {{q_, PC_ACCESS_READ_WRITE}, {kc_, PC_ACCESS_READ_WRITE}, {vc_, PC_ACCESS_READ_WRITE},
+                                  {qn_, PC_ACCESS_READ},       {kn_, PC_ACCESS_READ},        {cos_, PC_ACCESS_READ},
+                                  {sin_, PC_ACCESS_READ}};
+        if (has_pos_) b.push_back({pos_, PC_ACCESS_READ});
+        return b;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::QKNormRope p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::qk_norm_rope(p, s); });
+    }
+
+private:
+    Tensor q_, kc_, vc_, qn_, kn_, cos_, sin_, pos_;
+    bool has_pos_ = false;
+    launch::QKNormRope p_{};
+};
+
+// ---------------------------------------------------------------------------
 // All-reduce + Add + RMSNorm over peer memory (allreduce.cu)
 // ---------------------------------------------------------------------------
 class PeerAllReduceKernel : public Kernel {
@@ -1303,6 +1448,41 @@ int pc_kernel_gated_activation(const pc_tensor* gate_up, int32_t activation, con
     PC_GUARD_BEGIN
     return wrap(std::make_unique<GatedActivationKernel>(tensor_arg(gate_up, "gate_up"), activation,
                                                         tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_rope_build_cos_sin(const pc_tensor* positions, const pc_tensor* inv_freq, const pc_tensor* cos_out,
+                                 const pc_tensor* sin_out, float attention_scaling, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<RopeBuildCosSinKernel>(tensor_arg(positions, "positions"),
+                                                        tensor_arg(inv_freq, "inv_freq"), tensor_arg(cos_out, "cos_out"),
+                                                        tensor_arg(sin_out, "sin_out"), attention_scaling),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_rope_apply(const pc_tensor* x, const pc_tensor* cos_t, const pc_tensor* sin_t, const pc_tensor* out,
+                         pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<RopeApplyKernel>(tensor_arg(x, "x"), tensor_arg(cos_t, "cos"),
+                                                  tensor_arg(sin_t, "sin"), tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_qk_norm_rope(const pc_tensor* q, const pc_tensor* k_cache, const pc_tensor* v_cache,
+                           const pc_tensor* q_norm, const pc_tensor* k_norm, const pc_tensor* cos_t,
+                           const pc_tensor* sin_t, float eps, int32_t add_one_to_weight, int32_t norm_v,
+                           int64_t offset, const pc_tensor* position, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor pos;
+    if (position) pos = tensor_arg(position, "position");
+    return wrap(std::make_unique<QKNormRopeKernel>(tensor_arg(q, "q"), tensor_arg(k_cache, "k_cache"),
+                                                   tensor_arg(v_cache, "v_cache"), tensor_arg(q_norm, "q_norm"),
+                                                   tensor_arg(k_norm, "k_norm"), tensor_arg(cos_t, "cos"),
+                                                   tensor_arg(sin_t, "sin"), eps, add_one_to_weight != 0, norm_v != 0,
+                                                   offset, position ? &pos : nullptr),
                 kernel);
     PC_GUARD_END
 }

@@ -188,3 +188,44 @@ def test_argmax_rules():
     assert oracle.argmax(x, "f32").tolist() == [3, 22, 0x7fffffff, 0]
     y = np.array([[np.nan, 1.0, 2.0]], np.float32)  # n < 32: element 0 (NaN) is never beaten
     assert oracle.argmax(y, "f32").tolist() == [0]
+
+
+def _rope_kat_expected(k):
+    """The reference test's expected values (KernelsTests.swift:457-489)."""
+    x = np.array(k["x"], np.float64).reshape(2, 4)
+    pos = np.array(k["positions"], np.float64)
+    inv = np.array(k["inv_freq"], np.float64)
+    ang = pos[:, None] * inv[None, :]
+    c, s = np.cos(ang), np.sin(ang)
+    x1, x2 = x[:, :2], x[:, 2:]
+    return c, s, np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=1)
+
+
+def test_rope_kat(kats):
+    k = kats["rope"]
+    ec, es, eout = _rope_kat_expected(k)
+    c, s = oracle.rope_build(k["positions"], k["inv_freq"])
+    assert approx_equal(c, ec).all() and approx_equal(s, es).all()
+    x = np.array(k["x"], np.float32).reshape(k["x_shape"])
+    out = oracle.rope_apply(x, "f32", c, s, "f32")
+    assert approx_equal(out.reshape(2, 4), eout).all()
+    assert np.array_equal(out[0, 0, 0], x[0, 0, 0])  # t = 0: unchanged
+
+
+def test_rope_dtype_combinations():
+    """RopeApply.swift:19-31 routes f32/f32, bf16/bf16 and bf16 x with f32
+    tables; every combination agrees with a float64 rotation within the
+    storage rounding."""
+    rng = np.random.default_rng(3)
+    T, Hd = 5, 16
+    x = rng.standard_normal((2, T, 3, Hd)).astype(np.float32)
+    inv = (10000.0 ** (-np.arange(Hd // 2) * 2.0 / Hd)).astype(np.float32)
+    c, s = oracle.rope_build(np.arange(7, 7 + T), inv, scaling=0.5)
+    xd = x.astype(np.float64)
+    cd, sd = c.astype(np.float64)[None, :, None, :], s.astype(np.float64)[None, :, None, :]
+    x1, x2 = xd[..., :Hd // 2], xd[..., Hd // 2:]
+    exact = np.concatenate([x1 * cd - x2 * sd, x1 * sd + x2 * cd], axis=-1)
+    for xdt, tdt, tol in [("f32", "f32", 1e-5), ("bf16", "bf16", 3e-2), ("bf16", "f32", 2e-2)]:
+        out = oracle.to_f32(oracle.rope_apply(oracle.to_dtype(x, xdt), xdt, oracle.to_dtype(c, tdt),
+                                              oracle.to_dtype(s, tdt), tdt), xdt)
+        assert np.allclose(out, exact, rtol=tol, atol=tol), (xdt, tdt)
