@@ -403,12 +403,20 @@ typedef struct pc_decode_layer {
     const float* mlp_norm;
     void* k_cache;
     void* v_cache;
+    /* Per-head q / k RMSNorm weights f32 [Hd] (used when the descriptor's
+     * qk_norm is set; NULL = no weight) and RoPE tables f32 [rope_rows, Hd/2]
+     * (NULL = no RoPE), Gemma4TextInference.swift:352-381. */
+    const float* q_norm;
+    const float* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
 } pc_decode_layer;
 
 /* A batch-1 decode step through a stack of layers. Each layer is the op
  * sequence of Gemma4TextInference.swift:312-436 restricted to RMSNorm ->
  * QKV -> KVCacheWrite -> FlashAttention (Sq = 1) -> o_proj -> Add ->
- * RMSNorm -> gated MLP -> Add, with every intermediate rounded to `dtype`
+ * RMSNorm -> gated MLP -> Add (optionally with the per-head q / k / v norms
+ * and RoPE after the QKV projection), with every intermediate rounded to `dtype`
  * where the reference ops store it. `layers` points to `num_layers`
  * pc_decode_layer entries in DEVICE memory. Activation buffers (device,
  * `dtype`): x [H] holds the input and, for an even layer count, the output
@@ -437,6 +445,12 @@ typedef struct pc_decode_stack_desc {
     const int32_t* position;
     void* workspace;
     uint64_t workspace_bytes;
+    /* qk_norm: RMSNorm of each q and new k head after the QKV projection
+     * (and of each new v head without weight when norm_v); rope_rows: rows of
+     * the layers' RoPE tables (0: no RoPE; 1: the step's row; else indexed
+     * by position). */
+    int32_t qk_norm, norm_v;
+    int64_t rope_rows;
 } pc_decode_stack_desc;
 
 /* Extension (no reference counterpart): workspace size for a descriptor. */

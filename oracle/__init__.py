@@ -55,7 +55,7 @@ def _declare(L):
         "or_attention_exact": [P, I, P, P, I, P, L64, L64, L64, L64, L64, L64, P, L64, F, I,
                                ctypes.c_int32],
         "or_decode_layer": [P, I, P, P, P, P, P, P, P, P, P, L64, L64, L64, L64, L64, L64, L64, F, F,
-                            I, P],
+                            I, P, P, P, I, I, P, P],
         "or_set_threads": [I],
     }
     for name, args in sig.items():
@@ -253,15 +253,20 @@ def attention_exact(q, qdt, k, v, kvdt, scale, mask="causal", window=-1, seq_len
 
 
 def decode_layer(x, dt, w_attn_norm, w_mlp_norm, w_qkv, w_o, w_gate, w_up, w_down, k_cache, v_cache,
-                 Nq, Nkv, Hd, pos, eps=1e-6, attn_scale=1.0 / 16, act="gelu_tanh"):
-    """One batch-1 decode layer (see or_decode_layer). Caches [Nkv,Smax,Hd] updated in place."""
+                 Nq, Nkv, Hd, pos, eps=1e-6, attn_scale=1.0 / 16, act="gelu_tanh", q_norm=None, k_norm=None,
+                 qk_norm=False, norm_v=False, rope_cos=None, rope_sin=None):
+    """One batch-1 decode layer (see or_decode_layer). Caches [Nkv,Smax,Hd] updated in place.
+    qk_norm: per-head RMSNorm of q / k (weights q_norm / k_norm, None = no
+    weight) and, with norm_v, of v without weight; rope_cos / rope_sin: the
+    step's table row (f32 [Hd/2]) for RoPE of q and k."""
     H = x.shape[-1]
     F = w_gate.shape[0]
     Smax = k_cache.shape[-2]
     out = np.empty((H,), dtype=NP[dt])
     args = [_c(a) for a in (x, w_attn_norm, w_mlp_norm, w_qkv, w_o, w_gate, w_up, w_down)]
+    f32 = [None if a is None else _c(np.asarray(a, np.float32)) for a in (q_norm, k_norm, rope_cos, rope_sin)]
     lib().or_decode_layer(_p(args[0]), DT[dt], _p(args[1]), _p(args[2]), _p(args[3]), _p(args[4]),
                           _p(args[5]), _p(args[6]), _p(args[7]), _p(k_cache), _p(v_cache), H, Nq,
                           Nkv, Hd, F, Smax, pos, eps, attn_scale, 1 if act == "silu" else 0,
-                          _p(out))
+                          _p(out), _p(f32[0]), _p(f32[1]), int(qk_norm), int(norm_v), _p(f32[2]), _p(f32[3]))
     return out

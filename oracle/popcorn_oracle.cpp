@@ -554,7 +554,8 @@ void or_decode_layer(const void* x, int dt, const float* w_attn_norm, const floa
                      const void* w_qkv, const void* w_o, const void* w_gate, const void* w_up,
                      const void* w_down, void* k_cache, void* v_cache, int64_t H, int64_t Nq,
                      int64_t Nkv, int64_t Hd, int64_t F, int64_t Smax, int64_t pos, float eps,
-                     float attn_scale, int act, void* out) {
+                     float attn_scale, int act, void* out, const float* q_norm, const float* k_norm,
+                     int qk_norm, int norm_v, const float* rope_cos, const float* rope_sin) {
     auto el = [&](int64_t n) { return std::vector<uint8_t>(n * (dt == F32 ? 4 : 2)); };
     int64_t QKV = (Nq + 2 * Nkv) * Hd;
     auto xn = el(H), qkv = el(QKV), attn = el(Nq * Hd), o = el(H), h = el(H), hn = el(H);
@@ -562,8 +563,21 @@ void or_decode_layer(const void* x, int dt, const float* w_attn_norm, const floa
     or_rmsnorm(x, dt, w_attn_norm, xn.data(), dt, 1, H, eps, 1, 0);
     or_matvec_nk(xn.data(), dt, w_qkv, dt, qkv.data(), dt, H, QKV);
     size_t es = dt == F32 ? 4 : 2;
-    const uint8_t* kp = qkv.data() + Nq * Hd * es;
-    const uint8_t* vp = qkv.data() + (Nq + Nkv) * Hd * es;
+    uint8_t* kp = qkv.data() + Nq * Hd * es;
+    uint8_t* vp = qkv.data() + (Nq + Nkv) * Hd * es;
+    // Gemma4TextInference.swift:352-381: per-head RMSNorm of q (q_norm) and k
+    // (k_norm), of v without weight, then RoPE of q and k with the step's
+    // table row; each result stored in dt (in place here: each op reads its
+    // whole head before writing it).
+    if (qk_norm) {
+        or_rmsnorm(qkv.data(), dt, q_norm, qkv.data(), dt, Nq, Hd, eps, 1, 0);
+        or_rmsnorm(kp, dt, k_norm, kp, dt, Nkv, Hd, eps, 1, 0);
+        if (norm_v) or_rmsnorm(vp, dt, nullptr, vp, dt, Nkv, Hd, eps, 1, 0);
+    }
+    if (rope_cos) {
+        or_rope_apply(qkv.data(), dt, rope_cos, rope_sin, F32, qkv.data(), dt, 1, 1, Nq, Hd / 2);
+        or_rope_apply(kp, dt, rope_cos, rope_sin, F32, kp, dt, 1, 1, Nkv, Hd / 2);
+    }
     or_kv_cache_write(kp, dt, k_cache, dt, 1, Nkv, 1, Smax, Hd, pos);
     or_kv_cache_write(vp, dt, v_cache, dt, 1, Nkv, 1, Smax, Hd, pos);
     int32_t len = int32_t(pos + 1);

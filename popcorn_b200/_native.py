@@ -35,7 +35,8 @@ class pc_decode_stack_desc(ctypes.Structure):
                 ("attn_scale", ctypes.c_float), ("activation", ctypes.c_int32), ("add_one_to_weight", ctypes.c_int32),
                 ("layers", ctypes.c_void_p), ("x", ctypes.c_void_p), ("x2", ctypes.c_void_p), ("h", ctypes.c_void_p),
                 ("q", ctypes.c_void_p), ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p),
-                ("position", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64)]
+                ("position", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+                ("qk_norm", ctypes.c_int32), ("norm_v", ctypes.c_int32), ("rope_rows", ctypes.c_int64)]
 
 
 class pc_scratch_allocator(ctypes.Structure):

@@ -122,6 +122,45 @@ __device__ __forceinline__ float widen16(uint32_t bits) {
     return Elem<T>::load(&b, 0);
 }
 
+// One head of 256 elements held by a warp, 8 per lane (lane l: elements
+// 8l..8l+7): RMSNorm with weight w (NULL = none) when `norm`, the result
+// rounded to T as RMSNorm stores it; then, when cs is set, RoPE with table
+// row (cs, sn): element i pairs with i + 128, which lane l ^ 16 holds, and
+// the rotated value is rounded as RopeApply stores it (RMSNorm.metal:7-42,
+// RopeApply.metal:6-49). Every lane of the warp must call it.
+template <class T>
+__device__ __forceinline__ void head_norm_rope(float* f, int lane, bool norm, const float* w, float eps,
+                                               bool add_one, const float* cs, const float* sn) {
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+        ss = warp_sum(ss);
+        const float scale = rsqrtf(ss / float(kHD) + eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float v = f[e] * scale;
+            if (w) v *= add_one ? 1.0f + w[lane * 8 + e] : w[lane * 8 + e];
+            f[e] = Elem<T>::round(v);
+        }
+    }
+    if (cs) {
+        const int i0 = (lane & 15) * 8;
+        const bool second = lane & 16;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float other = __shfl_xor_sync(0xffffffffu, f[e], 16);
+            const float c = __ldg(cs + i0 + e), sv = __ldg(sn + i0 + e);
+            f[e] = Elem<T>::round(second ? other * sv + f[e] * c : f[e] * c - other * sv);
+        }
+    }
+}
+
+template <class T>
+__device__ __forceinline__ uint4 pack8(const float* f) {
+    return make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+}
+
 }  // namespace
 
 // The producer's walk over every stage this CTA loads in one step, in
@@ -247,7 +286,9 @@ struct StageCursor {
     }
 };
 
-template <class T, int GQ>
+// QK: the layers carry the per-head q / k / v norms and RoPE (a separate
+// instance, so the plain layer's attention items carry none of that code).
+template <class T, int GQ, bool QK>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __grid_constant__ DecodeStep p) {
     extern __shared__ __align__(128) unsigned char smem[];
     // full/empty barrier of slot s of group g at index g * kSlots + s
@@ -279,7 +320,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 
     const int pos = p.pos[0];
     const int len = pos + 1;
-    if (tid == 0 && (pos < 0 || pos >= p.Smax)) {
+    if (tid == 0 && (pos < 0 || pos >= p.Smax || (p.rope_rows > 1 && pos >= p.rope_rows))) {
         atomicOr(&g_step_error_word, 2u);  // position outside the cache: do nothing
         s_abort = 1;
     }
@@ -415,11 +456,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
 #pragma unroll
                             for (int e = 0; e < kE; ++e) o[g][e] = 0.f;
                         }
+                        // the step's RoPE table row (Gemma4TextInference.swift:346-351)
+                        const int64_t trow = (p.rope_rows == 1 ? 0 : int64_t(pos)) * (kHD / 2);
+                        const float* rcos = p.has_rope && L.rope_cos ? L.rope_cos + trow : nullptr;
+                        const float* rsin = p.has_rope && L.rope_sin ? L.rope_sin + trow : nullptr;
+                        const bool qk_xform = QK && (p.qk_norm || rcos);
 #pragma unroll
                         for (int g = 0; g < G; ++g) {
                             uint4 qv = ldcg16(static_cast<const char*>(p.q) + (int64_t(hq0 + g) * kHD + lane * kE) * 2);
                             float f[8];
                             unpack8<T>(qv, f);
+                            // q is stored as the QKV projection wrote it; each item
+                            // normalises and rotates its own copy
+                            if (qk_xform) head_norm_rope<T>(f, lane, p.qk_norm, L.q_norm, p.eps, p.add_one, rcos, rsin);
 #pragma unroll
                             for (int e = 0; e < kE; ++e) q[g][e] = f[e] * qs;
                         }
@@ -439,8 +488,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const __gr
                                 // memory now that op0 is complete.
                                 if (gw == 0 && !s_abort) {
                                     const int64_t row = (int64_t(hkv) * p.Smax + pos) * kHD * 2 + lane * 16;
-                                    const uint4 kv = ldcg16(static_cast<const char*>(L.k_cache) + row);
-                                    const uint4 vv = ldcg16(static_cast<const char*>(L.v_cache) + row);
+                                    uint4 kv = ldcg16(static_cast<const char*>(L.k_cache) + row);
+                                    uint4 vv = ldcg16(static_cast<const char*>(L.v_cache) + row);
+                                    if (qk_xform) {
+                                        // the new key / value heads get their norms and RoPE
+                                        // here, the one item that holds them, which also
+                                        // writes them back to the caches for later steps
+                                        float f[8];
+                                        unpack8<T>(kv, f);
+                                        head_norm_rope<T>(f, lane, p.qk_norm, L.k_norm, p.eps, p.add_one, rcos, rsin);
+                                        kv = pack8<T>(f);
+                                        *reinterpret_cast<uint4*>(static_cast<char*>(L.k_cache) + row) = kv;
+                                        if (p.qk_norm && p.norm_v) {
+                                            unpack8<T>(vv, f);
+                                            head_norm_rope<T>(f, lane, true, nullptr, p.eps, false, nullptr, nullptr);
+                                            vv = pack8<T>(f);
+                                            *reinterpret_cast<uint4*>(static_cast<char*>(L.v_cache) + row) = vv;
+                                        }
+                                    }
                                     *reinterpret_cast<uint4*>(ktile + (pos - j0) * kHD * 2 + lane * 16) = kv;
                                     *reinterpret_cast<uint4*>(vtile + (pos - j0) * kHD * 2 + lane * 16) = vv;
                                     // generic writes before the slot's next bulk copy
@@ -856,12 +921,20 @@ size_t decode_step_workspace_bytes(const DecodeStep& p) {
     return o + 2 * ml + size_t(p.L * kOps + 1 + p.L * p.Nkv) * 4 + 1024;
 }
 
+template <class T, bool QK>
+static void (*pick_step(int gq))(DecodeStep) {
+    return gq == 1 ? decode_step_kernel<T, 1, QK> : gq == 2 ? decode_step_kernel<T, 2, QK> : decode_step_kernel<T, 4, QK>;
+}
+
 cudaError_t decode_step(const DecodeStep& p, cudaStream_t s) {
     const size_t smem = decode_step_smem(p);
     void (*kern)(DecodeStep) = nullptr;
     const int gq = p.Nq / p.Nkv;
-    if (p.dtype == PC_BF16) kern = gq == 1 ? decode_step_kernel<TBF16, 1> : gq == 2 ? decode_step_kernel<TBF16, 2> : decode_step_kernel<TBF16, 4>;
-    else kern = gq == 1 ? decode_step_kernel<TF16, 1> : gq == 2 ? decode_step_kernel<TF16, 2> : decode_step_kernel<TF16, 4>;
+    const bool qk = p.qk_norm || p.has_rope;
+    if (p.dtype == PC_BF16)
+        kern = qk ? pick_step<TBF16, true>(gq) : pick_step<TBF16, false>(gq);
+    else
+        kern = qk ? pick_step<TF16, true>(gq) : pick_step<TF16, false>(gq);
     cudaError_t e = allow_smem(kern, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -889,8 +962,10 @@ uint32_t read_and_clear_step_errors() {
 
 namespace {
 RegisterFunctions reg_step({
-    {"decode_step_f16", reinterpret_cast<const void*>(decode_step_kernel<TF16, 2>)},
-    {"decode_step_bf16", reinterpret_cast<const void*>(decode_step_kernel<TBF16, 2>)},
+    {"decode_step_f16", reinterpret_cast<const void*>(decode_step_kernel<TF16, 2, false>)},
+    {"decode_step_bf16", reinterpret_cast<const void*>(decode_step_kernel<TBF16, 2, false>)},
+    {"decode_step_qk_f16", reinterpret_cast<const void*>(decode_step_kernel<TF16, 2, true>)},
+    {"decode_step_qk_bf16", reinterpret_cast<const void*>(decode_step_kernel<TBF16, 2, true>)},
 });
 }  // namespace
 

@@ -264,6 +264,10 @@ struct DecodeLayer {
     const float* mlp_norm;
     void* k_cache;  // [Nkv, Smax, Hd]
     void* v_cache;
+    const float* q_norm;  // [Hd] per-head norm weights (qk_norm), NULL = none
+    const float* k_norm;
+    const float* rope_cos;  // [rope_rows, Hd/2]; NULL = no RoPE
+    const float* rope_sin;
 };
 struct DecodeStep {
     const DecodeLayer* layers;
@@ -286,6 +290,9 @@ struct DecodeStep {
     int xs_bytes;
     int grid;
     int64_t l2_ahead;  // bytes of L2 prefetch the producer keeps ahead of its ring
+    int qk_norm, norm_v;
+    int has_rope;  // some layer has RoPE tables
+    int64_t rope_rows;
 };
 bool decode_step_plan(DecodeStep& p, int sm_count);
 size_t decode_step_workspace_bytes(const DecodeStep& p);

@@ -1060,6 +1060,12 @@ launch::DecodeStep make_step(const pc_decode_stack_desc* d) {
     p.eps = d->eps; p.scale = d->attn_scale; p.activation = d->activation; p.add_one = d->add_one_to_weight != 0;
     p.dtype = d->dtype;
     p.x = d->x; p.x2 = d->x2; p.h = d->h; p.q = d->q; p.attn = d->attn; p.act = d->act; p.pos = d->position;
+    static_assert(sizeof(pc_decode_layer) == sizeof(launch::DecodeLayer), "decode layer table layout");
+    p.qk_norm = d->qk_norm != 0;
+    p.norm_v = d->norm_v != 0;
+    if (d->rope_rows < 0) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "rope_rows must be >= 0.");
+    p.has_rope = d->rope_rows > 0;
+    p.rope_rows = d->rope_rows < 1 ? 1 : d->rope_rows;
     int dev = 0;
     cudaGetDevice(&dev);
     p.grid = launch::device_info(dev).sm_count;
@@ -1083,7 +1089,8 @@ public:
         p_.po = reinterpret_cast<float*>(ws + off);
         p_.pm = reinterpret_cast<float*>(ws + off + o);
         p_.pl = reinterpret_cast<float*>(ws + off + o + ml);
-        function_names_ = d->dtype == PC_BF16 ? "decode_step_bf16" : "decode_step_f16";
+        function_names_ = std::string(p_.qk_norm || p_.has_rope ? "decode_step_qk_" : "decode_step_") +
+                          (d->dtype == PC_BF16 ? "bf16" : "f16");
         auto t = [](void* ptr, int64_t n, int dt) {
             pc_tensor x{};
             x.data = ptr;

@@ -162,6 +162,7 @@ RegisterFunctions reg_rope({
     {"rope_apply", reinterpret_cast<const void*>(rope_apply_kernel<TF32, TF32, TF32>)},
     {"rope_apply_bf16", reinterpret_cast<const void*>(rope_apply_kernel<TBF16, TBF16, TBF16>)},
     {"rope_apply_f32_tables_bf16", reinterpret_cast<const void*>(rope_apply_kernel<TBF16, TF32, TBF16>)},
+    {"rope_apply_f16", reinterpret_cast<const void*>(rope_apply_kernel<TF16, TF16, TF16>)},
     {"rope_apply_f32_tables_f16", reinterpret_cast<const void*>(rope_apply_kernel<TF16, TF32, TF16>)},
     {"qk_norm_rope_bf16", reinterpret_cast<const void*>(qk_norm_rope_kernel<TBF16>)},
     {"qk_norm_rope_f16", reinterpret_cast<const void*>(qk_norm_rope_kernel<TF16>)},

@@ -90,10 +90,18 @@ class DecodeStack:
     output on exit (it ping-pongs through two buffers).
     """
 
-    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False, vocab=0):
+    def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False, vocab=0,
+                 qk_norm_rope=False, rope_theta=10000.0):
         """vocab > 0 adds the step's tail: the final RMSNorm fused into the LM
         head GEMV (tied embedding [vocab, H]) into `logits`, then Argmax into
-        `token` (int32) — the greedy next token (Argmax.metal)."""
+        `token` (int32) — the greedy next token (Argmax.metal).
+
+        qk_norm_rope adds the Gemma-3/4 attention prologue
+        (Gemma4TextInference.swift:346-381): per-head RMSNorm of q and the new
+        k (weights q_norm / k_norm) and of the new v (no weight), then RoPE of
+        q and k with tables over every position (RopeBuildCosSin, built once
+        here). The per-op path runs it as one QKNormRope launch after the QKV
+        projection; the fused step folds it into the attention items."""
         import torch
         self.shape = shape
         self.library = library
@@ -105,6 +113,18 @@ class DecodeStack:
         s = shape
         tdt = _torch_dtype(s.dtype)
         dev = "cuda:%d" % device
+        self.qk_norm_rope = qk_norm_rope
+        if qk_norm_rope:
+            for w in self.layers:
+                w.q_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
+                w.k_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
+            self.inv_freq = (rope_theta ** (-torch.arange(0, s.Hd, 2, dtype=torch.float32) / s.Hd)).to(dev)
+            self.rope_cos = torch.empty(s.Smax, s.Hd // 2, dtype=torch.float32, device=dev)
+            self.rope_sin = torch.empty_like(self.rope_cos)
+            positions = torch.arange(s.Smax, dtype=torch.int32, device=dev)
+            KernelCommandEncoder(library).encode(
+                Kernels.RopeBuildCosSin(positions, self.inv_freq, self.rope_cos, self.rope_sin, 1.0))
+            torch.cuda.synchronize(dev)
         # One device block holds the step's inputs: the hidden state x, then
         # the position state [pos, pos + 1] (int32) at a 16-byte boundary,
         # so a caller feeds a step with a single host-to-device copy.
@@ -144,6 +164,10 @@ class DecodeStack:
         for i, w in enumerate(self.layers):
             ks.append(Kernels.QKVProjection(cur, w.attn_norm, w.w_qkv, self.q, w.k_cache, w.v_cache, position=pos,
                                             eps=s.eps, add_one_to_weight=True))
+            if self.qk_norm_rope:
+                ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
+                                             self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True,
+                                             norm_v=True))
             ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                                   mask=AttentionMask.causal))
             ks.append(Kernels.MatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
@@ -167,13 +191,16 @@ class DecodeStack:
         dev = self.x.device
         rows = [[w.w_qkv.data_ptr(), w.w_o.data_ptr(), w.w_gate.data_ptr(), w.w_up.data_ptr(), w.w_down.data_ptr(),
                  w.attn_norm.data_ptr(), w.mlp_norm.data_ptr(), w.k_cache.data_ptr(), w.v_cache.data_ptr()]
+                + ([w.q_norm.data_ptr(), w.k_norm.data_ptr(), self.rope_cos.data_ptr(), self.rope_sin.data_ptr()]
+                   if self.qk_norm_rope else [0, 0, 0, 0])
                 for w in self.layers]
         self._layer_table = torch.tensor(rows, dtype=torch.int64).to(dev)
         dt = {"f16": 9, "bf16": 10}[s.dtype]
         desc = N.pc_decode_stack_desc(dt, len(self.layers), s.H, s.Nq, s.Nkv, s.Hd, s.F, s.Smax, s.eps, s.scale,
                                       s.activation, 1, self._layer_table.data_ptr(), self.x.data_ptr(),
                                       self.x2.data_ptr(), self.h.data_ptr(), self.q.data_ptr(),
-                                      self.attn.data_ptr(), self.act.data_ptr(), self.pos_state.data_ptr(), None, 0)
+                                      self.attn.data_ptr(), self.act.data_ptr(), self.pos_state.data_ptr(), None, 0,
+                                      int(self.qk_norm_rope), int(self.qk_norm_rope), s.Smax if self.qk_norm_rope else 0)
         nbytes = DecodeStackKernel.workspace_bytes(desc)
         self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         desc.workspace = self._workspace.data_ptr()
@@ -205,7 +232,8 @@ class DecodeStack:
         L = len(self.layers)
         for i, w in enumerate(self.layers):
             nxt = self.layers[(i + 1) % L]
-            qkv, fd, oproj, mlp, down = ks[5 * i:5 * i + 5]
+            per = len(ks) // L
+            qkv, fd, oproj, mlp, down = [ks[per * i + j] for j in (0, per - 4, per - 3, per - 2, per - 1)]
             qkv.set_l2_prefetch(0, w.k_cache).set_l2_prefetch(1, w.v_cache)
             fd.set_l2_prefetch(0, w.w_o)
             oproj.set_l2_prefetch(0, w.w_gate, min(cap, _nbytes(w.w_gate)))

@@ -118,5 +118,28 @@ def test_decode_layer_whole(dt, act, ctx, pos, fused):
         assert_chain_close(g, e, dt, what="layer output")
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("ctx,pos", [(4096, 4095), (512, 33), (256, 0)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_decode_layer_qk_norm_rope(dt, ctx, pos, fused):
+    """The layer with the Gemma-3/4 attention prologue (per-head q/k/v
+    RMSNorm and RoPE, Gemma4TextInference.swift:346-381): the per-op path
+    (QKNormRope launch) and the fused step (norms and RoPE inside the
+    attention items) against the oracle layer."""
+    from popcorn_b200.decode import LayerShape
+    shape = LayerShape(max_ctx=ctx, dtype=dt)
+    g, e, (kc, vc), ins = ge.smoke_layer(shape, pos=pos, seed=ctx + pos, fused=fused, qk_norm_rope=True)
+    other = np.ones(ctx, bool)
+    other[pos] = False
+    assert np.array_equal(kc[:, other].view(np.uint16), ins["k_cache"][:, other].view(np.uint16))
+    assert_chain_close(g, e, dt, what="layer output")
+    # the normalised, rotated key row and the normalised value row reach the
+    # caches (the oracle layer updated its copies in place)
+    for i, what in ((0, "k row"), (1, "v row")):
+        got = oracle.to_f32(np.ascontiguousarray((kc, vc)[i][:, pos]), dt)
+        ref = oracle.to_f32(np.ascontiguousarray(ins[("k_cache", "v_cache")[i]][:, pos]), dt)
+        assert_chain_close(got, ref, dt, what=what, ulps=4)
+
+
 def test_smoke():
     ge.smoke()
