@@ -104,7 +104,9 @@ PC_API int pc_memcpy_htod_async(void* dst, const void* src, size_t bytes, void* 
 PC_API int pc_memcpy_dtoh_async(void* dst, const void* src, size_t bytes, void* stream);
 PC_API int pc_stream_synchronize(void* stream);
 /* Reads and clears the device-side error word of `device` (bit 0: a bounded
- * wait inside a kernel gave up). 0 when clean. Synchronises the device. */
+ * wait inside a kernel gave up; bit 1: a decode position outside the cache;
+ * bit 4: an embedding id outside the table). 0 when clean. Synchronises the
+ * device. */
 PC_API int pc_device_error_check(int device, uint32_t* flags);
 
 /* ---- KernelLibrary (Sources/Popcorn/KernelLibrary.swift:4-41) ----------- */
@@ -341,6 +343,37 @@ PC_API int pc_kernel_qk_norm_rope(const pc_tensor* q, const pc_tensor* k_cache, 
                                   const pc_tensor* q_norm, const pc_tensor* k_norm, const pc_tensor* cos_t,
                                   const pc_tensor* sin_t, float eps, int32_t add_one_to_weight, int32_t norm_v,
                                   int64_t offset, const pc_tensor* position, pc_kernel** kernel);
+
+/* ---- affine-quantized weights and embedding gathers ----------------------- */
+
+/* Kernels.Matmul(_:_:into:) with an AffineQuantizedTensor RHS (Matmul.swift:
+ * 99-131, 279-351): c [M, N] = a [M, K] . dequant(b)^T, b the logical
+ * [out_features = N, in_features = K] weight stored MLX-style: packed u32
+ * [N, K/8] (bits = 4, value k in bits 4(k%8).. of word k/8), scales and
+ * biases [N, K/group_size] (biases NULL: none; AffineQuantizedTensor.swift).
+ * bits 4 and group_size 64 only; K % 64 == 0. (a, scales, c) dtypes:
+ * bf16/bf16/bf16, bf16/bf16/f32, f32/bf16/f32 (reference) and f16/f16/f16
+ * (extension). fp32 accumulation, one rounding at the store. An encoder with
+ * a scratch allocator splits K over CTAs when the rows are few. */
+PC_API int pc_kernel_matmul_affine_quantized(const pc_tensor* a, const pc_tensor* packed, const pc_tensor* scales,
+                                             const pc_tensor* biases, int64_t out_features, int64_t in_features,
+                                             int32_t bits, int32_t group_size, const pc_tensor* c,
+                                             pc_kernel** kernel);
+/* Kernels.EmbeddingGather(ids:table:into:) (EmbeddingGather.swift): out
+ * [T, H] = table[ids]; ids int32, (table, out) f32/f32, f16/f16, bf16/bf16,
+ * bf16/f32. An id outside the table sets bit 4 of the device error word
+ * and leaves its output row unwritten. */
+PC_API int pc_kernel_embedding_gather(const pc_tensor* ids, const pc_tensor* table, const pc_tensor* out,
+                                      pc_kernel** kernel);
+/* Kernels.EmbeddingGather with an AffineQuantizedTensor table [vocab, H]
+ * (EmbeddingGather.swift, AffineQuantizedEmbeddingGather.metal): rows
+ * dequantised on the fly; ids rank 1 int32; (scales, out) bf16/bf16,
+ * bf16/f32 (reference), f16/f16 (extension); bits 4, group_size 64. */
+PC_API int pc_kernel_embedding_gather_affine_quantized(const pc_tensor* ids, const pc_tensor* packed,
+                                                       const pc_tensor* scales, const pc_tensor* biases,
+                                                       int64_t vocab, int64_t hidden, int32_t bits,
+                                                       int32_t group_size, const pc_tensor* out,
+                                                       pc_kernel** kernel);
 
 /* ---- tensor parallelism over peer memory (extension) ---------------------- */
 

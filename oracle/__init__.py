@@ -56,6 +56,10 @@ def _declare(L):
                                ctypes.c_int32],
         "or_decode_layer": [P, I, P, P, P, P, P, P, P, P, P, L64, L64, L64, L64, L64, L64, L64, F, F,
                             I, P, P, P, I, I, P, P],
+        "or_aq_matmul": [P, I, P, P, P, I, P, I, L64, L64, L64],
+        "or_aq_matmul_exact": [P, I, P, P, P, I, P, L64, L64, L64],
+        "or_embedding_gather": [P, P, I, P, I, L64, L64],
+        "or_aq_embedding_gather": [P, P, P, P, I, P, I, L64, L64],
         "or_set_threads": [I],
     }
     for name, args in sig.items():
@@ -187,6 +191,91 @@ def rope_apply(x, xdt, cos, sin, tdt, odt=None):
     B, T, Nh, Hd = x.shape
     out = np.empty(x.shape, dtype=NP[odt])
     lib().or_rope_apply(_p(x), DT[xdt], _p(cos), _p(sin), DT[tdt], _p(out), DT[odt], B, T, Nh, Hd // 2)
+    return out
+
+
+def aq_quantize(w, group=64, sdt="bf16", bias=True):
+    """MLX-style affine 4-bit quantisation of w [N, K] (float): per group of
+    `group` values scale = (max - min) / 15, bias = min (scale and bias
+    rounded to sdt first), q = clip(round((w - bias) / scale), 0, 15), packed
+    8 per u32 word, lowest index in the lowest bits
+    (AffineQuantizationFormat.swift:22-29). Without bias (the reference's
+    nil-bias case): scale = max|w| / 15, q = clip(round(w / scale), 0, 15).
+    This is test-data generation; the kernels only consume the format.
+    Returns (packed u32 [N, K/8], scales [N, K/group], biases or None)."""
+    w = np.asarray(w, np.float32)
+    N, K = w.shape
+    g = w.reshape(N, K // group, group)
+    lo, hi = g.min(axis=2), g.max(axis=2)
+    if bias:
+        sc = np.maximum((hi - lo) / 15.0, 1e-8).astype(np.float32)
+        scales = to_dtype(sc, sdt)
+        biases = to_dtype(lo, sdt)
+        s32, b32 = to_f32(scales, sdt) if sdt != "f32" else scales, to_f32(biases, sdt) if sdt != "f32" else biases
+        q = np.clip(np.rint((g - b32[..., None]) / s32[..., None]), 0, 15)
+    else:
+        sc = np.maximum(np.abs(g).max(axis=2) / 15.0, 1e-8).astype(np.float32)
+        scales = to_dtype(sc, sdt)
+        biases = None
+        s32 = to_f32(scales, sdt) if sdt != "f32" else scales
+        q = np.clip(np.rint(g / s32[..., None]), 0, 15)
+    q = q.astype(np.uint32).reshape(N, K // 8, 8)
+    packed = np.zeros((N, K // 8), np.uint32)
+    for i in range(8):
+        packed |= q[:, :, i] << np.uint32(4 * i)
+    return packed, scales, biases
+
+
+def aq_dequantize(packed, scales, biases, sdt, K, group=64):
+    """float32 [N, K] = q * scale + bias (fp32 arithmetic, as the kernels)."""
+    N = packed.shape[0]
+    q = np.stack([(packed >> np.uint32(4 * i)) & np.uint32(15) for i in range(8)], axis=-1).reshape(N, K)
+    s = (to_f32(scales, sdt) if sdt != "f32" else scales).astype(np.float32)
+    out = q.astype(np.float32) * np.repeat(s, group, axis=1)
+    if biases is not None:
+        b = (to_f32(biases, sdt) if sdt != "f32" else biases).astype(np.float32)
+        out = out + np.repeat(b, group, axis=1)
+    return out
+
+
+def aq_matmul(x, xdt, packed, scales, biases, sdt, odt):
+    """Affine-quantised Matmul (see or_aq_matmul): x [M, K] . dequant(W)^T."""
+    x, packed, scales = _c(x), _c(np.asarray(packed, np.uint32)), _c(scales)
+    biases = None if biases is None else _c(biases)
+    M, K = x.shape
+    N = packed.shape[0]
+    out = np.empty((M, N), dtype=NP[odt])
+    lib().or_aq_matmul(_p(x), DT[xdt], _p(packed), _p(scales), _p(biases), DT[sdt], _p(out), DT[odt], M, N, K)
+    return out
+
+
+def aq_matmul_exact(x, xdt, packed, scales, biases, sdt):
+    x, packed, scales = _c(x), _c(np.asarray(packed, np.uint32)), _c(scales)
+    biases = None if biases is None else _c(biases)
+    M, K = x.shape
+    N = packed.shape[0]
+    out = np.empty((M, N), dtype=np.float64)
+    lib().or_aq_matmul_exact(_p(x), DT[xdt], _p(packed), _p(scales), _p(biases), DT[sdt], _p(out), M, N, K)
+    return out
+
+
+def embedding_gather(ids, table, tdt, odt=None):
+    """EmbeddingGather.metal: rows of table [V, H] at ids (int32)."""
+    ids, table = _c(np.asarray(ids, np.int32)), _c(table)
+    odt = odt or tdt
+    T, H = ids.size, table.shape[1]
+    out = np.empty((T, H), dtype=NP[odt])
+    lib().or_embedding_gather(_p(ids), _p(table), DT[tdt], _p(out), DT[odt], T, H)
+    return out
+
+
+def aq_embedding_gather(ids, packed, scales, biases, sdt, odt, H):
+    """AffineQuantizedEmbeddingGather.metal: dequantised rows at ids."""
+    ids, packed, scales = _c(np.asarray(ids, np.int32)), _c(np.asarray(packed, np.uint32)), _c(scales)
+    biases = None if biases is None else _c(biases)
+    T = ids.size
+    out = np.empty((T, H), dtype=NP[odt])
+    lib().or_aq_embedding_gather(_p(ids), _p(packed), _p(scales), _p(biases), DT[sdt], _p(out), DT[odt], T, H)
     return out
 
 

@@ -18,6 +18,10 @@
 //   or_mul / or_add        Sources/Popcorn/Kernels/Mul.metal:7-25, Add.metal:7-25
 //   or_rope_build          Sources/Popcorn/Kernels/RopeBuildCosSin.metal:5-21
 //   or_rope_apply          Sources/Popcorn/Kernels/RopeApply.metal:6-49
+//   or_aq_matmul           Sources/Popcorn/Kernels/Quantized/AffineQuantizedMatmul.metal:9-160,
+//                          routing Kernels/Matmul.swift:279-333
+//   or_embedding_gather    Sources/Popcorn/Kernels/EmbeddingGather.metal:6-30
+//   or_aq_embedding_gather Sources/Popcorn/Kernels/Quantized/AffineQuantizedEmbeddingGather.metal:6-27
 //   or_argmax              Sources/Popcorn/Kernels/Argmax.metal:5-76, routing
 //                          Argmax.swift:21 (n >= 32 -> argmax_row)
 //   or_flash_decoding      Sources/Popcorn/Kernels/FlashDecoding.metal:29-231
@@ -550,6 +554,102 @@ void or_attention_exact(const void* q, int qdt, const void* k, const void* v, in
 //   out  = h + d                                   -> dt
 //
 // Weights are [out, in] (transposeB). Caches are [Nkv, Smax, Hd].
+// Affine-quantized Matmul c = a . dequant(b)^T, b [N, K] 4-bit values packed
+// little-endian in u32 words (value i in bits 4(i%8).. of word i/8, 
+// AffineQuantizationFormat.swift:22-29), one scale / bias per 64 values of a
+// row (AffineQuantizedTensor.swift:5-18). Routing and arithmetic of
+// Matmul.swift:279-333: m == 1 follows aq_qmv_fast_typed
+// (AffineQuantizedMatmul.metal:74-160: per lane 16 consecutive k, acc +=
+// scale * sum(x q) + bias * sum(x), then the 32 lanes summed pairwise),
+// m > 1 follows aq_matvec_simd4_typed (:9-69: per lane k = lane, lane+32 ..
+// of each group, acc += x * (q * scale + bias)). biases NULL = no bias.
+static float simd_sum32(const float* v) {
+    float t[32];
+    for (int i = 0; i < 32; ++i) t[i] = v[i];
+    for (int s = 16; s > 0; s >>= 1)
+        for (int i = 0; i < s; ++i) t[i] += t[i + s];
+    return t[0];
+}
+
+void or_aq_matmul(const void* x, int xdt, const uint32_t* w, const void* scales, const void* biases, int sdt,
+                  void* out, int odt, int64_t M, int64_t N, int64_t K) {
+    const int64_t G = 64, kg = K / G, wpr = K / 8;
+    auto q_at = [&](int64_t row, int64_t k) { return (w[row * wpr + k / 8] >> ((k % 8) * 4)) & 15u; };
+#pragma omp parallel for schedule(static)
+    for (int64_t mn = 0; mn < M * N; ++mn) {
+        const int64_t m = mn / N, row = mn % N;
+        float lanes[32] = {0};
+        if (M == 1) {
+            for (int64_t kb = 0; kb < K; kb += 512)
+                for (int lane = 0; lane < 32; ++lane) {
+                    const int64_t k0 = kb + lane * 16;
+                    if (k0 >= K) continue;
+                    float xv[16], sx = 0.f;
+                    for (int j = 0; j < 16; ++j) {
+                        xv[j] = k0 + j < K ? load(x, xdt, m * K + k0 + j) : 0.f;
+                        sx += xv[j];
+                    }
+                    const int64_t g = k0 / G;
+                    const float sc = load(scales, sdt, row * kg + g);
+                    const float bi = biases ? load(biases, sdt, row * kg + g) : 0.f;
+                    float qd = 0.f;
+                    for (int j = 0; j < 16; ++j) qd += xv[j] * float(q_at(row, k0 + j));
+                    lanes[lane] += sc * qd + bi * sx;
+                }
+        } else {
+            for (int64_t g = 0; g < kg; ++g) {
+                const float sc = load(scales, sdt, row * kg + g);
+                const float bi = biases ? load(biases, sdt, row * kg + g) : 0.f;
+                for (int lane = 0; lane < 32; ++lane)
+                    for (int64_t i = lane; i < G; i += 32) {
+                        const int64_t k = g * G + i;
+                        lanes[lane] += load(x, xdt, m * K + k) * (float(q_at(row, k)) * sc + bi);
+                    }
+            }
+        }
+        store(out, odt, m * N + row, simd_sum32(lanes));
+    }
+}
+
+// Exact (float64) dequantised product, for error budgeting.
+void or_aq_matmul_exact(const void* x, int xdt, const uint32_t* w, const void* scales, const void* biases, int sdt,
+                        double* out, int64_t M, int64_t N, int64_t K) {
+    const int64_t kg = K / 64, wpr = K / 8;
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t row = 0; row < N; ++row) {
+            double acc = 0.0;
+            for (int64_t k = 0; k < K; ++k) {
+                const double q = double((w[row * wpr + k / 8] >> ((k % 8) * 4)) & 15u);
+                const double sc = load(scales, sdt, row * kg + k / 64);
+                const double bi = biases ? load(biases, sdt, row * kg + k / 64) : 0.0;
+                acc += double(load(x, xdt, m * K + k)) * (q * sc + bi);
+            }
+            out[m * N + row] = acc;
+        }
+}
+
+// EmbeddingGather.metal:6-30: out[n, :] = table[ids[n], :] (converted).
+void or_embedding_gather(const int32_t* ids, const void* table, int tdt, void* out, int odt, int64_t T, int64_t H) {
+    for (int64_t n = 0; n < T; ++n)
+        for (int64_t h = 0; h < H; ++h) store(out, odt, n * H + h, load(table, tdt, int64_t(ids[n]) * H + h));
+}
+
+// AffineQuantizedEmbeddingGather.metal:6-27: out[n, h] = q * scale + bias of
+// row ids[n] (one rounding at the store).
+void or_aq_embedding_gather(const int32_t* ids, const uint32_t* w, const void* scales, const void* biases, int sdt,
+                            void* out, int odt, int64_t T, int64_t H) {
+    const int64_t kg = H / 64, wpr = H / 8;
+    for (int64_t n = 0; n < T; ++n) {
+        const int64_t row = ids[n];
+        for (int64_t h = 0; h < H; ++h) {
+            const float sc = load(scales, sdt, row * kg + h / 64);
+            const float bi = biases ? load(biases, sdt, row * kg + h / 64) : 0.f;
+            const uint32_t q = (w[row * wpr + h / 8] >> ((h % 8) * 4)) & 15u;
+            store(out, odt, n * H + h, float(q) * sc + bi);
+        }
+    }
+}
+
 void or_decode_layer(const void* x, int dt, const float* w_attn_norm, const float* w_mlp_norm,
                      const void* w_qkv, const void* w_o, const void* w_gate, const void* w_up,
                      const void* w_down, void* k_cache, void* v_cache, int64_t H, int64_t Nq,

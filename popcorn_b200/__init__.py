@@ -5,10 +5,10 @@ The kernels and the C ABI live in ``_lib/libpopcorn_cuda.so`` (sources in
 reference's Swift surface in Python over that ABI; ``decode`` composes the
 decode layer and stack used by the benchmark.
 """
-from .api import (Access, AttentionMask, DataType, FixedScratch, Kernel, KernelCommandEncoder, KernelLibrary,
+from .api import (Access, AffineQuantizedTensor, AttentionMask, DataType, FixedScratch, Kernel, KernelCommandEncoder, KernelLibrary,
                   KernelScratchAllocator, Kernels, PeerGroup, PopcornError, ScratchPool, ScratchSpec, Tensor,
                   device_error_check)
 
-__all__ = ["Access", "AttentionMask", "DataType", "FixedScratch", "Kernel", "KernelCommandEncoder", "KernelLibrary",
+__all__ = ["Access", "AffineQuantizedTensor", "AttentionMask", "DataType", "FixedScratch", "Kernel", "KernelCommandEncoder", "KernelLibrary",
            "KernelScratchAllocator", "Kernels", "PeerGroup", "PopcornError", "ScratchPool", "ScratchSpec", "Tensor",
            "device_error_check"]

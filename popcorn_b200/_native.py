@@ -126,6 +126,9 @@ def _declare(L):
         "pc_kernel_qkv_scatter": ([T, T, T, T, I64, T, PP], I),
         "pc_kernel_argmax": ([T, T, I32, PP], I),
         "pc_kernel_rope_build_cos_sin": ([T, T, T, T, F, PP], I),
+        "pc_kernel_matmul_affine_quantized": ([T, T, T, T, I64, I64, I32, I32, T, PP], I),
+        "pc_kernel_embedding_gather": ([T, T, T, PP], I),
+        "pc_kernel_embedding_gather_affine_quantized": ([T, T, T, T, I64, I64, I32, I32, T, PP], I),
         "pc_kernel_rope_apply": ([T, T, T, T, PP], I),
         "pc_kernel_qk_norm_rope": ([T, T, T, T, T, T, T, F, I32, I32, I64, T, PP], I),
         "pc_ipc_get_handle": ([P, ctypes.POINTER(ctypes.c_uint8)], I),

@@ -81,7 +81,7 @@ def _torch_dtype_map():
     import torch
     return {torch.float32: DataType.f32, torch.float16: DataType.f16, torch.bfloat16: DataType.bf16,
             torch.int32: DataType.i32, torch.int64: DataType.i64, torch.uint8: DataType.u8,
-            torch.int8: DataType.i8, torch.int16: DataType.i16}
+            torch.int8: DataType.i8, torch.int16: DataType.i16, torch.uint32: DataType.u32}
 
 
 class Access(enum.IntFlag):
@@ -406,6 +406,37 @@ def _keep(*ts):
     return tuple(t for t in ts if t is not None)
 
 
+class AffineQuantizedTensor:
+    """AffineQuantizedTensor (Quantization/AffineQuantizedTensor.swift): a
+    logical [out_features, in_features] weight stored as unsigned `bits`-bit
+    values packed little-endian into u32 words (packed_values [out, in / 8]
+    for 4 bits) with one scale / bias per `group_size` consecutive inner
+    values (scales, biases [out, in / group_size]; biases may be None).
+    w = q * scale + bias."""
+
+    def __init__(self, packed_values, scales, biases, shape, bits=4, group_size=64):
+        if biases is not None and (biases.dtype != scales.dtype or tuple(biases.shape) != tuple(scales.shape)):
+            raise PopcornError(-1007, "AffineQuantizedTensor scales and biases must share a data type and shape.")
+        if len(shape) < 2:
+            raise PopcornError(-1008, "AffineQuantizedTensor shape must have rank >= 2.")
+        import torch
+        if isinstance(packed_values, torch.Tensor) and packed_values.dtype == torch.int32:
+            # the same 32-bit words, typed as the format's u32 storage
+            packed_values = Tensor(packed_values.data_ptr(), tuple(packed_values.shape), DataType.u32,
+                                   owner=packed_values)
+        self.packed_values, self.scales, self.biases = packed_values, scales, biases
+        self.shape = tuple(int(d) for d in shape)
+        self.bits, self.group_size = int(bits), int(group_size)
+
+    @property
+    def out_features(self):
+        return self.shape[-2]
+
+    @property
+    def in_features(self):
+        return self.shape[-1]
+
+
 class Kernels:
     """The op namespace (public extension Kernels { ... })."""
 
@@ -463,17 +494,39 @@ class Kernels:
                                  ctypes.c_float(eps), int(add_one_to_weight), keep=_keep(x, weight, into))
 
     class Matmul(Kernel):
-        """Kernels.Matmul(_:_:into:transposeB:) (Matmul.swift:68-93)."""
+        """Kernels.Matmul(_:_:into:transposeB:) (Matmul.swift:68-93); with an
+        AffineQuantizedTensor b, Kernels.Matmul(_:_:into:) (Matmul.swift:
+        99-131): c = a . dequant(b)^T."""
 
         def __init__(self, a, b, into, transpose_b=False, dims=None):
             L = N.lib()
-            if dims is None:
+            if isinstance(b, AffineQuantizedTensor):
+                super().__init__(L.pc_kernel_matmul_affine_quantized, _tc(a), _tc(b.packed_values), _tc(b.scales),
+                                 _tc(b.biases), b.out_features, b.in_features, b.bits, b.group_size, _tc(into),
+                                 keep=_keep(a, b.packed_values, b.scales, b.biases, into))
+            elif dims is None:
                 super().__init__(L.pc_kernel_matmul, _tc(a), _tc(b), _tc(into), int(transpose_b),
                                  keep=_keep(a, b, into))
             else:
                 m, k, n = dims
                 super().__init__(L.pc_kernel_matmul_dims, _tc(a), _tc(b), _tc(into), m, k, n, int(transpose_b),
                                  keep=_keep(a, b, into))
+
+    class EmbeddingGather(Kernel):
+        """Kernels.EmbeddingGather(ids:table:into:) (EmbeddingGather.swift):
+        rows of a dense table, or of an AffineQuantizedTensor dequantised on
+        the fly."""
+
+        def __init__(self, ids, table, into):
+            L = N.lib()
+            if isinstance(table, AffineQuantizedTensor):
+                super().__init__(L.pc_kernel_embedding_gather_affine_quantized, _tc(ids), _tc(table.packed_values),
+                                 _tc(table.scales), _tc(table.biases), table.out_features, table.in_features,
+                                 table.bits, table.group_size, _tc(into),
+                                 keep=_keep(ids, table.packed_values, table.scales, table.biases, into))
+            else:
+                super().__init__(L.pc_kernel_embedding_gather, _tc(ids), _tc(table), _tc(into),
+                                 keep=_keep(ids, table, into))
 
     class GeluTanh(Kernel):
         def __init__(self, x, into):

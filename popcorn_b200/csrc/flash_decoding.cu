@@ -788,6 +788,7 @@ uint32_t read_and_clear_gemm_errors();
 uint32_t read_and_clear_fa_errors();
 uint32_t read_and_clear_allreduce_errors();
 uint32_t read_and_clear_step_errors();
+uint32_t read_and_clear_aq_errors();
 
 }  // namespace launch
 }  // namespace popcorn
@@ -802,7 +803,8 @@ extern "C" int pc_device_error_check(int device, uint32_t* flags) {
     cudaDeviceSynchronize();
     *flags = popcorn::launch::read_and_clear_fd_errors() | popcorn::launch::read_and_clear_gemv_errors() |
              popcorn::launch::read_and_clear_gemm_errors() | popcorn::launch::read_and_clear_step_errors() |
-             popcorn::launch::read_and_clear_fa_errors() | popcorn::launch::read_and_clear_allreduce_errors();
+             popcorn::launch::read_and_clear_fa_errors() | popcorn::launch::read_and_clear_allreduce_errors() |
+             popcorn::launch::read_and_clear_aq_errors();
     cudaSetDevice(prev);
     return PC_OK;
 }

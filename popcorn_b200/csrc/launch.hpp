@@ -214,6 +214,45 @@ struct QKNormRope {
 };
 cudaError_t qk_norm_rope(const QKNormRope& p, cudaStream_t stream);
 
+// Affine-quantized Matmul and the embedding gathers (aq_matmul.cu).
+struct AqMatmul {
+    const void* x;  // [M, K]
+    int x_dtype;
+    const uint32_t* w;   // [N, K/8] 4-bit values, little-endian in u32 words
+    const void* scales;  // [N, K/64]
+    const void* biases;  // [N, K/64] or NULL
+    int s_dtype;
+    void* out;  // [M, N]
+    int out_dtype;
+    int64_t M, N, K;
+    int kslices;      // K groups split over CTAs when > 1 (aq_matmul_plan)
+    int chunk_groups;  // K groups whose x is staged in shared memory at once (set at launch)
+    int no_tma;        // force the register-fed form (tests)
+    void* workspace;  // kslices > 1: aq_matmul_workspace bytes
+    float* ws;
+    unsigned int* cnt;
+};
+struct AqTmaPlan {
+    int ks;           // warps sharing a tile's K (1, 2, 4, 8, 16)
+    int mt, mtiles;   // tokens staged per CTA, token tiles (grid z)
+    size_t smem;
+};
+int aq_matmul_plan(const AqMatmul& p, int sm_count);
+size_t aq_matmul_workspace(const AqMatmul& p, int kslices);
+cudaError_t aq_matmul(const AqMatmul& p, cudaStream_t stream);
+struct EmbeddingGather {
+    const int32_t* ids;  // [T]
+    const void* table;   // dense [vocab, H]
+    int table_dtype;     // dense: table dtype; quantized: scale dtype
+    const uint32_t* packed;  // quantized table [vocab, H/8] (NULL: dense)
+    const void* scales;
+    const void* biases;
+    void* out;  // [T, H]
+    int out_dtype;
+    int64_t T, H, vocab;
+};
+cudaError_t embedding_gather(const EmbeddingGather& p, cudaStream_t stream);
+
 // Kernels.Argmax (argmax.cu).
 struct Argmax {
     const void* x;  // [rows, N]

@@ -734,6 +734,174 @@ private:
 };
 
 // ---------------------------------------------------------------------------
+// Affine-quantized Matmul and embedding gathers (aq_matmul.cu)
+// ---------------------------------------------------------------------------
+// Checks of an AffineQuantizedTensor (AffineQuantizedTensor.swift:22-50) and
+// the format subset the kernels serve (Matmul.swift:323-333).
+void check_affine_quantized(const Tensor& packed, const Tensor& scales, const Tensor* biases, int64_t rows,
+                            int64_t cols, int bits, int group, const char* what) {
+    if (bits != 4 || group != 64)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+             std::string(what) + " supports affine quantized tensors with bits=4, groupSize=64 only.");
+    if (packed.dtype() != PC_U32)
+        fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+             "AffineQuantizedTensor packed values must use u32 for packing uint32LittleEndian.");
+    if (biases && (biases->dtype() != scales.dtype() || !biases->same_shape(scales)))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "AffineQuantizedTensor scales and biases must share a data type and shape.");
+    if (rows < 1 || cols < 1 || cols % group != 0)
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(what) + ": inner size " + std::to_string(cols) +
+                                               " is not divisible by groupSize=" + std::to_string(group) + ".");
+    require_elements(packed, rows * cols / 8, "packed values");
+    require_elements(scales, rows * (cols / group), "scales");
+    if (biases) require_elements(*biases, rows * (cols / group), "biases");
+    if (!aligned16_ptr(packed.data()))
+        fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(what) + ": packed values must be 16-byte aligned.");
+}
+
+class AqMatmulKernel : public Kernel {
+public:
+    AqMatmulKernel(Tensor a, Tensor packed, Tensor scales, const Tensor* biases, int64_t n, int64_t k, int bits,
+                   int group, Tensor c)
+        : a_(a), packed_(packed), scales_(scales), c_(c) {
+        if (a.rank() != 2) fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(a.rank()) + ".");
+        if (c.rank() != 2) fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(c.rank()) + ".");
+        const int64_t m = a[0];
+        if (a[1] != k)  // Matmul.swift:111-115
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul quantized RHS shape mismatch: a.shape=[" + std::to_string(m) +
+                                                   "," + std::to_string(a[1]) + "] but b.inFeatures=" +
+                                                   std::to_string(k) + ".");
+        if (c[0] != m || c[1] != n)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul output shape mismatch: expected [" + std::to_string(m) + "," +
+                                                   std::to_string(n) + "], got " + c.shape_string() + ".");
+        check_affine_quantized(packed, scales, biases, n, k, bits, group, "Matmul quantized RHS");
+        const int xd = a.dtype(), sd = scales.dtype(), od = c.dtype();
+        // Matmul.swift:323-333, plus the f16 extension
+        const bool ok = (xd == PC_BF16 && sd == PC_BF16 && (od == PC_BF16 || od == PC_F32)) ||
+                        (xd == PC_F32 && sd == PC_BF16 && od == PC_F32) ||
+                        (xd == PC_F16 && sd == PC_F16 && od == PC_F16);
+        if (!ok)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+                 std::string("Unsupported affine quantized matmul combination: bits=4 groupSize=64, x=") +
+                     dt_tag(xd) + ", scales=" + dt_tag(sd) + ", out=" + dt_tag(od) + ".");
+        if (!aligned16_ptr(a.data()))
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "Matmul quantized: activations must be 16-byte aligned.");
+        if (biases) {
+            b_ = *biases;
+            has_b_ = true;
+        }
+        p_ = launch::AqMatmul{a.data(), xd, static_cast<const uint32_t*>(packed.data()), scales.data(),
+                              biases ? biases->data() : nullptr, sd, c.data(), od, m, n, k, 1, 0, 0, nullptr,
+                              nullptr, nullptr};
+        // Matmul.swift:302-304
+        function_names_ = std::string(m == 1 ? "aq_qmv_fast_" : "aq_matvec_simd4_") + dt_tag(xd) + "_" + dt_tag(sd) +
+                          "_" + dt_tag(od) + "_b4_g64";
+    }
+    const char* name() const override { return "Matmul"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{a_, PC_ACCESS_READ}, {packed_, PC_ACCESS_READ}, {scales_, PC_ACCESS_READ},
+                                  {c_, PC_ACCESS_WRITE}};
+        if (has_b_) v.push_back({b_, PC_ACCESS_READ});
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::AqMatmul p = p_;
+        const int ks = enc.has_scratch() ? launch::aq_matmul_plan(p, enc.sm_count()) : 1;
+        if (ks <= 1) {
+            enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::aq_matmul(p, s); });
+            return;
+        }
+        p.kslices = ks;
+        std::vector<ScratchSpec> specs = {{{int64_t(launch::aq_matmul_workspace(p, ks))}, PC_U8}};
+        enc.with_temporaries(specs, [&](const std::vector<Tensor>& t) {
+            launch::AqMatmul q = p;
+            q.workspace = t[0].data();
+            std::vector<Binding> b = tensors();
+            b.push_back({t[0], PC_ACCESS_READ_WRITE});
+            enc.dispatch(function_names_, b, [q](cudaStream_t s) { return launch::aq_matmul(q, s); });
+        });
+    }
+
+private:
+    Tensor a_, packed_, scales_, c_, b_;
+    bool has_b_ = false;
+    launch::AqMatmul p_{};
+};
+
+class EmbeddingGatherKernel : public Kernel {
+public:
+    // dense table: EmbeddingGather.swift:12-44
+    EmbeddingGatherKernel(Tensor ids, Tensor table, Tensor out) : ids_(ids), table_(table), out_(out) {
+        if (table.rank() != 2)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(table.rank()) + ".");
+        if (out.rank() < 1 || ids.element_count() != out[0])
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "EmbeddingGather output first dimension must match ids element count; got " +
+                                                   out.shape_string() + ", ids count " +
+                                                   std::to_string(ids.element_count()) + ".");
+        if (out.rank() != 2 || out[1] != table[1])
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "EmbeddingGather output shape must be [ids.count, " +
+                                                   std::to_string(table[1]) + "]; got " + out.shape_string() + ".");
+        if (ids.dtype() != PC_I32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "EmbeddingGather ids must be i32.");
+        const int td = table.dtype(), od = out.dtype();
+        const char* fn = nullptr;
+        if (td == PC_F32 && od == PC_F32) fn = "embedding_gather";
+        else if (td == PC_F16 && od == PC_F16) fn = "embedding_gather_f16";
+        else if (td == PC_BF16 && od == PC_BF16) fn = "embedding_gather_bf16";
+        else if (td == PC_BF16 && od == PC_F32) fn = "embedding_gather_bf16_to_f32";
+        else
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, std::string("Unsupported embedding gather data type combination: ") +
+                                                               dt_tag(td) + ", " + dt_tag(od) + ".");
+        function_names_ = fn;
+        p_ = launch::EmbeddingGather{static_cast<const int32_t*>(ids.data()), table.data(), td, nullptr, nullptr,
+                                     nullptr, out.data(), od, ids.element_count(), table[1], table[0]};
+    }
+    // quantized table: EmbeddingGather.swift:46-95
+    EmbeddingGatherKernel(Tensor ids, Tensor packed, Tensor scales, const Tensor* biases, int64_t vocab, int64_t H,
+                          int bits, int group, Tensor out)
+        : ids_(ids), table_(packed), scales_(scales), out_(out), quantized_(true) {
+        if (ids.rank() != 1)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 1, got rank " + std::to_string(ids.rank()) + ".");
+        if (ids.dtype() != PC_I32)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "EmbeddingGather with quantized table requires i32 ids.");
+        if (out.rank() != 2)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(out.rank()) + ".");
+        if (out[0] != ids[0] || out[1] != H)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "EmbeddingGather output shape mismatch: expected [" +
+                                                   std::to_string(ids[0]) + "," + std::to_string(H) + "], got " +
+                                                   out.shape_string() + ".");
+        check_affine_quantized(packed, scales, biases, vocab, H, bits, group, "EmbeddingGather");
+        const int sd = scales.dtype(), od = out.dtype();
+        const bool ok = (sd == PC_BF16 && (od == PC_BF16 || od == PC_F32)) || (sd == PC_F16 && od == PC_F16);
+        if (!ok)
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, std::string("Unsupported quantized embedding gather: scales=") +
+                                                               dt_tag(sd) + ", out=" + dt_tag(od) + ".");
+        if (biases) {
+            b_ = *biases;
+            has_b_ = true;
+        }
+        function_names_ = std::string("aq_embedding_gather_") + dt_tag(sd) + "_" + dt_tag(od) + "_b4_g64";
+        p_ = launch::EmbeddingGather{static_cast<const int32_t*>(ids.data()), nullptr, sd,
+                                     static_cast<const uint32_t*>(packed.data()), scales.data(),
+                                     biases ? biases->data() : nullptr, out.data(), od, ids[0], H, vocab};
+    }
+    const char* name() const override { return "EmbeddingGather"; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{ids_, PC_ACCESS_READ}, {table_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
+        if (quantized_) v.push_back({scales_, PC_ACCESS_READ});
+        if (has_b_) v.push_back({b_, PC_ACCESS_READ});
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::EmbeddingGather p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::embedding_gather(p, s); });
+    }
+
+private:
+    Tensor ids_, table_, scales_, out_, b_;
+    bool quantized_ = false, has_b_ = false;
+    launch::EmbeddingGather p_{};
+};
+
+// ---------------------------------------------------------------------------
 // Rotary embedding (rope.cu)
 // ---------------------------------------------------------------------------
 class RopeBuildCosSinKernel : public Kernel {
@@ -1455,6 +1623,42 @@ int pc_kernel_gated_activation(const pc_tensor* gate_up, int32_t activation, con
     PC_GUARD_BEGIN
     return wrap(std::make_unique<GatedActivationKernel>(tensor_arg(gate_up, "gate_up"), activation,
                                                         tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_matmul_affine_quantized(const pc_tensor* a, const pc_tensor* packed, const pc_tensor* scales,
+                                      const pc_tensor* biases, int64_t out_features, int64_t in_features,
+                                      int32_t bits, int32_t group_size, const pc_tensor* c, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor b;
+    if (biases) b = tensor_arg(biases, "biases");
+    return wrap(std::make_unique<AqMatmulKernel>(tensor_arg(a, "a"), tensor_arg(packed, "packed"),
+                                                 tensor_arg(scales, "scales"), biases ? &b : nullptr, out_features,
+                                                 in_features, bits, group_size, tensor_arg(c, "c")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_embedding_gather(const pc_tensor* ids, const pc_tensor* table, const pc_tensor* out,
+                               pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<EmbeddingGatherKernel>(tensor_arg(ids, "ids"), tensor_arg(table, "table"),
+                                                        tensor_arg(out, "out")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_embedding_gather_affine_quantized(const pc_tensor* ids, const pc_tensor* packed,
+                                                const pc_tensor* scales, const pc_tensor* biases, int64_t vocab,
+                                                int64_t hidden, int32_t bits, int32_t group_size,
+                                                const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor b;
+    if (biases) b = tensor_arg(biases, "biases");
+    return wrap(std::make_unique<EmbeddingGatherKernel>(tensor_arg(ids, "ids"), tensor_arg(packed, "packed"),
+                                                        tensor_arg(scales, "scales"), biases ? &b : nullptr, vocab,
+                                                        hidden, bits, group_size, tensor_arg(out, "out")),
                 kernel);
     PC_GUARD_END
 }

@@ -229,3 +229,46 @@ def test_rope_dtype_combinations():
         out = oracle.to_f32(oracle.rope_apply(oracle.to_dtype(x, xdt), xdt, oracle.to_dtype(c, tdt),
                                               oracle.to_dtype(s, tdt), tdt), xdt)
         assert np.allclose(out, exact, rtol=tol, atol=tol), (xdt, tdt)
+
+
+def test_aq_format_roundtrip():
+    """4-bit little-endian packing (AffineQuantizationFormat.swift:22-29):
+    value i sits in bits 4(i % 8) .. of word i / 8; dequantisation is
+    q * scale + bias per group of 64 (AffineQuantizedTensor.swift:5-18)."""
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((3, 128)).astype(np.float32)
+    packed, sc, bi = oracle.aq_quantize(w, sdt="f32")
+    assert packed.shape == (3, 16) and sc.shape == (3, 2)
+    q0 = packed[1, 5] >> np.uint32(4 * 3) & np.uint32(15)  # value 43 of row 1
+    assert np.isclose(q0 * sc[1, 0] + bi[1, 0], oracle.aq_dequantize(packed, sc, bi, "f32", 128)[1, 43])
+    deq = oracle.aq_dequantize(packed, sc, bi, "f32", 128)
+    assert np.abs(deq - w).max() <= sc.max() / 2 + 1e-6
+
+
+@pytest.mark.parametrize("M", [1, 3])
+@pytest.mark.parametrize("bias", [True, False])
+def test_aq_matmul_routes(M, bias):
+    """m == 1 (aq_qmv_fast arithmetic) and m > 1 (aq_matvec_simd4
+    arithmetic) both equal the float64 dequantised product within fp32
+    accumulation error."""
+    rng = np.random.default_rng(M)
+    K, N = 640, 24
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.05
+    if not bias:
+        w = np.abs(w)
+    packed, sc, bi = oracle.aq_quantize(w, sdt="bf16", bias=bias)
+    x = oracle.to_dtype(rng.standard_normal((M, K)), "bf16")
+    got = oracle.aq_matmul(x, "bf16", packed, sc, bi, "bf16", "f32")
+    exact = oracle.aq_matmul_exact(x, "bf16", packed, sc, bi, "bf16")
+    assert np.allclose(got, exact, rtol=1e-4, atol=1e-4)
+
+
+def test_embedding_gather():
+    rng = np.random.default_rng(1)
+    table = oracle.to_dtype(rng.standard_normal((50, 128)), "bf16")
+    ids = np.array([3, 0, 49, 3], np.int32)
+    assert np.array_equal(oracle.embedding_gather(ids, table, "bf16"), table[ids])
+    packed, sc, bi = oracle.aq_quantize(oracle.to_f32(table, "bf16"), sdt="bf16")
+    deq = oracle.aq_dequantize(packed, sc, bi, "bf16", 128)
+    got = oracle.aq_embedding_gather(ids, packed, sc, bi, "bf16", "f32", 128)
+    assert np.array_equal(got, deq[ids])
