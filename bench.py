@@ -408,6 +408,60 @@ def run_tp(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def time_aq_matvec(pc, enc, stream, shape, copies=4, reps=10):
+    """Affine 4-bit quantized Matmul (Kernels.Matmul with an
+    AffineQuantizedTensor) at batch 1: algorithmic bytes = packed weights +
+    scales + biases + x + out, CUDA events over graph replays."""
+    import torch
+    hbm = peaks()[0]
+
+    def qt(n, k):
+        packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device="cuda")
+        sc = (torch.rand(n, k // 64, device="cuda") * 0.002).bfloat16()
+        bi = (torch.randn(n, k // 64, device="cuda") * 0.01).bfloat16()
+        return pc.AffineQuantizedTensor(packed, sc, bi, (n, k))
+
+    def qbytes(n, k):
+        return n * k // 2 + 2 * n * (k // 64) * 2 + k * 2 + n * 2
+
+    def timed(kernels, nbytes):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enc.encode(*kernels)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1000.0 / reps
+        del g
+        return us, nbytes / (us * 1e-6) / 1e9
+
+    H, F, Nq, Nkv, Hd = shape.H, shape.F, shape.Nq, shape.Nkv, shape.Hd
+    shapes = [((Nq + 2 * Nkv) * Hd, H), (H, Nq * Hd), (F, H), (F, H), (H, F)]
+    x_in = {k: torch.randn(1, k, device="cuda").bfloat16() for k in {s_[1] for s_ in shapes}}
+    ks, nbytes = [], 0
+    for _ in range(copies):
+        for n, k in shapes:
+            ks.append(pc.Kernels.Matmul(x_in[k], qt(n, k), torch.empty(1, n, device="cuda", dtype=torch.bfloat16)))
+            nbytes += qbytes(n, k)
+    layer_us, layer_gbs = timed(ks, nbytes)
+    del ks
+    head = qt(256000, H)
+    head_us, head_gbs = timed([pc.Kernels.Matmul(x_in[H], head, torch.empty(1, 256000, device="cuda",
+                                                                            dtype=torch.bfloat16))],
+                              qbytes(256000, H))
+    del head
+    return {"kernel": "aq_qmv_tma (mma.sync m16n8k16 bf16, TMA rings), bf16 x / scales / out",
+            "layer_us": layer_us / copies, "layer_gbs": layer_gbs, "layer_frac_of_measured_hbm": layer_gbs / hbm,
+            "lm_head_us": head_us, "lm_head_gbs": head_gbs, "lm_head_frac_of_measured_hbm": head_gbs / hbm,
+            "bytes_per_layer": nbytes // copies}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -572,6 +626,11 @@ def main():
         tail_bytes = 256000 * shape.H * 2 + 256000 * 2
         del g_t, tail
 
+        # ---- 4-bit affine weights (MLX format, group 64, bf16 scales / biases):
+        # the config-2 layer's five GEMVs at batch 1 over 4 distinct layer copies
+        # (175 MB > L2) and the LM head (256000 x 2304), each from a graph ----
+        aq = time_aq_matvec(pc, enc, stream, shape)
+
         # ---- the same step as one persistent kernel (DecodeStack(fused=True)) ----
         fused = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, fused=True)
         fused.set_position(pos)
@@ -640,6 +699,7 @@ def main():
         "lm_head_argmax": {"kernels": "RMSNorm + LM head GEMV (vocab 256000) + Argmax", "us": tail_us,
                            "bytes": tail_bytes, "gbs": tail_bytes / (tail_us * 1e-6) / 1e9,
                            "frac_of_measured_hbm": tail_bytes / (tail_us * 1e-6) / 1e9 / hbm_gbs},
+        "aq_matvec": aq,
         "fused_step": {"kernel": "decode_step_f16 (one persistent launch per token, all 26 layers)",
                        "ms_per_step": fused_ms, "tok_s": 1000.0 / fused_ms,
                        "step_hbm_gbs": bytes_step / (fused_ms * 1e-3) / 1e9, "device_error_word": fused_err},
