@@ -444,6 +444,12 @@ def time_aq_matvec(pc, enc, stream, shape, copies=4, reps=10):
     H, F, Nq, Nkv, Hd = shape.H, shape.F, shape.Nq, shape.Nkv, shape.Hd
     shapes = [((Nq + 2 * Nkv) * Hd, H), (H, Nq * Hd), (F, H), (F, H), (H, F)]
     x_in = {k: torch.randn(1, k, device="cuda").bfloat16() for k in {s_[1] for s_ in shapes}}
+    # the 4-bit LM head first (its first launch is the one a profile captures)
+    head = qt(256000, H)
+    head_us, head_gbs = timed([pc.Kernels.Matmul(x_in[H], head, torch.empty(1, 256000, device="cuda",
+                                                                            dtype=torch.bfloat16))],
+                              qbytes(256000, H))
+    del head
     ks, nbytes = [], 0
     for _ in range(copies):
         for n, k in shapes:
@@ -451,15 +457,23 @@ def time_aq_matvec(pc, enc, stream, shape, copies=4, reps=10):
             nbytes += qbytes(n, k)
     layer_us, layer_gbs = timed(ks, nbytes)
     del ks
-    head = qt(256000, H)
-    head_us, head_gbs = timed([pc.Kernels.Matmul(x_in[H], head, torch.empty(1, 256000, device="cuda",
-                                                                            dtype=torch.bfloat16))],
-                              qbytes(256000, H))
-    del head
     return {"kernel": "aq_qmv_tma (mma.sync m16n8k16 bf16, TMA rings), bf16 x / scales / out",
             "layer_us": layer_us / copies, "layer_gbs": layer_gbs, "layer_frac_of_measured_hbm": layer_gbs / hbm,
             "lm_head_us": head_us, "lm_head_gbs": head_gbs, "lm_head_frac_of_measured_hbm": head_gbs / hbm,
             "bytes_per_layer": nbytes // copies}
+
+
+def run_aq(args):
+    """The affine 4-bit GEMV alone (config-2 layer shapes and the LM head)."""
+    import torch
+    import popcorn_b200 as pc
+    from popcorn_b200.decode import LayerShape
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    enc = pc.KernelCommandEncoder(pc.KernelLibrary(0), stream=stream, scratch=pc.ScratchPool())
+    with torch.cuda.stream(stream):
+        res = time_aq_matvec(pc, enc, stream, LayerShape(dtype="bf16"))
+    print(json.dumps({"workload": "aq", "aq_matvec": res, "device_error_word": pc.device_error_check(0)}), flush=True)
 
 
 def main():
@@ -470,7 +484,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
-    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill"])
+    ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill", "aq"])
     ap.add_argument("--tp-layers", type=int, default=42)
     ap.add_argument("--allreduce", default="peer", choices=["peer", "peer-fused", "nccl"],
                     help="tp9b: all-reduce over peer memory with Add + RMSNorm as one kernel after the GEMM "
@@ -487,6 +501,8 @@ def main():
         return run_tp(args)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "aq":
+        return run_aq(args)
 
     import torch
     import torch.distributed as dist
