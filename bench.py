@@ -463,6 +463,36 @@ def time_aq_matvec(pc, enc, stream, shape, copies=4, reps=10):
             "bytes_per_layer": nbytes // copies}
 
 
+def time_aq_step(pc, lib, stream, n_layers, pos, warmup, steps, device):
+    """The decode step over 4-bit affine weights (AqDecodeStack, bf16
+    activations, ctx 4096): CUDA events over graph replays."""
+    import torch
+    from popcorn_b200.decode import AqDecodeStack, LayerShape
+    st = AqDecodeStack(lib, LayerShape(dtype="bf16"), n_layers, seed=77, device=device)
+    st.set_position(pos)
+    st.x.normal_()
+    enc = st.encoder(stream)
+    st.kernels()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        st.encode_step(enc)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    nbytes = st.algorithmic_bytes_per_step(pos + 1)
+    del g, st
+    return {"stack": "AqDecodeStack, %d layers, batch 1, ctx 4096, bf16 activations, 4-bit weights" % n_layers,
+            "ms_per_step": ms, "tok_s": 1000.0 / ms, "bytes_per_step": nbytes,
+            "step_hbm_gbs": nbytes / (ms * 1e-3) / 1e9}
+
+
 def run_aq(args):
     """The affine 4-bit GEMV alone (config-2 layer shapes and the LM head)."""
     import torch
@@ -646,6 +676,7 @@ def main():
         # the config-2 layer's five GEMVs at batch 1 over 4 distinct layer copies
         # (175 MB > L2) and the LM head (256000 x 2304), each from a graph ----
         aq = time_aq_matvec(pc, enc, stream, shape)
+        aq["decode_step"] = time_aq_step(pc, lib, stream, n_layers, pos, args.warmup, min(args.steps, 50), local)
 
         # ---- the same step as one persistent kernel (DecodeStack(fused=True)) ----
         fused = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, fused=True)

@@ -420,6 +420,7 @@ class AffineQuantizedTensor:
         if len(shape) < 2:
             raise PopcornError(-1008, "AffineQuantizedTensor shape must have rank >= 2.")
         import torch
+        self.packed_tensor = packed_values if isinstance(packed_values, torch.Tensor) else None
         if isinstance(packed_values, torch.Tensor) and packed_values.dtype == torch.int32:
             # the same 32-bit words, typed as the format's u32 storage
             packed_values = Tensor(packed_values.data_ptr(), tuple(packed_values.shape), DataType.u32,

@@ -366,7 +366,9 @@ struct AqCursor {
     }
 };
 
-template <class XT, class ST, class OT>
+// ONE: the token tile is a single token (batch-1 decode), known at compile
+// time: only B column 0 and accumulator columns of token 0 carry data.
+template <class XT, class ST, class OT, bool ONE>
 __global__ void __launch_bounds__(kQThreads, 1)
     aq_qmv_tma_kernel(const __grid_constant__ CUtensorMap wmap, const AqMatmul p, const AqTmaPlan q) {
     constexpr bool F16 = std::is_same<XT, TF16>::value;
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     uint4* xs = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(parts) + size_t(ts_count) * q.ks * 512);
     float* sxs = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + size_t(G) * q.mt * NP * 128);
     const int64_t m0 = int64_t(blockIdx.z) * q.mt;
-    const int mt = int(p.M - m0 < q.mt ? p.M - m0 : q.mt);
+    const int mt = ONE ? 1 : int(p.M - m0 < q.mt ? p.M - m0 : q.mt);
 
     if (lane == 0)
         for (int i = 0; i < kQSlots; ++i) mbar_init(smem_u32(&full[warp][i]), 1);
@@ -442,6 +444,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
     __syncthreads();  // x staged, barriers and partial slots initialised
     const bool tok = g < mt;
     const bool has_b = p.biases != nullptr;
+    // per-thread shared offsets: the weights' swizzled 8-byte word pair of
+    // group jl of a segment (row g; row g + 8 is 1 KB further), and x
+    uint32_t woff[4];
+#pragma unroll
+    for (int jl = 0; jl < 4; ++jl) woff[jl] = g * 128 + (t & 1) * 8 + ((((jl << 1) | (t >> 1)) ^ g) << 4);
+    const size_t xstep = size_t(mt) * NP * 8;  // uint4s per group
+    const uint4* xthr = xs + size_t(g) * NP * 8 + t;
 
     AqCursor cc;  // consume cursor
     cc.v = warp;
@@ -470,25 +479,34 @@ __global__ void __launch_bounds__(kQThreads, 1)
             const float sc1[4] = {unpack2<ST>(sb.x).x, unpack2<ST>(sb.x).y, unpack2<ST>(sb.y).x, unpack2<ST>(sb.y).y};
             const float bi0[4] = {unpack2<ST>(ba.x).x, unpack2<ST>(ba.x).y, unpack2<ST>(ba.y).x, unpack2<ST>(ba.y).y};
             const float bi1[4] = {unpack2<ST>(bb.x).x, unpack2<ST>(bb.x).y, unpack2<ST>(bb.y).x, unpack2<ST>(bb.y).y};
+            const uint4* xseg = xthr + size_t(cc.seg) * 4 * xstep;
+            // sum(x) of the segment's four groups (token 0 only when ONE)
+            float4 sx4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if constexpr (ONE) sx4 = *reinterpret_cast<const float4*>(sxs + cc.seg * 4);
 #pragma unroll
             for (int jl = 0; jl < 4; ++jl) {
                 const int j = cc.seg * 4 + jl;
-                const int c = (jl << 1) | (t >> 1);
                 // 128-byte swizzle: 16-byte chunk c of row line g sits at c ^ (g & 7)
-                const unsigned char* l0 = stg + g * 128 + (t & 1) * 8 + ((c ^ g) << 4);
-                const uint2 wa = *reinterpret_cast<const uint2*>(l0);
-                const uint2 wb = *reinterpret_cast<const uint2*>(l0 + 8 * 128);
-                const uint4* xl = xs + ((size_t(j) * mt + g) * NP * 2) * 4 + t;
+                const uint2 wa = *reinterpret_cast<const uint2*>(stg + woff[jl]);
+                const uint2 wb = *reinterpret_cast<const uint2*>(stg + woff[jl] + 8 * 128);
+                const uint4* xl = xseg + jl * xstep;
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 group_mma<F16, NP>(wa.x, wa.y, wb.x, wb.y, xl, xl + 4, tok, d);
                 // D = sum x (kOff + q): acc += scale * D + (bias - kOff * scale) * sum(x)
                 const float k0 = fmaf(-kOff, sc0[jl], bi0[jl]), k1 = fmaf(-kOff, sc1[jl], bi1[jl]);
-                const float sxa = 2 * t < mt ? sxs[j * mt + 2 * t] : 0.f;
-                const float sxb = 2 * t + 1 < mt ? sxs[j * mt + 2 * t + 1] : 0.f;
-                acc[0] += fmaf(sc0[jl], d[0], k0 * sxa);
-                acc[1] += fmaf(sc0[jl], d[1], k0 * sxb);
-                acc[2] += fmaf(sc1[jl], d[2], k1 * sxa);
-                acc[3] += fmaf(sc1[jl], d[3], k1 * sxb);
+                if constexpr (ONE) {
+                    // accumulator columns 2t, 2t + 1: only t == 0, column 0 is a token
+                    const float sxa = jl == 0 ? sx4.x : jl == 1 ? sx4.y : jl == 2 ? sx4.z : sx4.w;
+                    acc[0] += fmaf(sc0[jl], d[0], k0 * sxa);
+                    acc[2] += fmaf(sc1[jl], d[2], k1 * sxa);
+                } else {
+                    const float sxa = 2 * t < mt ? sxs[j * mt + 2 * t] : 0.f;
+                    const float sxb = 2 * t + 1 < mt ? sxs[j * mt + 2 * t + 1] : 0.f;
+                    acc[0] += fmaf(sc0[jl], d[0], k0 * sxa);
+                    acc[1] += fmaf(sc0[jl], d[1], k0 * sxb);
+                    acc[2] += fmaf(sc1[jl], d[2], k1 * sxa);
+                    acc[3] += fmaf(sc1[jl], d[3], k1 * sxb);
+                }
             }
             __syncwarp();  // the slot is refilled by a later issue()
             ++consumed;
@@ -680,10 +698,11 @@ cudaError_t run_tma_o(const CUtensorMap& map, const AqMatmul& p, const AqTmaPlan
         dim3 grid(unsigned(ctas), 1, unsigned(q.mtiles));
         return launch_k(kern, grid, dim3(kQThreads), q.smem, s, map, p, q);
     };
+    const bool one = q.mt == 1;
     switch (p.out_dtype) {
-    case PC_F32: return go(aq_qmv_tma_kernel<XT, ST, TF32>);
-    case PC_F16: return go(aq_qmv_tma_kernel<XT, ST, TF16>);
-    case PC_BF16: return go(aq_qmv_tma_kernel<XT, ST, TBF16>);
+    case PC_F32: return go(one ? aq_qmv_tma_kernel<XT, ST, TF32, true> : aq_qmv_tma_kernel<XT, ST, TF32, false>);
+    case PC_F16: return go(one ? aq_qmv_tma_kernel<XT, ST, TF16, true> : aq_qmv_tma_kernel<XT, ST, TF16, false>);
+    case PC_BF16: return go(one ? aq_qmv_tma_kernel<XT, ST, TBF16, true> : aq_qmv_tma_kernel<XT, ST, TBF16, false>);
     }
     return cudaErrorInvalidValue;
 }

@@ -109,7 +109,7 @@ class DecodeStack:
         self.device = device
         g = torch.Generator(device="cuda:%d" % device)
         g.manual_seed(seed)
-        self.layers = [DecodeLayerWeights(shape, g) for _ in range(n_layers)]
+        self.layers = self._make_layers(shape, g, n_layers)
         s = shape
         tdt = _torch_dtype(s.dtype)
         dev = "cuda:%d" % device
@@ -149,6 +149,9 @@ class DecodeStack:
             self.logits = torch.zeros(1, vocab, dtype=tdt, device=dev)
             self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self._kernels = None
+
+    def _make_layers(self, shape, generator, n_layers):
+        return [DecodeLayerWeights(shape, generator) for _ in range(n_layers)]
 
     def kernels(self):
         """The validated kernel objects of one step (built once)."""
@@ -260,8 +263,104 @@ class DecodeStack:
         return len(self.layers) * self.shape.bytes_per_token(ctx) + lm
 
 
+class AqLayerWeights:
+    """A decode layer whose five weight matrices are affine 4-bit tensors in
+    the reference's MLX format (AffineQuantizedTensor.swift: u32-packed
+    values, bf16 scale and bias per 64 inputs): random q in 0..15 with
+    scales ~0.004 and biases centring each group, so the dequantised weights
+    are ~N(0, 0.02)-sized. W_q/W_k/W_v are one [(Nq+2Nkv)*Hd, H] tensor and
+    W_gate/W_up one [2F, H] tensor (rows F.. are W_up). Norm weights f32, KV
+    cache bf16 N(0, 1)."""
+
+    def __init__(self, shape, generator, device="cuda"):
+        import torch
+        from .api import AffineQuantizedTensor
+        s = shape
+
+        def q4(n, k):
+            packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=generator, device=device,
+                                   dtype=torch.int64).to(torch.int32)
+            sc = (torch.rand(n, k // 64, generator=generator, device=device) * 0.004 + 0.002)
+            bi = (-7.5 * sc + torch.randn(n, k // 64, generator=generator, device=device) * 0.002)
+            return AffineQuantizedTensor(packed, sc.bfloat16(), bi.bfloat16(), (n, k))
+
+        self.attn_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
+        self.mlp_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
+        self.w_qkv = q4((s.Nq + 2 * s.Nkv) * s.Hd, s.H)
+        self.w_o = q4(s.H, s.Nq * s.Hd)
+        self.w_gate_up = q4(2 * s.F, s.H)
+        self.w_down = q4(s.H, s.F)
+        self.k_cache = torch.randn(1, s.Nkv, s.Smax, s.Hd, generator=generator, device=device).bfloat16()
+        self.v_cache = torch.randn(1, s.Nkv, s.Smax, s.Hd, generator=generator, device=device).bfloat16()
+
+    @staticmethod
+    def nbytes(qt):
+        n, k = qt.shape
+        return n * k // 2 + 2 * n * (k // 64) * 2
+
+
+class AqDecodeStack(DecodeStack):
+    """DecodeStack over 4-bit affine weights (bf16 activations): per layer
+
+        xn = RMSNorm(x); qkv = Matmul(xn, W_qkv) -> q, K/V rows (QKVScatter)
+        [QKNormRope]; attn = FlashDecoding; o = Matmul(attn, W_o)
+        h = x + o, hn = RMSNorm(h) (AddRMSNorm); gu = Matmul(hn, [W_gate; W_up])
+        act = act(g) * u (GatedActivation); x' = h + Matmul(act, W_down) (Add)
+
+    — the reference layer (Gemma4TextInference.swift:312-436) with its
+    Matmuls on AffineQuantizedTensor weights (Matmul.swift:99-131), every
+    intermediate stored in bf16 where the reference stores it."""
+
+    def _make_layers(self, shape, generator, n_layers):
+        assert shape.dtype == "bf16", "the 4-bit stack runs bf16 activations"
+        return [AqLayerWeights(shape, generator) for _ in range(n_layers)]
+
+    def kernels(self):
+        import torch
+        if self._kernels is not None:
+            return self._kernels
+        s = self.shape
+        dev = self.x.device
+        pos = self.pos_state[0:1]
+        lens = self.pos_state[1:2]
+        bf = torch.bfloat16
+        self.xn = torch.zeros(1, s.H, dtype=bf, device=dev)
+        self.qkv = torch.zeros(1, (s.Nq + 2 * s.Nkv) * s.Hd, dtype=bf, device=dev)
+        self.o = torch.zeros(1, s.H, dtype=bf, device=dev)
+        self.hn = torch.zeros(1, s.H, dtype=bf, device=dev)
+        self.gu = torch.zeros(1, 2 * s.F, dtype=bf, device=dev)
+        self.dn = torch.zeros(1, s.H, dtype=bf, device=dev)
+        ks = []
+        cur, nxt = self.x, self.x2
+        for w in self.layers:
+            ks.append(Kernels.RMSNorm(cur, w.attn_norm, into=self.xn, eps=s.eps, add_one_to_weight=True))
+            ks.append(Kernels.Matmul(self.xn, w.w_qkv, self.qkv))
+            ks.append(Kernels.QKVScatter(self.qkv, self.q, w.k_cache, w.v_cache, position=pos))
+            if self.qk_norm_rope:
+                ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
+                                             self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True,
+                                             norm_v=True))
+            ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
+                                                  mask=AttentionMask.causal))
+            ks.append(Kernels.Matmul(self.attn.view(1, s.Nq * s.Hd), w.w_o, self.o))
+            ks.append(Kernels.AddRMSNorm(cur, self.o, w.mlp_norm, self.h, self.hn, eps=s.eps, add_one_to_weight=True))
+            ks.append(Kernels.Matmul(self.hn, w.w_gate_up, self.gu))
+            ks.append(Kernels.GatedActivation(self.gu, self.act, activation=s.activation))
+            ks.append(Kernels.Matmul(self.act, w.w_down, self.dn))
+            ks.append(Kernels.Add(self.h, self.dn, into=nxt))
+            cur, nxt = nxt, cur
+        self.out = cur
+        self._kernels = ks
+        return ks
+
+    def algorithmic_bytes_per_step(self, ctx):
+        per = sum(AqLayerWeights.nbytes(t) for t in (self.layers[0].w_qkv, self.layers[0].w_o,
+                                                    self.layers[0].w_gate_up, self.layers[0].w_down))
+        return len(self.layers) * (per + self.shape.kv_bytes(ctx))
+
+
 def _nbytes(t):
     return t.numel() * t.element_size()
 
 
-__all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack"]
+__all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack", "AqLayerWeights", "AqDecodeStack"]
