@@ -359,6 +359,39 @@ PC_API int pc_kernel_matmul_affine_quantized(const pc_tensor* a, const pc_tensor
                                              const pc_tensor* biases, int64_t out_features, int64_t in_features,
                                              int32_t bits, int32_t group_size, const pc_tensor* c,
                                              pc_kernel** kernel);
+/* An AffineQuantizedTensor argument of the fused 4-bit forms. */
+typedef struct pc_affine_quantized {
+    const pc_tensor* packed; /* u32 [out_features, in_features / 8] */
+    const pc_tensor* scales; /* [out_features, in_features / group_size] */
+    const pc_tensor* biases; /* same shape, or NULL */
+    int64_t out_features, in_features;
+    int32_t bits, group_size;
+} pc_affine_quantized;
+
+/* Extensions: the decode forms of the 4-bit Matmul, each equal to a
+ * reference op sequence with its rounding points (bf16 x with bf16 scales,
+ * or f16 / f16; outputs in x's dtype; in_features % 256 == 0, packed values
+ * 16-byte and scales / biases 8-byte aligned):
+ *   aq_rmsnorm_matmul: out = Matmul(RMSNorm(x, norm_weight), w);
+ *   aq_matmul_residual: out = Add(Matmul(x, w), residual);
+ *   aq_gated_mlp: out [rows, F] = act(g) * u, [g, u] = Matmul(RMSNorm(x), w)
+ *     with w's rows interleaved in blocks of 8: rows 16i..16i+7 are gate rows
+ *     8i..8i+7 and rows 16i+8..16i+15 the up rows 8i..8i+7 (F % 8 == 0);
+ *   aq_qkv_projection: Matmul(RMSNorm(x), w_qkv) split into q [B,Nq,1,Hd]
+ *     and the new K/V rows written into the caches [B,Nkv,Smax,Hd] at the
+ *     position (offset, or position int32 [1] on the device). */
+PC_API int pc_kernel_aq_rmsnorm_matmul(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                       int32_t add_one_to_weight, const pc_affine_quantized* w,
+                                       const pc_tensor* out, pc_kernel** kernel);
+PC_API int pc_kernel_aq_matmul_residual(const pc_tensor* x, const pc_affine_quantized* w, const pc_tensor* residual,
+                                        const pc_tensor* out, pc_kernel** kernel);
+PC_API int pc_kernel_aq_gated_mlp(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                  int32_t add_one_to_weight, const pc_affine_quantized* w_gate_up,
+                                  int32_t activation, const pc_tensor* out, pc_kernel** kernel);
+PC_API int pc_kernel_aq_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                       int32_t add_one_to_weight, const pc_affine_quantized* w_qkv,
+                                       const pc_tensor* q_out, const pc_tensor* k_cache, const pc_tensor* v_cache,
+                                       int64_t offset, const pc_tensor* position, pc_kernel** kernel);
 /* Kernels.EmbeddingGather(ids:table:into:) (EmbeddingGather.swift): out
  * [T, H] = table[ids]; ids int32, (table, out) f32/f32, f16/f16, bf16/bf16,
  * bf16/f32. An id outside the table sets bit 4 of the device error word

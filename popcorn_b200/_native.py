@@ -39,6 +39,12 @@ class pc_decode_stack_desc(ctypes.Structure):
                 ("qk_norm", ctypes.c_int32), ("norm_v", ctypes.c_int32), ("rope_rows", ctypes.c_int64)]
 
 
+class pc_affine_quantized(ctypes.Structure):
+    _fields_ = [("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("biases", ctypes.c_void_p),
+                ("out_features", ctypes.c_int64), ("in_features", ctypes.c_int64), ("bits", ctypes.c_int32),
+                ("group_size", ctypes.c_int32)]
+
+
 class pc_scratch_allocator(ctypes.Structure):
     _fields_ = [("ctx", ctypes.c_void_p), ("borrow", BORROW_FN), ("release", RELEASE_FN)]
 
@@ -128,6 +134,11 @@ def _declare(L):
         "pc_kernel_rope_build_cos_sin": ([T, T, T, T, F, PP], I),
         "pc_kernel_matmul_affine_quantized": ([T, T, T, T, I64, I64, I32, I32, T, PP], I),
         "pc_kernel_embedding_gather": ([T, T, T, PP], I),
+        "pc_kernel_aq_rmsnorm_matmul": ([T, T, F, I32, ctypes.POINTER(pc_affine_quantized), T, PP], I),
+        "pc_kernel_aq_matmul_residual": ([T, ctypes.POINTER(pc_affine_quantized), T, T, PP], I),
+        "pc_kernel_aq_gated_mlp": ([T, T, F, I32, ctypes.POINTER(pc_affine_quantized), I32, T, PP], I),
+        "pc_kernel_aq_qkv_projection": ([T, T, F, I32, ctypes.POINTER(pc_affine_quantized), T, T, T, I64, T, PP],
+                                        I),
         "pc_kernel_embedding_gather_affine_quantized": ([T, T, T, T, I64, I64, I32, I32, T, PP], I),
         "pc_kernel_rope_apply": ([T, T, T, T, PP], I),
         "pc_kernel_qk_norm_rope": ([T, T, T, T, T, T, T, F, I32, I32, I64, T, PP], I),

@@ -429,6 +429,17 @@ class AffineQuantizedTensor:
         self.shape = tuple(int(d) for d in shape)
         self.bits, self.group_size = int(bits), int(group_size)
 
+    def c(self):
+        """pc_affine_quantized, plus the pc_tensor structs it points to."""
+        parts = [_tc(self.packed_values), _tc(self.scales), _tc(self.biases)]
+        st = N.pc_affine_quantized()
+        st.packed = ctypes.cast(parts[0], ctypes.c_void_p)
+        st.scales = ctypes.cast(parts[1], ctypes.c_void_p)
+        st.biases = ctypes.cast(parts[2], ctypes.c_void_p) if parts[2] is not None else None
+        st.out_features, st.in_features = self.out_features, self.in_features
+        st.bits, st.group_size = self.bits, self.group_size
+        return st, parts
+
     @property
     def out_features(self):
         return self.shape[-2]
@@ -512,6 +523,47 @@ class Kernels:
                 m, k, n = dims
                 super().__init__(L.pc_kernel_matmul_dims, _tc(a), _tc(b), _tc(into), m, k, n, int(transpose_b),
                                  keep=_keep(a, b, into))
+
+    class AqRMSNormMatmul(Kernel):
+        """Extension: Matmul(RMSNorm(x), w) with a 4-bit AffineQuantizedTensor w."""
+
+        def __init__(self, x, norm_weight, w, into, eps=1e-6, add_one_to_weight=False):
+            st, parts = w.c()
+            super().__init__(N.lib().pc_kernel_aq_rmsnorm_matmul, _tc(x), _tc(norm_weight), ctypes.c_float(eps),
+                             int(add_one_to_weight), ctypes.byref(st), _tc(into),
+                             keep=_keep(x, norm_weight, w.packed_values, w.scales, w.biases, into) + (st, parts))
+
+    class AqMatmulResidual(Kernel):
+        """Extension: Add(Matmul(x, w), residual) with a 4-bit w."""
+
+        def __init__(self, x, w, residual, into):
+            st, parts = w.c()
+            super().__init__(N.lib().pc_kernel_aq_matmul_residual, _tc(x), ctypes.byref(st), _tc(residual),
+                             _tc(into), keep=_keep(x, w.packed_values, w.scales, w.biases, residual, into) + (st, parts))
+
+    class AqGatedMLP(Kernel):
+        """Extension: act(g) * u of [g; u] = Matmul(RMSNorm(x), w_gate_up),
+        w_gate_up's rows interleaved in blocks of 8 (gate, up)."""
+
+        def __init__(self, x, norm_weight, w_gate_up, into, eps=1e-6, add_one_to_weight=False, activation=0):
+            st, parts = w_gate_up.c()
+            super().__init__(N.lib().pc_kernel_aq_gated_mlp, _tc(x), _tc(norm_weight), ctypes.c_float(eps),
+                             int(add_one_to_weight), ctypes.byref(st), int(activation), _tc(into),
+                             keep=_keep(x, norm_weight, w_gate_up.packed_values, w_gate_up.scales, w_gate_up.biases,
+                                        into) + (st, parts))
+
+    class AqQKVProjection(Kernel):
+        """Extension: RMSNorm -> 4-bit Matmul [q; k; v] -> q and the new K/V
+        rows into the caches at the position."""
+
+        def __init__(self, x, norm_weight, w_qkv, q_out, k_cache, v_cache, offset=0, position=None, eps=1e-6,
+                     add_one_to_weight=False):
+            st, parts = w_qkv.c()
+            super().__init__(N.lib().pc_kernel_aq_qkv_projection, _tc(x), _tc(norm_weight), ctypes.c_float(eps),
+                             int(add_one_to_weight), ctypes.byref(st), _tc(q_out), _tc(k_cache), _tc(v_cache),
+                             int(offset), _tc(position),
+                             keep=_keep(x, norm_weight, w_qkv.packed_values, w_qkv.scales, w_qkv.biases, q_out,
+                                        k_cache, v_cache, position) + (st, parts))
 
     class EmbeddingGather(Kernel):
         """Kernels.EmbeddingGather(ids:table:into:) (EmbeddingGather.swift):

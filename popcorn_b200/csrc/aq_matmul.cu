@@ -112,9 +112,20 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) { return float_to_bf16_bi
 // 16-byte vector (plane 0: b0-b3, plane 1: b4-b7; part 1: the lo half of an
 // f32 x), and the groups' sums sum(x) (fp32, in k order) per (j, n). All
 // `nthreads` threads from `tid` take part; the caller synchronises.
+//
+// nscale (optional, fused RMSNorm): token n's value k is staged as
+// round((x * nscale[n]) * w[k]) in x's type — what RMSNorm would have stored
+// (RMSNorm.metal:7-42) — and the group sums are of those values.
+template <class XT>
+__device__ __forceinline__ float norm_value(const AqMatmul& p, float v, float scale, int64_t k) {
+    v *= scale;
+    if (p.norm_weight) v *= p.add_one ? 1.0f + p.norm_weight[k] : p.norm_weight[k];
+    return Elem<XT>::round(v);
+}
+
 template <class XT>
 __device__ __forceinline__ void stage_x(const AqMatmul& p, int64_t m0, int mt, int64_t c0, int cg, uint4* xs,
-                                        float* sxs, int tid, int nthreads) {
+                                        float* sxs, int tid, int nthreads, const float* nscale = nullptr) {
     constexpr bool XF32 = std::is_same<XT, TF32>::value;
     constexpr int NP = XF32 ? 2 : 1;
     auto at = [&](int j, int n, int part, int plane, int tt) -> uint4& {
@@ -130,10 +141,16 @@ __device__ __forceinline__ void stage_x(const AqMatmul& p, int64_t m0, int mt, i
             if constexpr (!XF32) {
                 const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * tt);
                 const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * tt + 1);
-                const uint32_t q[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+                uint32_t q[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float2 f = unpack2<XT>(q[i]);
+                    float2 f = unpack2<XT>(q[i]);
+                    if (nscale) {
+                        const int64_t k = (c0 + j) * 64 + tt * 16 + 2 * i;
+                        f.x = norm_value<XT>(p, f.x, nscale[n], k);
+                        f.y = norm_value<XT>(p, f.y, nscale[n], k + 1);
+                        q[i] = pack2<XT>(f.x, f.y);
+                    }
                     sx += f.x;
                     sx += f.y;
                 }
@@ -145,7 +162,11 @@ __device__ __forceinline__ void stage_x(const AqMatmul& p, int64_t m0, int mt, i
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float4 f = __ldg(reinterpret_cast<const float4*>(src) + 4 * tt + i);
-                    const float e[4] = {f.x, f.y, f.z, f.w};
+                    float e[4] = {f.x, f.y, f.z, f.w};
+                    if (nscale)
+#pragma unroll
+                        for (int h = 0; h < 4; ++h)
+                            e[h] = norm_value<XT>(p, e[h], nscale[n], (c0 + j) * 64 + tt * 16 + 4 * i + h);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const float e0 = e[2 * h], e1 = e[2 * h + 1];
@@ -325,6 +346,61 @@ __global__ void __launch_bounds__(kAqThreads, 2) aq_matmul_kernel(const AqMatmul
     if (lane == 0) p.cnt[tile] = 0u;  // every slice has arrived
 }
 
+// Final values of a warp's 16-row tile: tot[i] is row tile*16 + g + (i < 2 ?
+// 0 : 8), token m0 + 2t + (i & 1). The epilogue keeps the reference's
+// rounding points: Matmul stores round(y); Add (Add.metal) then stores
+// round(round(y) + r); the gated form takes interleaved [gate; up] tiles
+// (rows 16u..16u+7 are gate rows 8u.., rows 16u+8.. the up rows) and stores
+// round(round(act(round(g))) * round(u)) (GeluTanh / Mul .metal); the QKV
+// form stores q and the new K/V rows into the caches at the position
+// (KVCacheWrite.metal:17-26).
+template <class OT>
+__device__ __forceinline__ void aq_epilogue(const AqMatmul& p, int tile, int g, int t, int mt, int64_t m0,
+                                            const float* tot) {
+    if (p.epilogue == kAqGated) {
+        const int64_t F = p.N / 2, n = int64_t(tile) * 8 + g;
+#pragma unroll
+        for (int ii = 0; ii < 2; ++ii) {
+            const int tk = 2 * t + ii;
+            if (n >= F || tk >= mt) continue;
+            const float gt = Elem<OT>::round(tot[ii]), up = Elem<OT>::round(tot[2 + ii]);
+            const float a = Elem<OT>::round(p.activation == 0 ? gelu_tanh(gt) : silu(gt));
+            Elem<OT>::store(p.out, (m0 + tk) * F + n, a * up);
+        }
+        return;
+    }
+    int64_t pos = 0;
+    if (p.epilogue == kAqQKV) {
+        pos = p.pos_dev ? int64_t(*p.pos_dev) : p.offset;
+        if (pos < 0 || pos >= p.Smax) return;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = int64_t(tile) * 16 + g + (i < 2 ? 0 : 8);
+        const int tk = 2 * t + (i & 1);
+        if (row >= p.N || tk >= mt) continue;
+        const int64_t m = m0 + tk;
+        if (p.epilogue == kAqResidual) {
+            Elem<OT>::store(p.out, m * p.N + row, Elem<OT>::round(tot[i]) + Elem<OT>::load(p.residual, m * p.N + row));
+        } else if (p.epilogue == kAqQKV) {
+            if (row < p.q_rows) {
+                Elem<OT>::store(p.q_out, m * p.q_rows + row, tot[i]);
+            } else {
+                int64_t r = row - p.q_rows;
+                void* cache = p.k_cache;
+                if (r >= p.kv_rows) {
+                    r -= p.kv_rows;
+                    cache = p.v_cache;
+                }
+                const int64_t nkv = p.kv_rows / p.Hd;
+                Elem<OT>::store(cache, ((m * nkv + r / p.Hd) * p.Smax + pos) * p.Hd + r % p.Hd, tot[i]);
+            }
+        } else {
+            Elem<OT>::store(p.out, m * p.N + row, tot[i]);
+        }
+    }
+}
+
 // ---- TMA-fed persistent form (K % 256 == 0) --------------------------------
 //
 // One CTA per SM, sixteen warps, each an independent stream: a warp takes
@@ -379,6 +455,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     __shared__ __align__(8) uint64_t full[kQWarps][kQSlots];
     __shared__ unsigned int tile_cnt[2 * kQWarps];
     __shared__ int slot_tile[2 * kQWarps];
+    __shared__ float nscale[8];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -440,7 +517,21 @@ __global__ void __launch_bounds__(kQThreads, 1)
     for (int i = 0; i < kQAhead; ++i) issue();
 
     pdl_wait();
-    stage_x<XT>(p, m0, mt, 0, int(G), xs, sxs, tid, kQThreads);
+    if (p.norm) {
+        // fused RMSNorm: token `warp`'s scale rsqrt(mean(x^2) + eps)
+        if (warp < mt) {
+            const char* row = static_cast<const char*>(p.x) + (m0 + warp) * p.K * Elem<XT>::bytes;
+            float ss = 0.f;
+            for (int64_t k = lane; k < p.K; k += 32) {
+                const float v = Elem<XT>::load(row, k);
+                ss += v * v;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) nscale[warp] = rsqrtf(ss / float(p.K) + p.eps);
+        }
+        __syncthreads();
+    }
+    stage_x<XT>(p, m0, mt, 0, int(G), xs, sxs, tid, kQThreads, p.norm ? nscale : nullptr);
     __syncthreads();  // x staged, barriers and partial slots initialised
     const bool tok = g < mt;
     const bool has_b = p.biases != nullptr;
@@ -515,12 +606,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
         if (!ok) break;
         // element i: row (i < 2 ? r0 : r1), token m0 + 2t + (i & 1)
         if (q.ks == 1) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int64_t row = i < 2 ? r0 : r1;
-                const int tk = 2 * t + (i & 1);
-                if (row < p.N && tk < mt) Elem<OT>::store(p.out, (m0 + tk) * p.N + row, acc[i]);
-            }
+            aq_epilogue<OT>(p, tile, g, t, mt, m0, acc);
             continue;
         }
         // K split over ks warps of this CTA: partial into the tile's slot; the
@@ -543,15 +629,15 @@ __global__ void __launch_bounds__(kQThreads, 1)
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev != unsigned(q.ks) - 1) continue;
         __threadfence_block();
+        float tot[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float sum = 0.f;
             for (int kk = 0; kk < q.ks; ++kk)
                 sum += *reinterpret_cast<volatile float*>(&slot_parts[size_t(kk) * 128 + i * 32 + lane]);
-            const int64_t row = i < 2 ? r0 : r1;
-            const int tk = 2 * t + (i & 1);
-            if (row < p.N && tk < mt) Elem<OT>::store(p.out, (m0 + tk) * p.N + row, sum);
+            tot[i] = sum;
         }
+        aq_epilogue<OT>(p, tile, g, t, mt, m0, tot);
         __syncwarp();
         if (lane == 0) {
             tile_cnt[ts] = 0u;
@@ -721,6 +807,8 @@ cudaError_t aq_matmul(const AqMatmul& p0, cudaStream_t s) {
             return cudaErrorInvalidValue;
         }
     }
+    // the fused forms exist in the TMA form only
+    if (p.norm || p.epilogue != kAqStore) return cudaErrorInvalidValue;
     if (p.kslices < 1) p.kslices = 1;
     if (p.kslices > 1) {
         // partials, then the per-tile arrival counters (zeroed per launch)
@@ -793,6 +881,8 @@ RegisterFunctions reg_aq({
     {"aq_qmv_fast_bf16_bf16_f32_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TBF16, TBF16, TF32>)},
     {"aq_qmv_fast_f32_bf16_f32_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TF32, TBF16, TF32>)},
     {"aq_qmv_fast_f16_f16_f16_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TF16, TF16, TF16>)},
+    {"aq_fused_bf16_b4_g64", reinterpret_cast<const void*>(aq_qmv_tma_kernel<TBF16, TBF16, TBF16, true>)},
+    {"aq_fused_f16_b4_g64", reinterpret_cast<const void*>(aq_qmv_tma_kernel<TF16, TF16, TF16, true>)},
     {"aq_matvec_simd4_bf16_bf16_bf16_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TBF16, TBF16, TBF16>)},
     {"aq_matvec_simd4_bf16_bf16_f32_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TBF16, TBF16, TF32>)},
     {"aq_matvec_simd4_f32_bf16_f32_b4_g64", reinterpret_cast<const void*>(aq_matmul_kernel<TF32, TBF16, TF32>)},

@@ -231,13 +231,28 @@ struct AqMatmul {
     void* workspace;  // kslices > 1: aq_matmul_workspace bytes
     float* ws;
     unsigned int* cnt;
+    // fused forms (TMA form only): RMSNorm of each x row first (norm_weight
+    // f32 [K], NULL with norm = 1: no weight), and the epilogue
+    int norm, add_one;
+    const float* norm_weight;
+    float eps;
+    int epilogue;         // AqEpilogue
+    const void* residual;  // kResidual: [M, N]
+    int activation;        // kGated: 0 GeluTanh, 1 SiLU
+    void* q_out;           // kQKV: q [M, Nq*Hd]; caches [M, Nkv, Smax, Hd]
+    void* k_cache;
+    void* v_cache;
+    int64_t q_rows, kv_rows, Hd, Smax, offset;
+    const int32_t* pos_dev;
 };
+enum AqEpilogue : int { kAqStore = 0, kAqResidual = 1, kAqGated = 2, kAqQKV = 3 };
 struct AqTmaPlan {
     int ks;           // warps sharing a tile's K (1, 2, 4, 8, 16)
     int mt, mtiles;   // tokens staged per CTA, token tiles (grid z)
     size_t smem;
 };
 int aq_matmul_plan(const AqMatmul& p, int sm_count);
+bool aq_tma_plan(const AqMatmul& p, AqTmaPlan& q);
 size_t aq_matmul_workspace(const AqMatmul& p, int kslices);
 cudaError_t aq_matmul(const AqMatmul& p, cudaStream_t stream);
 struct EmbeddingGather {

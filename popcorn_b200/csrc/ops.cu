@@ -827,6 +827,159 @@ private:
     launch::AqMatmul p_{};
 };
 
+// Fused decode forms of the quantized Matmul (TMA form only), each equal to
+// a reference op sequence with its rounding points:
+//   kNormMatmul: RMSNorm -> Matmul            (RMSNorm.metal, Matmul.swift:99-131)
+//   kResidual:   Matmul -> Add(residual)      (Add.metal)
+//   kGated:      RMSNorm -> Matmul [gate; up] (rows interleaved in 8s) -> act * up
+//   kQKV:        RMSNorm -> Matmul [q; k; v] -> q, KVCacheWrite(k, v at pos)
+struct AqWeight {
+    Tensor packed, scales, biases;
+    bool has_b = false;
+    int64_t n = 0, k = 0;
+    int bits = 0, group = 0;
+};
+
+AqWeight aq_weight_arg(const pc_affine_quantized* w, const char* what) {
+    if (!w) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(what) + " is null.");
+    AqWeight r;
+    r.packed = tensor_arg(w->packed, "packed");
+    r.scales = tensor_arg(w->scales, "scales");
+    if (w->biases) {
+        r.biases = tensor_arg(w->biases, "biases");
+        r.has_b = true;
+    }
+    r.n = w->out_features;
+    r.k = w->in_features;
+    r.bits = w->bits;
+    r.group = w->group_size;
+    check_affine_quantized(r.packed, r.scales, r.has_b ? &r.biases : nullptr, r.n, r.k, r.bits, r.group, what);
+    return r;
+}
+
+class AqFusedKernel : public Kernel {
+public:
+    enum Form { kNormMatmul, kResidual, kGated, kQKV };
+    AqFusedKernel(Form form, Tensor x, const Tensor* norm_w, float eps, bool add_one, const AqWeight& w, Tensor out,
+                  const Tensor* residual, int activation, const Tensor* kc, const Tensor* vc, int64_t offset,
+                  const Tensor* pos)
+        : x_(x), w_(w), out_(out) {
+        const int xd = x.dtype();
+        if (!((xd == PC_BF16 && w.scales.dtype() == PC_BF16) || (xd == PC_F16 && w.scales.dtype() == PC_F16)))
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "fused 4-bit forms take bf16 x with bf16 scales, or f16 / f16.");
+        if (out.dtype() != xd) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "output dtype must be x's.");
+        if (x.rank() != 2 || x[1] != w.k)
+            fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "x must be [rows, " + std::to_string(w.k) + "]; got " + x.shape_string() + ".");
+        if (!aligned16_ptr(x.data())) fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "x must be 16-byte aligned.");
+        const int64_t m = x[0];
+        launch::AqMatmul p{};
+        p.x = x.data();
+        p.x_dtype = xd;
+        p.w = static_cast<const uint32_t*>(w.packed.data());
+        p.scales = w.scales.data();
+        p.biases = w.has_b ? w.biases.data() : nullptr;
+        p.s_dtype = w.scales.dtype();
+        p.out = out.data();
+        p.out_dtype = xd;
+        p.M = m;
+        p.N = w.n;
+        p.K = w.k;
+        p.kslices = 1;
+        if (form != kResidual) {
+            p.norm = 1;
+            p.eps = eps;
+            p.add_one = add_one ? 1 : 0;
+            if (norm_w) {
+                if (norm_w->dtype() != PC_F32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "RMSNorm weight must be f32.");
+                require_elements(*norm_w, w.k, "norm weight");
+                p.norm_weight = static_cast<const float*>(norm_w->data());
+                extra_.push_back({*norm_w, PC_ACCESS_READ});
+            }
+        }
+        switch (form) {
+        case kNormMatmul:
+            p.epilogue = launch::kAqStore;
+            if (out.rank() != 2 || out[0] != m || out[1] != w.n)
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "out must be [rows, out_features].");
+            break;
+        case kResidual:
+            p.epilogue = launch::kAqResidual;
+            if (out.rank() != 2 || out[0] != m || out[1] != w.n || !residual || !residual->same_shape(out) ||
+                residual->dtype() != xd)
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "out and residual must be [rows, out_features] of x's dtype.");
+            p.residual = residual->data();
+            extra_.push_back({*residual, PC_ACCESS_READ});
+            break;
+        case kGated:
+            p.epilogue = launch::kAqGated;
+            if (activation != PC_ACT_GELU_TANH && activation != PC_ACT_SILU)
+                fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "unknown activation.");
+            p.activation = activation;
+            if (w.n % 16 != 0 || out.rank() != 2 || out[0] != m || out[1] != w.n / 2)
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "gated: out_features = 2F with F % 8 == 0, out [rows, F].");
+            break;
+        case kQKV: {
+            p.epilogue = launch::kAqQKV;
+            if (!kc || !vc || kc->rank() != 4 || !kc->same_shape(*vc) || out.rank() != 4 || kc->dtype() != xd ||
+                vc->dtype() != xd)
+                fail(PC_ERR_TENSOR_INVALID_RANK, "QKV: q [B,Nq,1,Hd] and caches [B,Nkv,Smax,Hd] of x's dtype.");
+            const int64_t B = out[0], Nq = out[1], Hd = out[3], Nkv = (*kc)[1], Smax = (*kc)[2];
+            if (out[2] != 1 || B != m || (*kc)[0] != B || (*kc)[3] != Hd || (Nq + 2 * Nkv) * Hd != w.n)
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "QKV: out_features must be (Nq + 2 Nkv) * Hd, x [B, H].");
+            if (!pos && (offset < 0 || offset >= Smax))
+                fail(PC_ERR_TENSOR_SHAPE_MISMATCH, "KV cache write offset " + std::to_string(offset) +
+                                                       " outside cache length " + std::to_string(Smax) + ".");
+            p.q_out = out.data();
+            p.k_cache = kc->data();
+            p.v_cache = vc->data();
+            p.q_rows = Nq * Hd;
+            p.kv_rows = Nkv * Hd;
+            p.Hd = Hd;
+            p.Smax = Smax;
+            p.offset = offset;
+            extra_.push_back({*kc, PC_ACCESS_WRITE});
+            extra_.push_back({*vc, PC_ACCESS_WRITE});
+            if (pos) {
+                if (pos->dtype() != PC_I32 || pos->element_count() < 1)
+                    fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "position must be int32 [1].");
+                p.pos_dev = static_cast<const int32_t*>(pos->data());
+                extra_.push_back({*pos, PC_ACCESS_READ});
+            }
+            break;
+        }
+        }
+        launch::AqTmaPlan q{};
+        if (!launch::aq_tma_plan(p, q))
+            fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
+                 "fused 4-bit forms need in_features % 256 == 0, 16-byte aligned packed values and 8-byte aligned "
+                 "scales / biases.");
+        p_ = p;
+        function_names_ = std::string("aq_fused_") + dt_tag(xd) + "_b4_g64";
+        name_ = form == kNormMatmul ? "AqRMSNormMatmul" : form == kResidual ? "AqMatmulResidual"
+                : form == kGated ? "AqGatedMLP" : "AqQKVProjection";
+    }
+    const char* name() const override { return name_; }
+    std::vector<Binding> tensors() const override {
+        std::vector<Binding> v = {{x_, PC_ACCESS_READ}, {w_.packed, PC_ACCESS_READ}, {w_.scales, PC_ACCESS_READ},
+                                  {out_, PC_ACCESS_WRITE}};
+        if (w_.has_b) v.push_back({w_.biases, PC_ACCESS_READ});
+        v.insert(v.end(), extra_.begin(), extra_.end());
+        return v;
+    }
+    void encode(KernelCommandEncoder& enc) const override {
+        launch::AqMatmul p = p_;
+        enc.dispatch(function_names_, tensors(), [p](cudaStream_t s) { return launch::aq_matmul(p, s); });
+    }
+
+private:
+    Tensor x_;
+    AqWeight w_;
+    Tensor out_;
+    std::vector<Binding> extra_;
+    launch::AqMatmul p_{};
+    const char* name_ = "";
+};
+
 class EmbeddingGatherKernel : public Kernel {
 public:
     // dense table: EmbeddingGather.swift:12-44
@@ -1636,6 +1789,61 @@ int pc_kernel_matmul_affine_quantized(const pc_tensor* a, const pc_tensor* packe
     return wrap(std::make_unique<AqMatmulKernel>(tensor_arg(a, "a"), tensor_arg(packed, "packed"),
                                                  tensor_arg(scales, "scales"), biases ? &b : nullptr, out_features,
                                                  in_features, bits, group_size, tensor_arg(c, "c")),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_aq_rmsnorm_matmul(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                int32_t add_one_to_weight, const pc_affine_quantized* w, const pc_tensor* out,
+                                pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(std::make_unique<AqFusedKernel>(AqFusedKernel::kNormMatmul, tensor_arg(x, "x"), norm_weight ? &nw : nullptr,
+                                                eps, add_one_to_weight != 0, aq_weight_arg(w, "w"),
+                                                tensor_arg(out, "out"), nullptr, 0, nullptr, nullptr, 0, nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_aq_matmul_residual(const pc_tensor* x, const pc_affine_quantized* w, const pc_tensor* residual,
+                                 const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor r = tensor_arg(residual, "residual");
+    return wrap(std::make_unique<AqFusedKernel>(AqFusedKernel::kResidual, tensor_arg(x, "x"), nullptr, 0.f, false,
+                                                aq_weight_arg(w, "w"), tensor_arg(out, "out"), &r, 0, nullptr,
+                                                nullptr, 0, nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_aq_gated_mlp(const pc_tensor* x, const pc_tensor* norm_weight, float eps, int32_t add_one_to_weight,
+                           const pc_affine_quantized* w_gate_up, int32_t activation, const pc_tensor* out,
+                           pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    return wrap(std::make_unique<AqFusedKernel>(AqFusedKernel::kGated, tensor_arg(x, "x"), norm_weight ? &nw : nullptr,
+                                                eps, add_one_to_weight != 0, aq_weight_arg(w_gate_up, "w_gate_up"),
+                                                tensor_arg(out, "out"), nullptr, activation, nullptr, nullptr, 0,
+                                                nullptr),
+                kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_aq_qkv_projection(const pc_tensor* x, const pc_tensor* norm_weight, float eps,
+                                int32_t add_one_to_weight, const pc_affine_quantized* w_qkv, const pc_tensor* q_out,
+                                const pc_tensor* k_cache, const pc_tensor* v_cache, int64_t offset,
+                                const pc_tensor* position, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    Tensor nw, pos;
+    if (norm_weight) nw = tensor_arg(norm_weight, "norm_weight");
+    if (position) pos = tensor_arg(position, "position");
+    Tensor kc = tensor_arg(k_cache, "k_cache"), vc = tensor_arg(v_cache, "v_cache");
+    return wrap(std::make_unique<AqFusedKernel>(AqFusedKernel::kQKV, tensor_arg(x, "x"), norm_weight ? &nw : nullptr,
+                                                eps, add_one_to_weight != 0, aq_weight_arg(w_qkv, "w_qkv"),
+                                                tensor_arg(q_out, "q_out"), nullptr, 0, &kc, &vc, offset,
+                                                position ? &pos : nullptr),
                 kernel);
     PC_GUARD_END
 }

@@ -269,8 +269,10 @@ class AqLayerWeights:
     values, bf16 scale and bias per 64 inputs): random q in 0..15 with
     scales ~0.004 and biases centring each group, so the dequantised weights
     are ~N(0, 0.02)-sized. W_q/W_k/W_v are one [(Nq+2Nkv)*Hd, H] tensor and
-    W_gate/W_up one [2F, H] tensor (rows F.. are W_up). Norm weights f32, KV
-    cache bf16 N(0, 1)."""
+    W_gate/W_up one [2F, H] tensor with rows interleaved in blocks of 8 (rows
+    16i..16i+7 are gate rows 8i..8i+7, rows 16i+8..16i+15 the up rows), the
+    layout the fused gated form reads. Norm weights f32, KV cache bf16
+    N(0, 1)."""
 
     def __init__(self, shape, generator, device="cuda"):
         import torch
@@ -288,7 +290,9 @@ class AqLayerWeights:
         self.mlp_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
         self.w_qkv = q4((s.Nq + 2 * s.Nkv) * s.Hd, s.H)
         self.w_o = q4(s.H, s.Nq * s.Hd)
-        self.w_gate_up = q4(2 * s.F, s.H)
+        self.w_gate = q4(s.F, s.H)
+        self.w_up = q4(s.F, s.H)
+        self.w_gate_up = _interleave8(self.w_gate, self.w_up)
         self.w_down = q4(s.H, s.F)
         self.k_cache = torch.randn(1, s.Nkv, s.Smax, s.Hd, generator=generator, device=device).bfloat16()
         self.v_cache = torch.randn(1, s.Nkv, s.Smax, s.Hd, generator=generator, device=device).bfloat16()
@@ -297,6 +301,20 @@ class AqLayerWeights:
     def nbytes(qt):
         n, k = qt.shape
         return n * k // 2 + 2 * n * (k // 64) * 2
+
+
+def _interleave8(a, b):
+    """[a; b] with rows interleaved in blocks of 8 (a's rows 8i..8i+7, then
+    b's), for packed values, scales and biases alike."""
+    import torch
+    from .api import AffineQuantizedTensor
+
+    def il(x, y):
+        n = x.shape[0]
+        return torch.stack([x.view(n // 8, 8, -1), y.view(n // 8, 8, -1)], dim=1).reshape(2 * n, -1).contiguous()
+
+    return AffineQuantizedTensor(il(a.packed_tensor, b.packed_tensor), il(a.scales, b.scales),
+                                 il(a.biases, b.biases), (2 * a.out_features, a.in_features))
 
 
 class AqDecodeStack(DecodeStack):
@@ -311,9 +329,33 @@ class AqDecodeStack(DecodeStack):
     Matmuls on AffineQuantizedTensor weights (Matmul.swift:99-131), every
     intermediate stored in bf16 where the reference stores it."""
 
+    def __init__(self, *args, ops="fused", **kwargs):
+        """ops="fused": five launches per layer (+ the attention's two) —
+        AqQKVProjection (RMSNorm + QKV + KV write), [QKNormRope],
+        FlashDecodingRagged, AqMatmulResidual (o_proj + Add), AqGatedMLP
+        (RMSNorm + gate/up + act * up), AqMatmulResidual (down_proj + Add).
+        ops="reference": the reference's op sequence, one kernel per op."""
+        self.ops = ops
+        super().__init__(*args, **kwargs)
+
     def _make_layers(self, shape, generator, n_layers):
         assert shape.dtype == "bf16", "the 4-bit stack runs bf16 activations"
         return [AqLayerWeights(shape, generator) for _ in range(n_layers)]
+
+    def _fused_layer(self, w, cur, nxt, pos, lens):
+        s = self.shape
+        ks = [Kernels.AqQKVProjection(cur, w.attn_norm, w.w_qkv, self.q, w.k_cache, w.v_cache, position=pos,
+                                      eps=s.eps, add_one_to_weight=True)]
+        if self.qk_norm_rope:
+            ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
+                                         self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True, norm_v=True))
+        ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
+                                              mask=AttentionMask.causal))
+        ks.append(Kernels.AqMatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
+        ks.append(Kernels.AqGatedMLP(self.h, w.mlp_norm, w.w_gate_up, into=self.act, eps=s.eps,
+                                     add_one_to_weight=True, activation=s.activation))
+        ks.append(Kernels.AqMatmulResidual(self.act, w.w_down, self.h, into=nxt))
+        return ks
 
     def kernels(self):
         import torch
@@ -328,11 +370,17 @@ class AqDecodeStack(DecodeStack):
         self.qkv = torch.zeros(1, (s.Nq + 2 * s.Nkv) * s.Hd, dtype=bf, device=dev)
         self.o = torch.zeros(1, s.H, dtype=bf, device=dev)
         self.hn = torch.zeros(1, s.H, dtype=bf, device=dev)
-        self.gu = torch.zeros(1, 2 * s.F, dtype=bf, device=dev)
+        self.g_out = torch.zeros(1, s.F, dtype=bf, device=dev)
+        self.u_out = torch.zeros(1, s.F, dtype=bf, device=dev)
+        self.a_out = torch.zeros(1, s.F, dtype=bf, device=dev)
         self.dn = torch.zeros(1, s.H, dtype=bf, device=dev)
         ks = []
         cur, nxt = self.x, self.x2
         for w in self.layers:
+            if self.ops == "fused":
+                ks += self._fused_layer(w, cur, nxt, pos, lens)
+                cur, nxt = nxt, cur
+                continue
             ks.append(Kernels.RMSNorm(cur, w.attn_norm, into=self.xn, eps=s.eps, add_one_to_weight=True))
             ks.append(Kernels.Matmul(self.xn, w.w_qkv, self.qkv))
             ks.append(Kernels.QKVScatter(self.qkv, self.q, w.k_cache, w.v_cache, position=pos))
@@ -344,8 +392,11 @@ class AqDecodeStack(DecodeStack):
                                                   mask=AttentionMask.causal))
             ks.append(Kernels.Matmul(self.attn.view(1, s.Nq * s.Hd), w.w_o, self.o))
             ks.append(Kernels.AddRMSNorm(cur, self.o, w.mlp_norm, self.h, self.hn, eps=s.eps, add_one_to_weight=True))
-            ks.append(Kernels.Matmul(self.hn, w.w_gate_up, self.gu))
-            ks.append(Kernels.GatedActivation(self.gu, self.act, activation=s.activation))
+            ks.append(Kernels.Matmul(self.hn, w.w_gate, self.g_out))
+            ks.append(Kernels.Matmul(self.hn, w.w_up, self.u_out))
+            ks.append(Kernels.GeluTanh(self.g_out, self.a_out) if s.activation == 0 else
+                      Kernels.SiLU(self.g_out, self.a_out))
+            ks.append(Kernels.Mul(self.a_out, self.u_out, self.act))
             ks.append(Kernels.Matmul(self.act, w.w_down, self.dn))
             ks.append(Kernels.Add(self.h, self.dn, into=nxt))
             cur, nxt = nxt, cur
@@ -355,7 +406,8 @@ class AqDecodeStack(DecodeStack):
 
     def algorithmic_bytes_per_step(self, ctx):
         per = sum(AqLayerWeights.nbytes(t) for t in (self.layers[0].w_qkv, self.layers[0].w_o,
-                                                    self.layers[0].w_gate_up, self.layers[0].w_down))
+                                                    self.layers[0].w_gate, self.layers[0].w_up,
+                                                    self.layers[0].w_down))
         return len(self.layers) * (per + self.shape.kv_bytes(ctx))
 
 

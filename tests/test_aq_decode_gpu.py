@@ -42,18 +42,20 @@ def _oracle_layer(x, w, kc, vc, shape, pos):
     o = mm(attn.reshape(-1), w.w_o)
     h = oracle.add(x, o, bf)
     hn = oracle.rmsnorm(h, bf, w.mlp_norm.cpu().numpy(), eps=s.eps, add_one=True)
-    gu = mm(hn, w.w_gate_up)
-    act = oracle.mul(oracle.gelu_tanh(gu[:s.F], bf), gu[s.F:], bf)
+    act = oracle.mul(oracle.gelu_tanh(mm(hn, w.w_gate), bf), mm(hn, w.w_up), bf)
     d = mm(act, w.w_down)
     return oracle.add(h, d, bf)
 
 
 @pytest.mark.parametrize("ctx,pos", [(512, 300), (4096, 4095)])
-def test_aq_decode_layer(ctx, pos):
+@pytest.mark.parametrize("ops", ["reference", "fused"])
+def test_aq_decode_layer(ctx, pos, ops):
+    """ops="reference": one kernel per reference op; ops="fused": the
+    RMSNorm / residual / activation / KV-write folded into the 4-bit GEMVs."""
     import popcorn_b200 as pc
     from popcorn_b200.decode import AqDecodeStack, LayerShape
     shape = LayerShape(max_ctx=ctx, dtype="bf16")
-    st = AqDecodeStack(pc.KernelLibrary(0), shape, 1, seed=ctx)
+    st = AqDecodeStack(pc.KernelLibrary(0), shape, 1, seed=ctx, ops=ops)
     st.set_position(pos)
     st.x.normal_(generator=torch.Generator(device="cuda").manual_seed(3))
     w = st.layers[0]
@@ -70,12 +72,13 @@ def test_aq_decode_layer(ctx, pos):
                        "bf16", what="k row", ulps=2)
 
 
-def test_aq_decode_stack_repeats():
-    """Two layers, graph-free repeated steps: identical results each time."""
+@pytest.mark.parametrize("ops", ["reference", "fused"])
+def test_aq_decode_stack_repeats(ops):
+    """Two layers, repeated steps: identical results each time."""
     import popcorn_b200 as pc
     from popcorn_b200.decode import AqDecodeStack, LayerShape
     shape = LayerShape(max_ctx=256, dtype="bf16")
-    st = AqDecodeStack(pc.KernelLibrary(0), shape, 2, seed=5)
+    st = AqDecodeStack(pc.KernelLibrary(0), shape, 2, seed=5, ops=ops)
     x0 = torch.randn(1, shape.H, device="cuda").bfloat16()
     enc = st.encoder()
     outs = []

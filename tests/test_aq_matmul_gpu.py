@@ -145,3 +145,65 @@ def test_embedding_gather_bad_id_sets_error(pc):
     torch.cuda.synchronize()
     assert pc.device_error_check(0) & 16
     assert torch.all(out[0] == 0) and torch.all(out[1] == 7.0)
+
+
+def _f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_aq_fused_forms(pc, M):
+    """The fused 4-bit decode forms against their reference op sequences on
+    the oracle: RMSNorm -> Matmul; Matmul -> Add; RMSNorm -> Matmul [gate;
+    up] (8-row interleave) -> GeluTanh * up; RMSNorm -> Matmul -> q + KV write."""
+    rng = np.random.default_rng(M)
+    K, N, eps = 2304, 512, 1e-6
+    bf = "bf16"
+    x = oracle.to_dtype(rng.standard_normal((M, K)), bf)
+    nw = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    qt, packed, sc, bi = _qtensor(pc, rng, N, K, bf)
+    enc = _enc(pc, False)
+    xd = to_dev(x, bf)
+    xn = oracle.rmsnorm(x, bf, nw, eps=eps, add_one=True)
+    # RMSNorm -> Matmul
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    enc.encode(pc.Kernels.AqRMSNormMatmul(xd, to_dev(nw, "f32"), qt, out, eps=eps, add_one_to_weight=True))
+    torch.cuda.synchronize()
+    assert_close(from_dev(out, bf), oracle.aq_matmul(xn, bf, packed, sc, bi, bf, bf), bf, what="norm+matmul",
+                 bf16_ulps=2)
+    # Matmul -> Add(residual)
+    res = oracle.to_dtype(rng.standard_normal((M, N)), bf)
+    out2 = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    enc.encode(pc.Kernels.AqMatmulResidual(xd, qt, to_dev(res, bf), out2))
+    torch.cuda.synchronize()
+    exp2 = oracle.add(oracle.aq_matmul(x, bf, packed, sc, bi, bf, bf), res, bf)
+    assert_close(from_dev(out2, bf), exp2, bf, what="matmul+residual", bf16_ulps=2)
+    # gated: gate / up interleaved in blocks of 8
+    F = N // 2
+    qg, pg, sg, bg = _qtensor(pc, rng, F, K, bf)
+    qu, pu, su, bu = _qtensor(pc, rng, F, K, bf)
+    from popcorn_b200.decode import _interleave8
+    out3 = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    enc.encode(pc.Kernels.AqGatedMLP(xd, to_dev(nw, "f32"), _interleave8(qg, qu), out3, eps=eps,
+                                     add_one_to_weight=True))
+    torch.cuda.synchronize()
+    g = oracle.aq_matmul(xn, bf, pg, sg, bg, bf, bf)
+    u = oracle.aq_matmul(xn, bf, pu, su, bu, bf, bf)
+    exp3 = oracle.mul(oracle.gelu_tanh(g, bf), u, bf)
+    from tests.gpu_util import assert_chain_close
+    assert_chain_close(oracle.to_f32(from_dev(out3, bf), bf), oracle.to_f32(exp3, bf), bf, what="gated", ulps=3)
+    # QKV: q [M, 2, 1, 128], caches [M, 1, 16, 128] written at position 5
+    Nq, Nkv, Hd, Smax, pos = 2, 1, 128, 16, 5
+    qk, pk, sk, bk = _qtensor(pc, rng, (Nq + 2 * Nkv) * Hd, K, bf)
+    q = torch.zeros(M, Nq, 1, Hd, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(M, Nkv, Smax, Hd, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    enc.encode(pc.Kernels.AqQKVProjection(xd, to_dev(nw, "f32"), qk, q, kc, vc,
+                                          position=to_dev(np.array([pos], np.int32), "i32"), eps=eps,
+                                          add_one_to_weight=True))
+    torch.cuda.synchronize()
+    qkv = oracle.aq_matmul(xn, bf, pk, sk, bk, bf, bf)
+    assert_close(from_dev(q, bf).reshape(M, -1), qkv[:, :Nq * Hd], bf, what="q", bf16_ulps=2)
+    assert_close(from_dev(kc, bf)[:, 0, pos], qkv[:, Nq * Hd:(Nq + 1) * Hd], bf, what="k", bf16_ulps=2)
+    assert_close(from_dev(vc, bf)[:, 0, pos], qkv[:, (Nq + 1) * Hd:], bf, what="v", bf16_ulps=2)
+    assert torch.count_nonzero(kc[:, :, :pos]) == 0 and torch.count_nonzero(kc[:, :, pos + 1:]) == 0
