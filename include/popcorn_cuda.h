@@ -258,6 +258,9 @@ PC_API int pc_kernel_add(const pc_tensor* a, const pc_tensor* b, const pc_tensor
  * extension (compared as their exact f32 values). Long rows use caller
  * scratch for their partial winners. */
 PC_API int pc_kernel_argmax(const pc_tensor* x, const pc_tensor* indices, int32_t axis, pc_kernel** kernel);
+/* Kernels.ScalarMul(_:by:into:) (ScalarMul.swift, ScalarMul.metal:6-25):
+ * out = x * scalar, f32 / f16 / bf16, out of x's shape and dtype. */
+PC_API int pc_kernel_scalar_mul(const pc_tensor* x, float scalar, const pc_tensor* out, pc_kernel** kernel);
 /* Extension: SiLU, silu(g) = g / (1 + exp(-g)) (no reference kernel). */
 PC_API int pc_kernel_silu(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel);
 

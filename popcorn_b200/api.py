@@ -585,6 +585,12 @@ class Kernels:
         def __init__(self, x, into):
             super().__init__(N.lib().pc_kernel_gelu_tanh, _tc(x), _tc(into), keep=_keep(x, into))
 
+    class ScalarMul(Kernel):
+        """Kernels.ScalarMul(_:by:into:) (ScalarMul.swift)."""
+
+        def __init__(self, x, by, into):
+            super().__init__(N.lib().pc_kernel_scalar_mul, _tc(x), ctypes.c_float(by), _tc(into), keep=_keep(x, into))
+
     class SiLU(Kernel):
         def __init__(self, x, into):
             super().__init__(N.lib().pc_kernel_silu, _tc(x), _tc(into), keep=_keep(x, into))

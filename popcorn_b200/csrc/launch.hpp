@@ -103,10 +103,10 @@ bool matmul_uses_tensor_cores(const Matmul& p);
 size_t matmul_tcgen05_workspace(const Matmul& p);
 
 // Elementwise: GeluTanh / SiLU (unary) and Mul / Add (binary).
-enum class Unary : int { kGeluTanh = 0, kSilu = 1 };
+enum class Unary : int { kGeluTanh = 0, kSilu = 1, kScalarMul = 2 };
 enum class Binary : int { kMul = 0, kAdd = 1 };
 cudaError_t unary(Unary op, const void* x, int x_dtype, void* out, int out_dtype, int64_t count,
-                  cudaStream_t stream);
+                  cudaStream_t stream, float scalar = 1.0f);
 cudaError_t binary(Binary op, const void* a, const void* b, void* out, int dtype, int64_t count,
                    cudaStream_t stream);
 

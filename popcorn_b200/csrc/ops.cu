@@ -353,9 +353,10 @@ private:
 // ---------------------------------------------------------------------------
 class UnaryKernel : public Kernel {
 public:
-    UnaryKernel(launch::Unary op, Tensor x, Tensor out) : op_(op), x_(x), out_(out) {
-        const char* base = op == launch::Unary::kGeluTanh ? "gelu_tanh" : "silu";
-        const char* opname = op == launch::Unary::kGeluTanh ? "GeluTanh" : "SiLU";
+    UnaryKernel(launch::Unary op, Tensor x, Tensor out, float scalar = 1.0f)
+        : op_(op), x_(x), out_(out), scalar_(scalar) {
+        const char* base = op == launch::Unary::kGeluTanh ? "gelu_tanh" : op == launch::Unary::kSilu ? "silu" : "scalar_mul";
+        const char* opname = op == launch::Unary::kGeluTanh ? "GeluTanh" : op == launch::Unary::kSilu ? "SiLU" : "ScalarMul";
         if (!x.same_shape(out))
             fail(PC_ERR_TENSOR_SHAPE_MISMATCH, std::string(opname) + " output shape must match input; got " +
                                                    out.shape_string() + ", expected " + x.shape_string() + ".");
@@ -374,12 +375,15 @@ public:
         int dt = x_.dtype();
         int64_t n = x_.element_count();
         if (n == 0) return;
-        enc.dispatch(function_names_, tensors(), [=](cudaStream_t s) { return launch::unary(op, x, dt, o, dt, n, s); });
+        const float sc = scalar_;
+        enc.dispatch(function_names_, tensors(),
+                     [=](cudaStream_t s) { return launch::unary(op, x, dt, o, dt, n, s, sc); });
     }
 
 private:
     launch::Unary op_;
     Tensor x_, out_;
+    float scalar_;
     const char* name_;
 };
 
@@ -1687,6 +1691,14 @@ int pc_kernel_gelu_tanh(const pc_tensor* x, const pc_tensor* out, pc_kernel** ke
 int pc_kernel_silu(const pc_tensor* x, const pc_tensor* out, pc_kernel** kernel) {
     PC_GUARD_BEGIN
     return wrap(std::make_unique<UnaryKernel>(launch::Unary::kSilu, tensor_arg(x, "x"), tensor_arg(out, "out")), kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_scalar_mul(const pc_tensor* x, float scalar, const pc_tensor* out, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<UnaryKernel>(launch::Unary::kScalarMul, tensor_arg(x, "x"), tensor_arg(out, "out"),
+                                              scalar),
+                kernel);
     PC_GUARD_END
 }
 

@@ -90,12 +90,13 @@ __global__ void rmsnorm_kernel(RMSNorm p) {
 
 // ---- elementwise (GeluTanh.metal, Mul.metal, Add.metal) -----------------------
 
+// OP 0: GeluTanh, 1: SiLU, 2: ScalarMul (ScalarMul.metal:6-25, x * scalar)
 template <class T, int OP>
-__global__ void unary_kernel(const void* x, void* out, int64_t n) {
+__global__ void unary_kernel(const void* x, void* out, int64_t n, float scalar) {
     pdl_wait();
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
         float v = Elem<T>::load(x, i);
-        Elem<T>::store(out, i, OP == 0 ? gelu_tanh(v) : silu(v));
+        Elem<T>::store(out, i, OP == 0 ? gelu_tanh(v) : OP == 1 ? silu(v) : v * scalar);
     }
 }
 
@@ -161,16 +162,22 @@ cudaError_t rmsnorm(const RMSNorm& p, cudaStream_t stream) {
     }
 }
 
-cudaError_t unary(Unary op, const void* x, int x_dtype, void* out, int, int64_t count, cudaStream_t stream) {
+cudaError_t unary(Unary op, const void* x, int x_dtype, void* out, int, int64_t count, cudaStream_t stream,
+                  float scalar) {
     dim3 g(grid_for(count, 256, current_sm_count())), b(256);
-    bool gelu = op == Unary::kGeluTanh;
+    auto go = [&](auto t) {
+        using T = decltype(t);
+        switch (op) {
+        case Unary::kGeluTanh: return launch_k(unary_kernel<T, 0>, g, b, 0, stream, x, out, count, scalar);
+        case Unary::kSilu: return launch_k(unary_kernel<T, 1>, g, b, 0, stream, x, out, count, scalar);
+        case Unary::kScalarMul: return launch_k(unary_kernel<T, 2>, g, b, 0, stream, x, out, count, scalar);
+        }
+        return cudaErrorInvalidValue;
+    };
     switch (x_dtype) {
-    case PC_F32: return gelu ? launch_k(unary_kernel<TF32, 0>, g, b, 0, stream, x, out, count)
-                             : launch_k(unary_kernel<TF32, 1>, g, b, 0, stream, x, out, count);
-    case PC_F16: return gelu ? launch_k(unary_kernel<TF16, 0>, g, b, 0, stream, x, out, count)
-                             : launch_k(unary_kernel<TF16, 1>, g, b, 0, stream, x, out, count);
-    case PC_BF16: return gelu ? launch_k(unary_kernel<TBF16, 0>, g, b, 0, stream, x, out, count)
-                              : launch_k(unary_kernel<TBF16, 1>, g, b, 0, stream, x, out, count);
+    case PC_F32: return go(TF32{});
+    case PC_F16: return go(TF16{});
+    case PC_BF16: return go(TBF16{});
     default: return cudaErrorInvalidValue;
     }
 }
@@ -205,6 +212,9 @@ RegisterFunctions reg_simple({
     {"silu", reinterpret_cast<const void*>(unary_kernel<TF32, 1>)},
     {"silu_f16", reinterpret_cast<const void*>(unary_kernel<TF16, 1>)},
     {"silu_bf16", reinterpret_cast<const void*>(unary_kernel<TBF16, 1>)},
+    {"scalar_mul", reinterpret_cast<const void*>(unary_kernel<TF32, 2>)},
+    {"scalar_mul_f16", reinterpret_cast<const void*>(unary_kernel<TF16, 2>)},
+    {"scalar_mul_bf16", reinterpret_cast<const void*>(unary_kernel<TBF16, 2>)},
     {"mul", reinterpret_cast<const void*>(binary_kernel<TF32, 0>)},
     {"mul_f16", reinterpret_cast<const void*>(binary_kernel<TF16, 0>)},
     {"mul_bf16", reinterpret_cast<const void*>(binary_kernel<TBF16, 0>)},

@@ -537,3 +537,26 @@ def test_matmul_tcgen05_config4_rows(pc, enc):
     exp = oracle.matmul(a_np, "bf16", from_dev(b, "bf16"), "bf16", "bf16", True)
     got = from_dev(out, "bf16")[rows]
     assert_close(got, exp, "bf16", what="config-4 GEMM rows")
+
+
+def test_scalar_mul_kat(kats):
+    """Kernels.ScalarMul (KernelsTests.swift:78-84): exact."""
+    import popcorn_b200 as pc
+    k = kats["scalar_mul"]
+    x = torch.tensor(k["x"], dtype=torch.float32, device="cuda")
+    out = torch.empty_like(x)
+    pc.KernelCommandEncoder(pc.KernelLibrary(0)).encode(pc.Kernels.ScalarMul(x, by=k["scalar"], into=out))
+    torch.cuda.synchronize()
+    assert out.cpu().tolist() == k["expected"]
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_scalar_mul_16bit(dt):
+    import popcorn_b200 as pc
+    tdt = torch.float16 if dt == "f16" else torch.bfloat16
+    x = torch.randn(1001, device="cuda").to(tdt)
+    out = torch.empty_like(x)
+    pc.KernelCommandEncoder(pc.KernelLibrary(0)).encode(pc.Kernels.ScalarMul(x, by=0.7071, into=out))
+    torch.cuda.synchronize()
+    # one fp32 product, one rounding to the storage type
+    assert torch.equal(out, (x.float() * 0.7071).to(tdt))
