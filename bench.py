@@ -468,7 +468,7 @@ def time_aq_step(pc, lib, stream, n_layers, pos, warmup, steps, device):
     activations, ctx 4096): CUDA events over graph replays."""
     import torch
     from popcorn_b200.decode import AqDecodeStack, LayerShape
-    st = AqDecodeStack(lib, LayerShape(dtype="bf16"), n_layers, seed=77, device=device)
+    st = AqDecodeStack(lib, LayerShape(dtype="bf16"), n_layers, seed=77, device=device, vocab=256000)
     st.set_position(pos)
     st.x.normal_()
     enc = st.encoder(stream)
@@ -488,7 +488,8 @@ def time_aq_step(pc, lib, stream, n_layers, pos, warmup, steps, device):
     ms = a.elapsed_time(b) / steps
     nbytes = st.algorithmic_bytes_per_step(pos + 1)
     del g, st
-    return {"stack": "AqDecodeStack, %d layers, batch 1, ctx 4096, bf16 activations, 4-bit weights" % n_layers,
+    return {"stack": "AqDecodeStack, %d layers + 4-bit LM head (vocab 256000) + Argmax, batch 1, ctx 4096, "
+                     "bf16 activations" % n_layers,
             "ms_per_step": ms, "tok_s": 1000.0 / ms, "bytes_per_step": nbytes,
             "step_hbm_gbs": nbytes / (ms * 1e-3) / 1e9}
 

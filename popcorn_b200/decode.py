@@ -276,15 +276,10 @@ class AqLayerWeights:
 
     def __init__(self, shape, generator, device="cuda"):
         import torch
-        from .api import AffineQuantizedTensor
         s = shape
 
         def q4(n, k):
-            packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=generator, device=device,
-                                   dtype=torch.int64).to(torch.int32)
-            sc = (torch.rand(n, k // 64, generator=generator, device=device) * 0.004 + 0.002)
-            bi = (-7.5 * sc + torch.randn(n, k // 64, generator=generator, device=device) * 0.002)
-            return AffineQuantizedTensor(packed, sc.bfloat16(), bi.bfloat16(), (n, k))
+            return _random_q4(n, k, generator, device)
 
         self.attn_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
         self.mlp_norm = (torch.randn(s.H, generator=generator, device=device) * 0.1).float()
@@ -301,6 +296,18 @@ class AqLayerWeights:
     def nbytes(qt):
         n, k = qt.shape
         return n * k // 2 + 2 * n * (k // 64) * 2
+
+
+def _random_q4(n, k, generator, device):
+    """A random 4-bit affine tensor [n, k]: q uniform in 0..15, bf16 scales
+    ~0.004 and biases centring each group (dequantised values ~N(0, 0.02))."""
+    import torch
+    from .api import AffineQuantizedTensor
+    packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=generator, device=device,
+                           dtype=torch.int64).to(torch.int32)
+    sc = torch.rand(n, k // 64, generator=generator, device=device) * 0.004 + 0.002
+    bi = -7.5 * sc + torch.randn(n, k // 64, generator=generator, device=device) * 0.002
+    return AffineQuantizedTensor(packed, sc.bfloat16(), bi.bfloat16(), (n, k))
 
 
 def _interleave8(a, b):
@@ -329,14 +336,36 @@ class AqDecodeStack(DecodeStack):
     Matmuls on AffineQuantizedTensor weights (Matmul.swift:99-131), every
     intermediate stored in bf16 where the reference stores it."""
 
-    def __init__(self, *args, ops="fused", **kwargs):
+    def __init__(self, *args, ops="fused", vocab=0, **kwargs):
         """ops="fused": five launches per layer (+ the attention's two) —
         AqQKVProjection (RMSNorm + QKV + KV write), [QKNormRope],
         FlashDecodingRagged, AqMatmulResidual (o_proj + Add), AqGatedMLP
         (RMSNorm + gate/up + act * up), AqMatmulResidual (down_proj + Add).
-        ops="reference": the reference's op sequence, one kernel per op."""
+        ops="reference": the reference's op sequence, one kernel per op.
+        vocab > 0: the step's tail on a 4-bit tied embedding [vocab, H]
+        (EmbeddingTable.encodeLMHead, EmbeddingTable.swift:38-46): final
+        RMSNorm fused into the LM head GEMV, then Argmax into `token`."""
+        import torch
         self.ops = ops
         super().__init__(*args, **kwargs)
+        self.vocab = vocab
+        if vocab:
+            s = self.shape
+            g = torch.Generator(device="cuda:%d" % self.device)
+            g.manual_seed(kwargs.get("seed", 0) + 7919)
+            dev = self.x.device
+            self.final_norm = (torch.randn(s.H, generator=g, device=dev) * 0.1).float()
+            self.lm_head = _random_q4(vocab, s.H, g, dev)
+            self.logits = torch.zeros(1, vocab, dtype=torch.bfloat16, device=dev)
+            self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def _tail_kernels(self):
+        if not self.vocab:
+            return []
+        s = self.shape
+        return [Kernels.AqRMSNormMatmul(self.out, self.final_norm, self.lm_head, self.logits, eps=s.eps,
+                                        add_one_to_weight=True),
+                Kernels.Argmax(self.logits, self.token)]
 
     def _make_layers(self, shape, generator, n_layers):
         assert shape.dtype == "bf16", "the 4-bit stack runs bf16 activations"
@@ -401,6 +430,7 @@ class AqDecodeStack(DecodeStack):
             ks.append(Kernels.Add(self.h, self.dn, into=nxt))
             cur, nxt = nxt, cur
         self.out = cur
+        ks += self._tail_kernels()
         self._kernels = ks
         return ks
 
@@ -408,7 +438,8 @@ class AqDecodeStack(DecodeStack):
         per = sum(AqLayerWeights.nbytes(t) for t in (self.layers[0].w_qkv, self.layers[0].w_o,
                                                     self.layers[0].w_gate, self.layers[0].w_up,
                                                     self.layers[0].w_down))
-        return len(self.layers) * (per + self.shape.kv_bytes(ctx))
+        head = AqLayerWeights.nbytes(self.lm_head) if self.vocab else 0
+        return len(self.layers) * (per + self.shape.kv_bytes(ctx)) + head
 
 
 def _nbytes(t):

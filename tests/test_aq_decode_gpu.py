@@ -88,3 +88,23 @@ def test_aq_decode_stack_repeats(ops):
         outs.append(st.encode_step(enc).clone())
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+def test_aq_decode_tail():
+    """The 4-bit LM head with the final RMSNorm fused, then Argmax: logits
+    against RMSNorm -> quantized Matmul on the oracle, the token against the
+    reference Argmax of the GPU's logits."""
+    import popcorn_b200 as pc
+    from popcorn_b200.decode import AqDecodeStack, LayerShape
+    shape = LayerShape(max_ctx=128, dtype="bf16")
+    st = AqDecodeStack(pc.KernelLibrary(0), shape, 1, seed=9, vocab=4096)
+    st.set_position(50)
+    st.encode_step(st.encoder())
+    torch.cuda.synchronize()
+    h = _host16(st.out)[0]
+    hn = oracle.rmsnorm(h, "bf16", st.final_norm.cpu().numpy(), eps=shape.eps, add_one=True)
+    packed, sc, bi = _q(st.lm_head)
+    exp = oracle.aq_matmul(hn.reshape(1, -1), "bf16", packed, sc, bi, "bf16", "bf16")
+    got = _host16(st.logits)
+    assert_chain_close(oracle.to_f32(got, "bf16"), oracle.to_f32(exp, "bf16"), "bf16", what="logits", ulps=3)
+    assert st.token.item() == int(oracle.argmax(got, "bf16")[0])
