@@ -516,16 +516,39 @@ __global__ void __launch_bounds__(kQThreads, 1)
 
     pdl_wait();
     if (p.norm) {
-        // fused RMSNorm: token `warp`'s scale rsqrt(mean(x^2) + eps)
-        if (warp < mt) {
-            const char* row = static_cast<const char*>(p.x) + (m0 + warp) * p.K * Elem<XT>::bytes;
+        // fused RMSNorm: token n's scale rsqrt(mean(x^2) + eps). Each (group,
+        // token) unit's sum of squares goes to the sums area first (one
+        // 16-byte load per 8 values, all in flight at once), then summed in
+        // group order; the staging pass below re-reads x from L1.
+        for (int u = tid; u < int(G) * mt; u += kQThreads) {
+            const int j = u / mt, n = u % mt;
+            const char* src = static_cast<const char*>(p.x) + ((m0 + n) * p.K + int64_t(j) * 64) * Elem<XT>::bytes;
             float ss = 0.f;
-            for (int64_t k = lane; k < p.K; k += 32) {
-                const float v = Elem<XT>::load(row, k);
-                ss += v * v;
+            if constexpr (!XF32) {
+                uint4 c[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) c[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float f[8];
+                    unpack8<XT>(c[i], f);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+                }
+            } else {
+                float4 c[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) c[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) ss += c[i].x * c[i].x + c[i].y * c[i].y + c[i].z * c[i].z + c[i].w * c[i].w;
             }
-            ss = warp_sum(ss);
-            if (lane == 0) nscale[warp] = rsqrtf(ss / float(p.K) + p.eps);
+            sxs[j * mt + n] = ss;
+        }
+        __syncthreads();
+        if (tid < mt) {
+            float ss = 0.f;
+            for (int j = 0; j < int(G); ++j) ss += sxs[j * mt + tid];
+            nscale[tid] = rsqrtf(ss / float(p.K) + p.eps);
         }
         __syncthreads();
     }
