@@ -720,7 +720,8 @@ def main():
     kernels = {}
     for n, us in kern_us.items():
         b = per_launch_bytes[n]
-        kernels[n] = {"us": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9, "frac_of_measured_hbm": b / (us * 1e-6) / 1e9 / hbm_gbs}
+        kernels[n] = {"us": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9,
+                      "frac_of_measured_hbm": b / (us * 1e-6) / 1e9 / hbm_gbs}
     dom = "geglu_matvec_f16"
     dom_gbs = kernels[dom]["gbs"]
     fd = kernels["flash_decoding_f16"]

@@ -539,7 +539,8 @@ class Kernels:
         def __init__(self, x, w, residual, into):
             st, parts = w.c()
             super().__init__(N.lib().pc_kernel_aq_matmul_residual, _tc(x), ctypes.byref(st), _tc(residual),
-                             _tc(into), keep=_keep(x, w.packed_values, w.scales, w.biases, residual, into) + (st, parts))
+                             _tc(into),
+                             keep=_keep(x, w.packed_values, w.scales, w.biases, residual, into) + (st, parts))
 
     class AqGatedMLP(Kernel):
         """Extension: act(g) * u of [g; u] = Matmul(RMSNorm(x), w_gate_up),

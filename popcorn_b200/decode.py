@@ -91,7 +91,7 @@ class DecodeStack:
     """
 
     def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False, vocab=0,
-                 qk_norm_rope=False, rope_theta=10000.0):
+                 qk_norm_rope=False, rope_theta=10000.0, norm_add_one=True):
         """vocab > 0 adds the step's tail: the final RMSNorm fused into the LM
         head GEMV (tied embedding [vocab, H]) into `logits`, then Argmax into
         `token` (int32) — the greedy next token (Argmax.metal).
@@ -101,8 +101,12 @@ class DecodeStack:
         k (weights q_norm / k_norm) and of the new v (no weight), then RoPE of
         q and k with tables over every position (RopeBuildCosSin, built once
         here). The per-op path runs it as one QKNormRope launch after the QKV
-        projection; the fused step folds it into the attention items."""
+        projection; the fused step folds it into the attention items.
+
+        norm_add_one: RMSNorm weights are applied as (1 + w) (Gemma 2 style,
+        RMSNorm.swift addOneToWeight) or as w (Gemma 4)."""
         import torch
+        self.norm_add_one = norm_add_one
         self.shape = shape
         self.library = library
         self.vocab = vocab
@@ -116,8 +120,9 @@ class DecodeStack:
         self.qk_norm_rope = qk_norm_rope
         if qk_norm_rope:
             for w in self.layers:
-                w.q_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
-                w.k_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
+                if not hasattr(w, "q_norm"):  # (weights read from an archive bring their own)
+                    w.q_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
+                    w.k_norm = (torch.randn(s.Hd, generator=g, device=dev) * 0.1).float()
             self.inv_freq = (rope_theta ** (-torch.arange(0, s.Hd, 2, dtype=torch.float32) / s.Hd)).to(dev)
             self.rope_cos = torch.empty(s.Smax, s.Hd // 2, dtype=torch.float32, device=dev)
             self.rope_sin = torch.empty_like(self.rope_cos)
@@ -166,16 +171,17 @@ class DecodeStack:
         cur, nxt = self.x, self.x2
         for i, w in enumerate(self.layers):
             ks.append(Kernels.QKVProjection(cur, w.attn_norm, w.w_qkv, self.q, w.k_cache, w.v_cache, position=pos,
-                                            eps=s.eps, add_one_to_weight=True))
+                                            eps=s.eps, add_one_to_weight=self.norm_add_one))
             if self.qk_norm_rope:
                 ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
-                                             self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True,
+                                             self.rope_sin, position=pos, eps=s.eps,
+                                             add_one_to_weight=self.norm_add_one,
                                              norm_v=True))
             ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                                   mask=AttentionMask.causal))
             ks.append(Kernels.MatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
             ks.append(Kernels.GatedMLP(self.h, w.w_gate, w.w_up, into=self.act, norm_weight=w.mlp_norm, eps=s.eps,
-                                       add_one_to_weight=True, activation=s.activation))
+                                       add_one_to_weight=self.norm_add_one, activation=s.activation))
             ks.append(Kernels.MatmulResidual(self.act, w.w_down, self.h, into=nxt))
             cur, nxt = nxt, cur
         if self.l2_prefetch:
@@ -200,10 +206,12 @@ class DecodeStack:
         self._layer_table = torch.tensor(rows, dtype=torch.int64).to(dev)
         dt = {"f16": 9, "bf16": 10}[s.dtype]
         desc = N.pc_decode_stack_desc(dt, len(self.layers), s.H, s.Nq, s.Nkv, s.Hd, s.F, s.Smax, s.eps, s.scale,
-                                      s.activation, 1, self._layer_table.data_ptr(), self.x.data_ptr(),
+                                      s.activation, int(self.norm_add_one), self._layer_table.data_ptr(),
+                                      self.x.data_ptr(),
                                       self.x2.data_ptr(), self.h.data_ptr(), self.q.data_ptr(),
                                       self.attn.data_ptr(), self.act.data_ptr(), self.pos_state.data_ptr(), None, 0,
-                                      int(self.qk_norm_rope), int(self.qk_norm_rope), s.Smax if self.qk_norm_rope else 0)
+                                      int(self.qk_norm_rope), int(self.qk_norm_rope),
+                                      s.Smax if self.qk_norm_rope else 0)
         nbytes = DecodeStackKernel.workspace_bytes(desc)
         self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         desc.workspace = self._workspace.data_ptr()
@@ -219,7 +227,7 @@ class DecodeStack:
             return []
         s = self.shape
         return [Kernels.RMSNormMatmul(self.out, self.final_norm, self.lm_head, into=self.logits, eps=s.eps,
-                                      add_one_to_weight=True),
+                                      add_one_to_weight=self.norm_add_one),
                 Kernels.Argmax(self.logits, self.token)]
 
     # Bytes of the next operand each kernel pulls into L2 once its own loads
@@ -324,6 +332,46 @@ def _interleave8(a, b):
                                  il(a.biases, b.biases), (2 * a.out_features, a.in_features))
 
 
+def _concat_rows(ts):
+    """Row-wise concatenation of affine 4-bit tensors with one in_features
+    (the format's rows are independent: packed values, scales and biases
+    concatenate alike)."""
+    import torch
+    from .api import AffineQuantizedTensor
+    return AffineQuantizedTensor(torch.cat([t.packed_tensor for t in ts]).contiguous(),
+                                 torch.cat([t.scales for t in ts]).contiguous(),
+                                 torch.cat([t.biases for t in ts]).contiguous(),
+                                 (sum(t.out_features for t in ts), ts[0].in_features),
+                                 bits=ts[0].bits, group_size=ts[0].group_size)
+
+
+class ArchiveAqLayer:
+    """One decode layer's 4-bit weights read through a WeightLoader
+    (Gemma4Weights.swift:59-75 names): q/k/v_proj concatenated into w_qkv,
+    gate/up_proj kept and interleaved for the fused gated form, norms
+    (input_layernorm before attention, pre_feedforward_layernorm before the
+    MLP, self_attn.q_norm / k_norm) widened to f32; fresh bf16 KV caches."""
+
+    def __init__(self, loader, index, shape, device):
+        import torch
+        p = loader.layer_prefix(index)
+        lin = loader.linear
+        self.w_qkv = _concat_rows([lin(p + ".self_attn.q_proj"), lin(p + ".self_attn.k_proj"),
+                                   lin(p + ".self_attn.v_proj")])
+        self.w_o = lin(p + ".self_attn.o_proj")
+        self.w_gate, self.w_up = lin(p + ".mlp.gate_proj"), lin(p + ".mlp.up_proj")
+        self.w_gate_up = _interleave8(self.w_gate, self.w_up)
+        self.w_down = lin(p + ".mlp.down_proj")
+        self.attn_norm = loader.norm_weight(p + ".input_layernorm.weight")
+        self.mlp_norm = loader.norm_weight(p + ".pre_feedforward_layernorm.weight")
+        if p + ".self_attn.q_norm.weight" in loader.archive:
+            self.q_norm = loader.norm_weight(p + ".self_attn.q_norm.weight")
+            self.k_norm = loader.norm_weight(p + ".self_attn.k_norm.weight")
+        s = shape
+        self.k_cache = torch.zeros(1, s.Nkv, s.Smax, s.Hd, dtype=torch.bfloat16, device=device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+
+
 class AqDecodeStack(DecodeStack):
     """DecodeStack over 4-bit affine weights (bf16 activations): per layer
 
@@ -336,7 +384,15 @@ class AqDecodeStack(DecodeStack):
     Matmuls on AffineQuantizedTensor weights (Matmul.swift:99-131), every
     intermediate stored in bf16 where the reference stores it."""
 
-    def __init__(self, *args, ops="fused", vocab=0, **kwargs):
+    @classmethod
+    def from_archive(cls, library, shape, loader, n_layers, **kwargs):
+        """The stack over the first n_layers of a 4-bit safetensors archive
+        (popcorn_b200.safetensors.WeightLoader)."""
+        kwargs["layers"] = [ArchiveAqLayer(loader, i, shape, "cuda:%d" % kwargs.get("device", 0))
+                            for i in range(n_layers)]
+        return cls(library, shape, n_layers, **kwargs)
+
+    def __init__(self, *args, ops="fused", vocab=0, layers=None, **kwargs):
         """ops="fused": five launches per layer (+ the attention's two) —
         AqQKVProjection (RMSNorm + QKV + KV write), [QKNormRope],
         FlashDecodingRagged, AqMatmulResidual (o_proj + Add), AqGatedMLP
@@ -347,6 +403,7 @@ class AqDecodeStack(DecodeStack):
         RMSNorm fused into the LM head GEMV, then Argmax into `token`."""
         import torch
         self.ops = ops
+        self._given_layers = layers
         super().__init__(*args, **kwargs)
         self.vocab = vocab
         if vocab:
@@ -364,25 +421,28 @@ class AqDecodeStack(DecodeStack):
             return []
         s = self.shape
         return [Kernels.AqRMSNormMatmul(self.out, self.final_norm, self.lm_head, self.logits, eps=s.eps,
-                                        add_one_to_weight=True),
+                                        add_one_to_weight=self.norm_add_one),
                 Kernels.Argmax(self.logits, self.token)]
 
     def _make_layers(self, shape, generator, n_layers):
         assert shape.dtype == "bf16", "the 4-bit stack runs bf16 activations"
+        if self._given_layers is not None:
+            return self._given_layers
         return [AqLayerWeights(shape, generator) for _ in range(n_layers)]
 
     def _fused_layer(self, w, cur, nxt, pos, lens):
         s = self.shape
         ks = [Kernels.AqQKVProjection(cur, w.attn_norm, w.w_qkv, self.q, w.k_cache, w.v_cache, position=pos,
-                                      eps=s.eps, add_one_to_weight=True)]
+                                      eps=s.eps, add_one_to_weight=self.norm_add_one)]
         if self.qk_norm_rope:
             ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
-                                         self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True, norm_v=True))
+                                         self.rope_sin, position=pos, eps=s.eps,
+                                         add_one_to_weight=self.norm_add_one, norm_v=True))
         ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                               mask=AttentionMask.causal))
         ks.append(Kernels.AqMatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
         ks.append(Kernels.AqGatedMLP(self.h, w.mlp_norm, w.w_gate_up, into=self.act, eps=s.eps,
-                                     add_one_to_weight=True, activation=s.activation))
+                                     add_one_to_weight=self.norm_add_one, activation=s.activation))
         ks.append(Kernels.AqMatmulResidual(self.act, w.w_down, self.h, into=nxt))
         return ks
 
@@ -410,17 +470,19 @@ class AqDecodeStack(DecodeStack):
                 ks += self._fused_layer(w, cur, nxt, pos, lens)
                 cur, nxt = nxt, cur
                 continue
-            ks.append(Kernels.RMSNorm(cur, w.attn_norm, into=self.xn, eps=s.eps, add_one_to_weight=True))
+            ks.append(Kernels.RMSNorm(cur, w.attn_norm, into=self.xn, eps=s.eps, add_one_to_weight=self.norm_add_one))
             ks.append(Kernels.Matmul(self.xn, w.w_qkv, self.qkv))
             ks.append(Kernels.QKVScatter(self.qkv, self.q, w.k_cache, w.v_cache, position=pos))
             if self.qk_norm_rope:
                 ks.append(Kernels.QKNormRope(self.q, w.k_cache, w.v_cache, w.q_norm, w.k_norm, self.rope_cos,
-                                             self.rope_sin, position=pos, eps=s.eps, add_one_to_weight=True,
+                                             self.rope_sin, position=pos, eps=s.eps,
+                                             add_one_to_weight=self.norm_add_one,
                                              norm_v=True))
             ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                                   mask=AttentionMask.causal))
             ks.append(Kernels.Matmul(self.attn.view(1, s.Nq * s.Hd), w.w_o, self.o))
-            ks.append(Kernels.AddRMSNorm(cur, self.o, w.mlp_norm, self.h, self.hn, eps=s.eps, add_one_to_weight=True))
+            ks.append(Kernels.AddRMSNorm(cur, self.o, w.mlp_norm, self.h, self.hn, eps=s.eps,
+                                         add_one_to_weight=self.norm_add_one))
             ks.append(Kernels.Matmul(self.hn, w.w_gate, self.g_out))
             ks.append(Kernels.Matmul(self.hn, w.w_up, self.u_out))
             ks.append(Kernels.GeluTanh(self.g_out, self.a_out) if s.activation == 0 else
@@ -446,4 +508,4 @@ def _nbytes(t):
     return t.numel() * t.element_size()
 
 
-__all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack", "AqLayerWeights", "AqDecodeStack"]
+__all__ = ["LayerShape", "DecodeLayerWeights", "DecodeStack", "AqLayerWeights", "ArchiveAqLayer", "AqDecodeStack"]

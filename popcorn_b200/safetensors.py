@@ -175,6 +175,16 @@ class WeightLoader:
         """EmbeddingTable: dense [vocab, hidden] or quantized, as linear()."""
         return self.linear(name)
 
+    def norm_weight(self, name):
+        """A norm weight as f32 on the device: bf16 values widened
+        (Support.swift:24-38), other dtypes as stored."""
+        import torch
+        dt = self.archive.info(name)[0]
+        a = self.archive.array(name)
+        if dt == "BF16":
+            a = (a.astype(np.uint32) << 16).view(np.float32)
+        return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.device)
+
     def _maybe_quantized(self, name):
         from .api import AffineQuantizedTensor
         if self.quantization is None:
