@@ -175,14 +175,62 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
         }
     } else {
         // ---- consumers ----
+        // 16-bit x in 16-byte chunks (one load per 8 elements, all in flight
+        // at once); the norm weights depend on nothing and load before the
+        // wait for the previous kernel.
+        constexpr bool kX16 = Elem<XT>::bytes == 2 && VEC == 8;
+        constexpr int kXC = 8;  // chunks per thread: rows up to 8 * 8 * 256 elements
+        const bool chunked = kX16 && K <= int64_t(kXC) * 8 * kConsumers * 32 &&
+                             (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+        float4 nwv[NORM ? kXC : 1][2];
+        const bool nw_chunked = NORM && chunked && p.norm_weight && (reinterpret_cast<uintptr_t>(p.norm_weight) & 15) == 0;
+        if constexpr (NORM) {
+            if (nw_chunked) {
+#pragma unroll
+                for (int j = 0; j < kXC; ++j) {
+                    const int c = tid + j * kConsumers * 32;
+                    if (c < nx) {
+                        nwv[j][0] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c);
+                        nwv[j][1] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c + 1);
+                    }
+                }
+            }
+        }
         pdl_wait();
         float ss = 0.f;
-        for (int64_t i = tid; i < K; i += kConsumers * 32) {
-            float v = Elem<XT>::load(p.x, i);
-            if constexpr (NORM) ss += v * v;
-            int c = int(i / VEC), e = int(i % VEC);
-            float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
-            plane[e & 3] = v;
+        auto stage_scalar = [&]() {
+            for (int64_t i = tid; i < K; i += kConsumers * 32) {
+                float v = Elem<XT>::load(p.x, i);
+                if constexpr (NORM) ss += v * v;
+                int c = int(i / VEC), e = int(i % VEC);
+                float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
+                plane[e & 3] = v;
+            }
+        };
+        if constexpr (!kX16) {
+            stage_scalar();
+        } else if (chunked) {
+            uint4 xr[kXC];
+#pragma unroll
+            for (int j = 0; j < kXC; ++j) {
+                const int c = tid + j * kConsumers * 32;
+                if (c < nx) xr[j] = __ldcg(reinterpret_cast<const uint4*>(p.x) + c);
+            }
+#pragma unroll
+            for (int j = 0; j < kXC; ++j) {
+                const int c = tid + j * kConsumers * 32;
+                if (c < nx) {
+                    float f[8];
+                    unpack8<XT>(xr[j], f);
+                    if constexpr (NORM)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+                    xs[c] = make_float4(f[0], f[1], f[2], f[3]);
+                    xs[nx + c] = make_float4(f[4], f[5], f[6], f[7]);
+                }
+            }
+        } else {
+            stage_scalar();
         }
         if constexpr (NORM) {
             ss = warp_sum(ss);
@@ -195,16 +243,49 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
             }
             named_sync(1, kConsumers * 32);
             const float scale = s_scale;
-            for (int64_t i = tid; i < K; i += kConsumers * 32) {
-                int c = int(i / VEC), e = int(i % VEC);
-                float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
-                float v = plane[e & 3] * scale;
-                if (p.norm_weight) {
-                    float w = p.norm_weight[i];
-                    if (p.add_one) w = 1.0f + w;
-                    v *= w;
+            if (chunked) {
+                // each thread rewrites the chunks it staged (no barrier needed)
+#pragma unroll
+                for (int j = 0; j < kXC; ++j) {
+                    const int c = tid + j * kConsumers * 32;
+                    if (c < nx) {
+                        const float4 lo = xs[c], hi = xs[nx + c];
+                        float f[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                        float w[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+                        if (nw_chunked) {
+                            const float4 a = nwv[j][0], b = nwv[j][1];
+                            const float ww[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) w[e] = p.add_one ? 1.0f + ww[e] : ww[e];
+                        } else if (p.norm_weight) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float ww = p.norm_weight[int64_t(c) * 8 + e];
+                                w[e] = p.add_one ? 1.0f + ww : ww;
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            float v = f[e] * scale;
+                            if (p.norm_weight) v *= w[e];
+                            f[e] = Elem<XT>::round(v);
+                        }
+                        xs[c] = make_float4(f[0], f[1], f[2], f[3]);
+                        xs[nx + c] = make_float4(f[4], f[5], f[6], f[7]);
+                    }
                 }
-                plane[e & 3] = Elem<XT>::round(v);
+            } else {
+                for (int64_t i = tid; i < K; i += kConsumers * 32) {
+                    int c = int(i / VEC), e = int(i % VEC);
+                    float* plane = reinterpret_cast<float*>(xs + (e < 4 ? 0 : nx) + c);
+                    float v = plane[e & 3] * scale;
+                    if (p.norm_weight) {
+                        float w = p.norm_weight[i];
+                        if (p.add_one) w = 1.0f + w;
+                        v *= w;
+                    }
+                    plane[e & 3] = Elem<XT>::round(v);
+                }
             }
         }
         named_sync(1, kConsumers * 32);
