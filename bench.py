@@ -13,7 +13,7 @@ so every step streams them from HBM.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 At N > 1 (torchrun, one process per GPU) every rank runs its own replica
-(the config-2 decode path at batch 1 does not shard; see DESIGN.md);
+(the config-2 decode path at batch 1 does not shard: replicas only);
 `value` is the tokens/s of all ranks together, timed as the max over ranks.
 Rank 0 prints one JSON line.
 """
@@ -31,9 +31,9 @@ LAYERS = 26
 CTX = 4096
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one gemv_tma_kernel
-# <f16,f16,f16,NORM,kGated> launch (one layer's gate/up), from the ncu
-# capture summarised in profiles/gemv_geglu_config2.md.
-GEGLU_NCU_TRAFFIC = 87_425_024
+# <f16,f16,f16,NORM,kGated> launch (one layer's gate/up), from an ncu
+# capture of that launch (bench.py --layers 4 --profile-steps 1).
+GEGLU_NCU_TRAFFIC = 87_360_256
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
