@@ -898,9 +898,11 @@ bool decode_step_plan(DecodeStep& p, int sm_count) {
     int kmax = p.H > p.F ? p.H : p.F;
     if (p.Nq * kHD > kmax) kmax = p.Nq * kHD;
     if (kmax > kChunkRegs * 8 * kCW * 32 || p.H > kNormChunks * 8 * kCW * 32) return false;
-    // L2 prefetch distance beyond the ring, per CTA (148 x 256 KB = 38 MB of
-    // the 126 MB L2). POPCORN_STEP_L2_AHEAD overrides it (bytes; 0 = off).
-    p.l2_ahead = 256 * 1024;
+    // L2 prefetch distance beyond the ring, per CTA (148 x 128 KB = 19 MB of
+    // the 126 MB L2; measured at config 2: 0 -> 1.424 ms, 128 KB -> 1.402,
+    // 256 KB -> 1.418, 512 KB -> 1.78). POPCORN_STEP_L2_AHEAD overrides it
+    // (bytes; 0 = off).
+    p.l2_ahead = 128 * 1024;
     if (const char* e = getenv("POPCORN_STEP_L2_AHEAD")) p.l2_ahead = atoll(e);
     p.xs_bytes = (kmax * 4 + 127) / 128 * 128;
     // attention split: about one item per SM and never more items than CTAs
