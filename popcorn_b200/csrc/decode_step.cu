@@ -35,10 +35,11 @@
 // CTAs, so all run at once) count in on a per-head counter, wait for each
 // other, and each combines a 1/splits slice of the head's outputs.
 //
-// Measured on B200 (config 2, 26 layers, ctx 4096): 1.415 ms per token
-// against 1.437 ms for the five-kernel graph. Streaming phases reach 5.4-6.9 TB/s; what
-// remains is latency at each op boundary (the activation row's loads queue
-// behind the SM's in-flight weight copies) and in the attention phase.
+// Measured on B200 (config 2, 26 layers, ctx 4096): 1.402 ms per token;
+// the five-kernel graph, whose GEMV prologues were since shortened, takes
+// 1.311 ms. Streaming phases reach 5.4-6.9 TB/s; what remains is latency at
+// each op boundary (the activation row's loads queue behind the SM's
+// in-flight weight copies) and in the attention phase.
 //
 // Every wait (mbarrier or counter) is bounded: on give-up the CTA sets the
 // device error word and skips its remaining work but keeps taking part in
