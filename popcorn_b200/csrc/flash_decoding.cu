@@ -524,10 +524,13 @@ __global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
 // partial sums are added in shared memory.
 constexpr int kCombThreads = 256;
 
+// blockIdx.z takes head dims [z * dchunk, (z + 1) * dchunk): more CTAs for
+// the few (b, hq) rows of a decode step.
 template <class OT>
 __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* po, const float* pm, const float* pl,
-                                                                  void* out, int64_t Nq, int64_t Hd, int splits) {
-    extern __shared__ float sh[];  // wts[splits (padded to 4)], part[groups][Hd]
+                                                                  void* out, int64_t Nq, int64_t Hd, int splits,
+                                                                  int64_t dchunk) {
+    extern __shared__ float sh[];  // wts[splits (padded to 4)], part[groups][dchunk]
     float* wts = sh;
     float* part = sh + ((splits + 3) & ~3);
     __shared__ float red[kCombThreads / 32];
@@ -566,11 +569,13 @@ __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* p
         s_L = v;
     }
     __syncthreads();
-    const float* o = po + bh * splits * Hd;
+    const int64_t d0 = int64_t(blockIdx.z) * dchunk;
+    const int64_t dn = Hd - d0 < dchunk ? Hd - d0 : dchunk;
+    const float* o = po + bh * splits * Hd + d0;
     const float L = s_L;
     const float inv_l = L > 0.f ? 1.0f / L : 0.f;
-    if ((Hd & 3) == 0 && Hd / 4 <= kCombThreads) {
-        const int cols = int(Hd / 4);
+    if ((Hd & 3) == 0 && (dn & 3) == 0 && dn / 4 <= kCombThreads) {
+        const int cols = int(dn / 4);
         const int groups = kCombThreads / cols;
         const int col = tid % cols, grp = tid / cols;
         if (grp < groups) {
@@ -592,19 +597,19 @@ __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* p
                 a0.z = fmaf(w0, v0.z, a0.z); a0.w = fmaf(w0, v0.w, a0.w);
             }
             float4 r = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
-            reinterpret_cast<float4*>(part + int64_t(grp) * Hd)[col] = r;
+            reinterpret_cast<float4*>(part + int64_t(grp) * dn)[col] = r;
         }
         __syncthreads();
-        for (int64_t d = tid; d < Hd; d += kCombThreads) {
+        for (int64_t d = tid; d < dn; d += kCombThreads) {
             float acc = 0.f;
-            for (int g = 0; g < groups; ++g) acc += part[g * Hd + d];
-            Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+            for (int g = 0; g < groups; ++g) acc += part[g * dn + d];
+            Elem<OT>::store(out, bh * Hd + d0 + d, acc * inv_l);
         }
     } else {
-        for (int64_t d = tid; d < Hd; d += kCombThreads) {
+        for (int64_t d = tid; d < dn; d += kCombThreads) {
             float acc = 0.f;
             for (int s = 0; s < splits; ++s) acc = fmaf(wts[s], o[int64_t(s) * Hd + d], acc);
-            Elem<OT>::store(out, bh * Hd + d, acc * inv_l);
+            Elem<OT>::store(out, bh * Hd + d0 + d, acc * inv_l);
         }
     }
 }
@@ -744,19 +749,21 @@ cudaError_t flash_decode(const FlashDecode& p, const FlashDecodePlan& plan, floa
 cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& plan, const float* po, const float* pm,
                                  const float* pl, cudaStream_t s) {
     if (plan.splits <= 1) return cudaSuccess;
-    dim3 grid(unsigned(p.Nq), unsigned(p.B));
-    const int64_t groups = (p.Hd % 4 == 0 && p.Hd / 4 <= kCombThreads) ? kCombThreads / (p.Hd / 4) : 0;
-    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(groups) * p.Hd) * 4;
+    // 64 head dims per CTA when that gives more CTAs for few rows
+    const int64_t dchunk = (p.Hd % 64 == 0 && p.Hd > 64 && p.B * p.Nq < 4 * current_sm_count()) ? 64 : p.Hd;
+    dim3 grid(unsigned(p.Nq), unsigned(p.B), unsigned(p.Hd / dchunk));
+    const int64_t groups = (dchunk % 4 == 0 && dchunk / 4 <= kCombThreads) ? kCombThreads / (dchunk / 4) : 0;
+    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(groups) * dchunk) * 4;
     switch (p.out_dtype) {
     case PC_F32:
         return launch_k(fd_combine_kernel<TF32>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
-                        plan.splits);
+                        plan.splits, dchunk);
     case PC_F16:
         return launch_k(fd_combine_kernel<TF16>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
-                        plan.splits);
+                        plan.splits, dchunk);
     case PC_BF16:
         return launch_k(fd_combine_kernel<TBF16>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
-                        plan.splits);
+                        plan.splits, dchunk);
     }
     return cudaErrorInvalidValue;
 }
