@@ -514,6 +514,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--l2-prefetch", action="store_true",
+                    help="each kernel of the step pulls the start of the next kernel's operand into L2")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--workload", default="config2", choices=["config2", "fd_sweep", "tp9b", "prefill", "aq"])
     ap.add_argument("--tp-layers", type=int, default=42)
@@ -555,7 +557,7 @@ def main():
     n_layers = args.layers
     shape = LayerShape(max_ctx=CTX, dtype="f16")
     lib = pc.KernelLibrary(local)
-    stack = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local)
+    stack = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, l2_prefetch=args.l2_prefetch)
     stream = torch.cuda.Stream(device=local)
     pos = CTX - 1
     hbm_gbs, _, peak_kind = peaks()
