@@ -37,6 +37,8 @@ def _qtensor(pc, rng, N, K, sdt, bias=True):
     return qt, packed, sc, bi
 
 
+TDT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
 COMBOS = [("bf16", "bf16", "bf16"), ("bf16", "bf16", "f32"), ("f32", "bf16", "f32"), ("f16", "f16", "f16")]
 
 
@@ -152,13 +154,14 @@ def _f32(t):
 
 
 @pytest.mark.parametrize("M", [1, 4])
-def test_aq_fused_forms(pc, M):
+@pytest.mark.parametrize("bf", ["bf16", "f16"])
+def test_aq_fused_forms(pc, M, bf):
     """The fused 4-bit decode forms against their reference op sequences on
     the oracle: RMSNorm -> Matmul; Matmul -> Add; RMSNorm -> Matmul [gate;
-    up] (8-row interleave) -> GeluTanh * up; RMSNorm -> Matmul -> q + KV write."""
+    up] (8-row interleave) -> GeluTanh * up; RMSNorm -> Matmul -> q + KV write.
+    bf16 x with bf16 scales (reference) and f16 / f16 (extension)."""
     rng = np.random.default_rng(M)
     K, N, eps = 2304, 512, 1e-6
-    bf = "bf16"
     x = oracle.to_dtype(rng.standard_normal((M, K)), bf)
     nw = (0.1 * rng.standard_normal(K)).astype(np.float32)
     qt, packed, sc, bi = _qtensor(pc, rng, N, K, bf)
@@ -166,14 +169,14 @@ def test_aq_fused_forms(pc, M):
     xd = to_dev(x, bf)
     xn = oracle.rmsnorm(x, bf, nw, eps=eps, add_one=True)
     # RMSNorm -> Matmul
-    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(M, N, dtype=TDT[bf], device="cuda")
     enc.encode(pc.Kernels.AqRMSNormMatmul(xd, to_dev(nw, "f32"), qt, out, eps=eps, add_one_to_weight=True))
     torch.cuda.synchronize()
     assert_close(from_dev(out, bf), oracle.aq_matmul(xn, bf, packed, sc, bi, bf, bf), bf, what="norm+matmul",
                  bf16_ulps=2)
     # Matmul -> Add(residual)
     res = oracle.to_dtype(rng.standard_normal((M, N)), bf)
-    out2 = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    out2 = torch.empty(M, N, dtype=TDT[bf], device="cuda")
     enc.encode(pc.Kernels.AqMatmulResidual(xd, qt, to_dev(res, bf), out2))
     torch.cuda.synchronize()
     exp2 = oracle.add(oracle.aq_matmul(x, bf, packed, sc, bi, bf, bf), res, bf)
@@ -183,7 +186,7 @@ def test_aq_fused_forms(pc, M):
     qg, pg, sg, bg = _qtensor(pc, rng, F, K, bf)
     qu, pu, su, bu = _qtensor(pc, rng, F, K, bf)
     from popcorn_b200.decode import _interleave8
-    out3 = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    out3 = torch.empty(M, F, dtype=TDT[bf], device="cuda")
     enc.encode(pc.Kernels.AqGatedMLP(xd, to_dev(nw, "f32"), _interleave8(qg, qu), out3, eps=eps,
                                      add_one_to_weight=True))
     torch.cuda.synchronize()
@@ -195,8 +198,8 @@ def test_aq_fused_forms(pc, M):
     # QKV: q [M, 2, 1, 128], caches [M, 1, 16, 128] written at position 5
     Nq, Nkv, Hd, Smax, pos = 2, 1, 128, 16, 5
     qk, pk, sk, bk = _qtensor(pc, rng, (Nq + 2 * Nkv) * Hd, K, bf)
-    q = torch.zeros(M, Nq, 1, Hd, dtype=torch.bfloat16, device="cuda")
-    kc = torch.zeros(M, Nkv, Smax, Hd, dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros(M, Nq, 1, Hd, dtype=TDT[bf], device="cuda")
+    kc = torch.zeros(M, Nkv, Smax, Hd, dtype=TDT[bf], device="cuda")
     vc = torch.zeros_like(kc)
     enc.encode(pc.Kernels.AqQKVProjection(xd, to_dev(nw, "f32"), qk, q, kc, vc,
                                           position=to_dev(np.array([pos], np.int32), "i32"), eps=eps,
