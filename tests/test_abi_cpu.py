@@ -200,3 +200,136 @@ def test_error_message_is_thread_local():
     for t in ts:
         t.join()
     assert "[5]" in msgs["a"] and "[6]" in msgs["b"]
+
+
+def test_argmax_validation():
+    """Argmax.swift:24-37: axis must be the last one, indices int32 with one
+    element per row; short rows route to `argmax`, long ones to `argmax_row`."""
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    k = K.Argmax(fake([2, 31], D.f32), fake([2], D.i32))
+    assert k.function_names == ["argmax"]
+    assert K.Argmax(fake([2, 32], D.bf16), fake([2], D.i32)).function_names == ["argmax_row"]
+    expect_error(E.tensorInvalidAxis, K.Argmax, fake([2, 3], D.f32), fake([3], D.i32), axis=0)
+    expect_error(E.tensorShapeMismatch, K.Argmax, fake([2, 3], D.f32), fake([3], D.i32))
+    expect_error(E.unsupportedDataTypeCombination, K.Argmax, fake([2, 3], D.f32), fake([2], D.f32))
+
+
+def test_rope_validation():
+    """RopeBuildCosSin.swift:31-50 and RopeApply.swift:19-64."""
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    t = fake([5, 8], D.f32)
+    K.RopeBuildCosSin(fake([5], D.i32), fake([8], D.f32), t, t)
+    expect_error(E.tensorShapeMismatch, K.RopeBuildCosSin, fake([5], D.i32), fake([8], D.f32), t,
+                 fake([5, 7], D.f32))
+    expect_error(E.tensorInvalidRank, K.RopeBuildCosSin, fake([5], D.i32), fake([8], D.f32), fake([40], D.f32),
+                 fake([40], D.f32))
+    expect_error(E.tensorShapeMismatch, K.RopeBuildCosSin, fake([4], D.i32), fake([8], D.f32), t, t)
+    expect_error(E.tensorShapeMismatch, K.RopeBuildCosSin, fake([5], D.i32), fake([7], D.f32), t, t)
+    x = fake([1, 5, 2, 16], D.bf16)
+    assert K.RopeApply(x, t, t, x).function_names == ["rope_apply_f32_tables_bf16"]
+    tb = fake([5, 8], D.bf16)
+    assert K.RopeApply(x, tb, tb, x).function_names == ["rope_apply_bf16"]
+    expect_error(E.unsupportedDataTypeCombination, K.RopeApply, fake([1, 5, 2, 16], D.f32), tb, tb,
+                 fake([1, 5, 2, 16], D.f32))
+    expect_error(E.tensorShapeMismatch, K.RopeApply, fake([1, 5, 2, 15], D.f32), fake([5, 7], D.f32),
+                 fake([5, 7], D.f32), fake([1, 5, 2, 15], D.f32))
+    expect_error(E.tensorShapeMismatch, K.RopeApply, x, fake([4, 8], D.f32), fake([4, 8], D.f32), x)
+    expect_error(E.tensorInvalidRank, K.RopeApply, fake([5, 2, 16], D.bf16), t, t, fake([5, 2, 16], D.bf16))
+    # the fused per-head norm + RoPE of a decode step
+    q = fake([1, 4, 1, 16], D.bf16)
+    kc = fake([1, 2, 32, 16], D.bf16)
+    w = fake([16], D.f32)
+    tq = fake([32, 8], D.f32)  # a row per position
+    k = K.QKNormRope(q, kc, kc, w, w, tq, tq, offset=31)
+    acc = [b[3] for b in k.tensors][:3]
+    assert acc == [pc.Access.readWrite] * 3
+    K.QKNormRope(q, kc, kc, w, w, fake([1, 8], D.f32), fake([1, 8], D.f32), offset=31)  # the step's row
+    expect_error(E.tensorShapeMismatch, K.QKNormRope, q, kc, kc, w, w, tq, tq, offset=32)
+    expect_error(E.tensorShapeMismatch, K.QKNormRope, q, kc, kc, w, w, t, t, offset=5)  # beyond the table
+    expect_error(E.unsupportedDataTypeCombination, K.QKNormRope, q, kc, kc, fake([16], D.bf16), w, tq, tq)
+
+
+def test_scalar_mul_validation():
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    assert K.ScalarMul(fake([4], D.f16), by=2.0, into=fake([4], D.f16)).function_names == ["scalar_mul_f16"]
+    expect_error(E.tensorShapeMismatch, K.ScalarMul, fake([4], D.f32), by=2.0, into=fake([5], D.f32))
+    expect_error(E.unsupportedDataTypeCombination, K.ScalarMul, fake([4], D.i32), by=2.0, into=fake([4], D.i32))
+
+
+def _aq(n, k, sdt=pc.DataType.bf16, bias=True, bits=4, group=64, packed_dt=pc.DataType.u32):
+    return pc.AffineQuantizedTensor(fake([n, k // 8], packed_dt), fake([n, k // 64], sdt),
+                                    fake([n, k // 64], sdt) if bias else None, (n, k), bits=bits,
+                                    group_size=group)
+
+
+def test_affine_quantized_matmul_validation():
+    """Matmul.swift:99-131, 279-351 and AffineQuantizedTensor.swift:22-50."""
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    x = fake([1, 256], D.bf16)
+    k = K.Matmul(x, _aq(32, 256), fake([1, 32], D.bf16))
+    assert k.function_names == ["aq_qmv_fast_bf16_bf16_bf16_b4_g64"]
+    assert K.Matmul(fake([3, 256], D.f32), _aq(32, 256), fake([3, 32], D.f32)).function_names == \
+        ["aq_matvec_simd4_f32_bf16_f32_b4_g64"]
+    K.Matmul(x, _aq(32, 256, bias=False), fake([1, 32], D.f32))
+    expect_error(E.tensorShapeMismatch, K.Matmul, fake([1, 192], D.bf16), _aq(32, 256), fake([1, 32], D.bf16))
+    expect_error(E.tensorShapeMismatch, K.Matmul, x, _aq(32, 256), fake([1, 31], D.bf16))
+    expect_error(E.unsupportedDataTypeCombination, K.Matmul, x, _aq(32, 256, bits=8), fake([1, 32], D.bf16))
+    expect_error(E.unsupportedDataTypeCombination, K.Matmul, x, _aq(32, 256, group=32), fake([1, 32], D.bf16))
+    expect_error(E.unsupportedDataTypeCombination, K.Matmul, x, _aq(32, 256, packed_dt=D.i32),
+                 fake([1, 32], D.bf16))
+    expect_error(E.unsupportedDataTypeCombination, K.Matmul, fake([1, 256], D.f16), _aq(32, 256),
+                 fake([1, 32], D.f16))
+    expect_error(E.tensorInvalidRank, K.Matmul, fake([256], D.bf16), _aq(32, 256), fake([1, 32], D.bf16))
+    with pytest.raises(pc.PopcornError):  # scales and biases must agree
+        pc.AffineQuantizedTensor(fake([32, 32], D.u32), fake([32, 4], D.bf16), fake([32, 4], D.f16), (32, 256))
+
+
+def test_embedding_gather_validation():
+    """EmbeddingGather.swift:12-95."""
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    ids = fake([3], D.i32)
+    assert K.EmbeddingGather(ids, fake([10, 64], D.bf16), fake([3, 64], D.f32)).function_names == \
+        ["embedding_gather_bf16_to_f32"]
+    expect_error(E.unsupportedDataTypeCombination, K.EmbeddingGather, ids, fake([10, 64], D.f16),
+                 fake([3, 64], D.f32))
+    expect_error(E.tensorShapeMismatch, K.EmbeddingGather, ids, fake([10, 64], D.f32), fake([4, 64], D.f32))
+    expect_error(E.tensorInvalidRank, K.EmbeddingGather, ids, fake([640], D.f32), fake([3, 64], D.f32))
+    q = _aq(1000, 256)
+    assert K.EmbeddingGather(ids, q, fake([3, 256], D.bf16)).function_names == \
+        ["aq_embedding_gather_bf16_bf16_b4_g64"]
+    expect_error(E.unsupportedDataTypeCombination, K.EmbeddingGather, fake([3], D.i64), q, fake([3, 256], D.bf16))
+    expect_error(E.tensorShapeMismatch, K.EmbeddingGather, ids, q, fake([3, 255], D.bf16))
+    expect_error(E.tensorInvalidRank, K.EmbeddingGather, fake([1, 3], D.i32), q, fake([3, 256], D.bf16))
+
+
+def test_fused_affine_quantized_validation():
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    x = fake([1, 256], D.bf16)
+    nw = fake([256], D.f32)
+    expect_error(E.unsupportedDataTypeCombination, K.AqRMSNormMatmul, fake([1, 256], D.f32), nw, _aq(32, 256),
+                 fake([1, 32], D.f32))
+    expect_error(E.tensorShapeMismatch, K.AqMatmulResidual, x, _aq(32, 256), fake([1, 31], D.bf16),
+                 fake([1, 32], D.bf16))
+    expect_error(E.tensorShapeMismatch, K.AqGatedMLP, x, nw, _aq(40, 256), fake([1, 20], D.bf16))
+    expect_error(E.unsupportedDataTypeCombination, K.AqRMSNormMatmul, x, fake([256], D.bf16), _aq(32, 256),
+                 fake([1, 32], D.bf16))
+
+
+def test_batched_helper_validation():
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    qkv = fake([4, (8 + 2 * 2) * 64], D.bf16)
+    q = fake([4, 8, 1, 64], D.bf16)
+    kc = fake([4, 2, 16, 64], D.bf16)
+    k = K.QKVScatter(qkv, q, kc, kc, offset=15)
+    assert [b[3] for b in k.tensors] == [pc.Access.read] + [pc.Access.write] * 3
+    expect_error(E.tensorShapeMismatch, K.QKVScatter, qkv, q, kc, kc, offset=16)
+    expect_error(E.tensorShapeMismatch, K.QKVScatter, fake([4, 700], D.bf16), q, kc, kc)
+    expect_error(E.unsupportedDataTypeCombination, K.QKVScatter, qkv, fake([4, 8, 1, 64], D.f16), kc, kc)
+    K.GatedActivation(fake([3, 64], D.f16), fake([3, 32], D.f16), activation=1)
+    expect_error(E.tensorShapeMismatch, K.GatedActivation, fake([3, 64], D.f16), fake([3, 31], D.f16))
+    expect_error(E.unsupportedDataTypeCombination, K.GatedActivation, fake([3, 64], D.f16), fake([3, 32], D.f16),
+                 activation=7)
+    a = fake([2, 128], D.bf16)
+    K.AddRMSNorm(a, a, fake([128], D.f32), a, a)
+    expect_error(E.tensorShapeMismatch, K.AddRMSNorm, a, fake([2, 127], D.bf16), None, a, a)
+    expect_error(E.unsupportedDataTypeCombination, K.AddRMSNorm, a, a, fake([128], D.bf16), a, a)
