@@ -34,6 +34,12 @@
 // are a 16-bit shift, bf16 stores are round-to-nearest-even with no NaN
 // special case (:29-34); f16 uses IEEE round-to-nearest-even (_Float16).
 //
+// Pinning: every function above with a reference test is checked against it
+// (tests/golden/reference_kats.json, tests/test_oracle.py). The affine-
+// quantized Matmul and the quantized embedding gather have none in the
+// reference: their restatements are parity unpinned (checked only against a
+// float64 dequantised product and their own format definition).
+//
 // Extensions that the reference does not have (f16 FlashDecoding / matvec /
 // KV write, ragged per-sequence lengths, SiLU) reuse the same templates with
 // the f16 load/store of PopcornDTypes.h:10,37, as the reference's own
