@@ -210,3 +210,14 @@ def test_aq_fused_forms(pc, M, bf):
     assert_close(from_dev(kc, bf)[:, 0, pos], qkv[:, Nq * Hd:(Nq + 1) * Hd], bf, what="k", bf16_ulps=2)
     assert_close(from_dev(vc, bf)[:, 0, pos], qkv[:, (Nq + 1) * Hd:], bf, what="v", bf16_ulps=2)
     assert torch.count_nonzero(kc[:, :, :pos]) == 0 and torch.count_nonzero(kc[:, :, pos + 1:]) == 0
+
+
+def test_embedding_gather_kat(pc, kats):
+    """KernelsTests.swift:121-138: exact."""
+    k = kats["embedding_gather"]
+    table = torch.tensor(k["table"], dtype=torch.float32, device="cuda").view(*k["shape"])
+    out = torch.empty(len(k["ids"]), k["shape"][1], device="cuda")
+    _enc(pc, False).encode(pc.Kernels.EmbeddingGather(torch.tensor(k["ids"], dtype=torch.int32, device="cuda"),
+                                                      table, out))
+    torch.cuda.synchronize()
+    assert out.cpu().view(-1).tolist() == k["expected"]

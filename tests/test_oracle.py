@@ -272,3 +272,9 @@ def test_embedding_gather():
     deq = oracle.aq_dequantize(packed, sc, bi, "bf16", 128)
     got = oracle.aq_embedding_gather(ids, packed, sc, bi, "bf16", "f32", 128)
     assert np.array_equal(got, deq[ids])
+
+
+def test_embedding_gather_kat(kats):
+    k = kats["embedding_gather"]
+    table = np.array(k["table"], np.float32).reshape(k["shape"])
+    assert oracle.embedding_gather(k["ids"], table, "f32").ravel().tolist() == k["expected"]
