@@ -258,6 +258,11 @@ PC_API int pc_kernel_add(const pc_tensor* a, const pc_tensor* b, const pc_tensor
  * extension (compared as their exact f32 values). Long rows use caller
  * scratch for their partial winners. */
 PC_API int pc_kernel_argmax(const pc_tensor* x, const pc_tensor* indices, int32_t axis, pc_kernel** kernel);
+/* Kernels.AttentionMaskBuild(mask:slidingWindow:) (AttentionMaskBuild.swift,
+ * AttentionMaskBuild.metal:5-21): f32 mask [Sq, Sk], 0 where query i (at key
+ * position Sk - Sq + i) may attend key j (causal, and within the window
+ * when sliding_window >= 0), -inf elsewhere. sliding_window < 0: none. */
+PC_API int pc_kernel_attention_mask_build(const pc_tensor* mask, int32_t sliding_window, pc_kernel** kernel);
 /* Kernels.ScalarMul(_:by:into:) (ScalarMul.swift, ScalarMul.metal:6-25):
  * out = x * scalar, f32 / f16 / bf16, out of x's shape and dtype. */
 PC_API int pc_kernel_scalar_mul(const pc_tensor* x, float scalar, const pc_tensor* out, pc_kernel** kernel);

@@ -279,6 +279,19 @@ def aq_embedding_gather(ids, packed, scales, biases, sdt, odt, H):
     return out
 
 
+def attention_mask(Sq, Sk, window=None):
+    """AttentionMaskBuild.metal:5-21: f32 [Sq, Sk], 0 where query i (key
+    position Sk - Sq + i) may see key j (j <= position, and position - j <
+    window when a window is given), -inf elsewhere."""
+    i = np.arange(Sq)[:, None]
+    j = np.arange(Sk)[None, :]
+    pos = Sk - Sq + i
+    ok = j <= pos
+    if window is not None and window >= 0:
+        ok &= (pos - j) < window
+    return np.where(ok, np.float32(0.0), np.float32(-np.inf)).astype(np.float32)
+
+
 def argmax(x, dt):
     """Argmax.metal:5-76 over the last axis: int32 index per row (ties -> the
     lowest index; NaN never wins; a row of NaN gives 0x7fffffff for n >= 32)."""

@@ -126,6 +126,7 @@ def _declare(L):
         "pc_kernel_add": ([T, T, T, PP], I),
         "pc_kernel_silu": ([T, T, PP], I),
         "pc_kernel_scalar_mul": ([T, F, T, PP], I),
+        "pc_kernel_attention_mask_build": ([T, I32, PP], I),
         "pc_kernel_rmsnorm_matmul": ([T, T, F, I32, T, T, PP], I),
         "pc_kernel_gated_mlp": ([T, T, F, I32, T, T, I32, T, PP], I),
         "pc_kernel_matmul_residual": ([T, T, T, T, PP], I),

@@ -586,6 +586,13 @@ class Kernels:
         def __init__(self, x, into):
             super().__init__(N.lib().pc_kernel_gelu_tanh, _tc(x), _tc(into), keep=_keep(x, into))
 
+    class AttentionMaskBuild(Kernel):
+        """Kernels.AttentionMaskBuild(mask:slidingWindow:) (AttentionMaskBuild.swift)."""
+
+        def __init__(self, mask, sliding_window=None):
+            super().__init__(N.lib().pc_kernel_attention_mask_build, _tc(mask),
+                             -1 if sliding_window is None else int(sliding_window), keep=_keep(mask))
+
     class ScalarMul(Kernel):
         """Kernels.ScalarMul(_:by:into:) (ScalarMul.swift)."""
 

@@ -107,6 +107,7 @@ enum class Unary : int { kGeluTanh = 0, kSilu = 1, kScalarMul = 2 };
 enum class Binary : int { kMul = 0, kAdd = 1 };
 cudaError_t unary(Unary op, const void* x, int x_dtype, void* out, int out_dtype, int64_t count,
                   cudaStream_t stream, float scalar = 1.0f);
+cudaError_t attention_mask_build(float* mask, int64_t Sq, int64_t Sk, int32_t window, cudaStream_t stream);
 cudaError_t binary(Binary op, const void* a, const void* b, void* out, int dtype, int64_t count,
                    cudaStream_t stream);
 

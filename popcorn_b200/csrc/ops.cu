@@ -387,6 +387,30 @@ private:
     const char* name_;
 };
 
+// Kernels.AttentionMaskBuild(mask:slidingWindow:) (AttentionMaskBuild.swift)
+class AttentionMaskBuildKernel : public Kernel {
+public:
+    AttentionMaskBuildKernel(Tensor mask, int32_t window) : mask_(mask), window_(window) {
+        if (mask.rank() != 2)
+            fail(PC_ERR_TENSOR_INVALID_RANK, "expected rank 2, got rank " + std::to_string(mask.rank()) + ".");
+        if (mask.dtype() != PC_F32) fail(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION, "the attention mask is f32.");
+        function_names_ = "attention_mask_build";
+    }
+    const char* name() const override { return "AttentionMaskBuild"; }
+    std::vector<Binding> tensors() const override { return {{mask_, PC_ACCESS_WRITE}}; }
+    void encode(KernelCommandEncoder& enc) const override {
+        float* m = static_cast<float*>(mask_.data());
+        const int64_t sq = mask_[0], sk = mask_[1];
+        const int32_t w = window_;
+        enc.dispatch(function_names_, tensors(),
+                     [=](cudaStream_t s) { return launch::attention_mask_build(m, sq, sk, w, s); });
+    }
+
+private:
+    Tensor mask_;
+    int32_t window_;
+};
+
 class BinaryKernel : public Kernel {
 public:
     BinaryKernel(launch::Binary op, Tensor a, Tensor b, Tensor out) : op_(op), a_(a), b_(b), out_(out) {
@@ -1699,6 +1723,12 @@ int pc_kernel_scalar_mul(const pc_tensor* x, float scalar, const pc_tensor* out,
     return wrap(std::make_unique<UnaryKernel>(launch::Unary::kScalarMul, tensor_arg(x, "x"), tensor_arg(out, "out"),
                                               scalar),
                 kernel);
+    PC_GUARD_END
+}
+
+int pc_kernel_attention_mask_build(const pc_tensor* mask, int32_t sliding_window, pc_kernel** kernel) {
+    PC_GUARD_BEGIN
+    return wrap(std::make_unique<AttentionMaskBuildKernel>(tensor_arg(mask, "mask"), sliding_window), kernel);
     PC_GUARD_END
 }
 

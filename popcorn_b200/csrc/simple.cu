@@ -109,6 +109,21 @@ __global__ void binary_kernel(const void* a, const void* b, void* out, int64_t n
     }
 }
 
+// AttentionMaskBuild.metal:5-21: additive mask [Sq, Sk]; query i sits at
+// key position Sk - Sq + i, key j is allowed when j <= that position and,
+// with a window w >= 0, when position - j < w.
+__global__ void attention_mask_build_kernel(float* mask, int64_t Sq, int64_t Sk, int32_t window) {
+    pdl_wait();
+    const int64_t n = Sq * Sk;
+    for (int64_t k = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; k < n; k += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = k / Sk, j = k % Sk;
+        const int64_t pos_q = Sk - Sq + i;
+        bool allowed = j <= pos_q;
+        if (window >= 0) allowed = allowed && (pos_q - j) < window;
+        mask[k] = allowed ? 0.0f : -INFINITY;
+    }
+}
+
 }  // namespace
 
 DeviceInfo device_info(int device) {
@@ -131,6 +146,13 @@ int current_sm_count() {
     int dev = 0;
     cudaGetDevice(&dev);
     return device_info(dev).sm_count;
+}
+
+cudaError_t attention_mask_build(float* mask, int64_t Sq, int64_t Sk, int32_t window, cudaStream_t stream) {
+    const int64_t n = Sq * Sk;
+    if (n == 0) return cudaSuccess;
+    return launch_k(attention_mask_build_kernel, dim3(grid_for(n, 256, current_sm_count())), dim3(256), 0, stream,
+                    mask, Sq, Sk, window);
 }
 
 cudaError_t kv_cache_write(const KVWrite& p, cudaStream_t stream) {
@@ -212,6 +234,7 @@ RegisterFunctions reg_simple({
     {"silu", reinterpret_cast<const void*>(unary_kernel<TF32, 1>)},
     {"silu_f16", reinterpret_cast<const void*>(unary_kernel<TF16, 1>)},
     {"silu_bf16", reinterpret_cast<const void*>(unary_kernel<TBF16, 1>)},
+    {"attention_mask_build", reinterpret_cast<const void*>(attention_mask_build_kernel)},
     {"scalar_mul", reinterpret_cast<const void*>(unary_kernel<TF32, 2>)},
     {"scalar_mul_f16", reinterpret_cast<const void*>(unary_kernel<TF16, 2>)},
     {"scalar_mul_bf16", reinterpret_cast<const void*>(unary_kernel<TBF16, 2>)},

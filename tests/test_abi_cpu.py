@@ -333,3 +333,10 @@ def test_batched_helper_validation():
     K.AddRMSNorm(a, a, fake([128], D.f32), a, a)
     expect_error(E.tensorShapeMismatch, K.AddRMSNorm, a, fake([2, 127], D.bf16), None, a, a)
     expect_error(E.unsupportedDataTypeCombination, K.AddRMSNorm, a, a, fake([128], D.bf16), a, a)
+
+
+def test_attention_mask_build_validation():
+    K, E, D = pc.Kernels, pc.PopcornError, pc.DataType
+    assert K.AttentionMaskBuild(fake([3, 5], D.f32)).function_names == ["attention_mask_build"]
+    expect_error(E.tensorInvalidRank, K.AttentionMaskBuild, fake([15], D.f32))
+    expect_error(E.unsupportedDataTypeCombination, K.AttentionMaskBuild, fake([3, 5], D.f16))

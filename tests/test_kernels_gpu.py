@@ -560,3 +560,13 @@ def test_scalar_mul_16bit(dt):
     torch.cuda.synchronize()
     # one fp32 product, one rounding to the storage type
     assert torch.equal(out, (x.float() * 0.7071).to(tdt))
+
+
+@pytest.mark.parametrize("Sq,Sk,window", [(3, 3, None), (4, 4, 2), (1, 97, None), (33, 200, 17), (64, 64, 0)])
+def test_attention_mask_build(Sq, Sk, window):
+    """Kernels.AttentionMaskBuild against the oracle rule, exact."""
+    import popcorn_b200 as pc
+    mask = torch.full((Sq, Sk), 7.0, device="cuda")
+    pc.KernelCommandEncoder(pc.KernelLibrary(0)).encode(pc.Kernels.AttentionMaskBuild(mask, sliding_window=window))
+    torch.cuda.synchronize()
+    assert np.array_equal(mask.cpu().numpy(), oracle.attention_mask(Sq, Sk, window))

@@ -278,3 +278,17 @@ def test_embedding_gather_kat(kats):
     k = kats["embedding_gather"]
     table = np.array(k["table"], np.float32).reshape(k["shape"])
     assert oracle.embedding_gather(k["ids"], table, "f32").ravel().tolist() == k["expected"]
+
+
+def test_attention_mask_kat(kats):
+    """KernelsTests.swift:407-434 (causal, and a window of 2)."""
+    k = kats["attention_mask"]
+    c = k["causal"]
+    m = oracle.attention_mask(c["Sq"], c["Sk"], c["window"])
+    assert ((m == 0) == np.array(c["allowed"], bool)).all() and np.isinf(m[m != 0]).all()
+    s = k["sliding"]
+    m = oracle.attention_mask(s["Sq"], s["Sk"], s["window"])
+    for r, row in enumerate(s["allowed_rows_0_to_2"]):
+        for j, a in enumerate(row):
+            if a is not None:
+                assert (m[r, j] == 0) == bool(a), (r, j)
