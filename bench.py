@@ -463,6 +463,36 @@ def time_aq_matvec(pc, enc, stream, shape, copies=4, reps=10):
             "bytes_per_layer": nbytes // copies}
 
 
+def time_qk_rope_step(lib, stream, n_layers, pos, warmup, steps, device):
+    """The config-2 step with the Gemma-3/4 attention prologue (per-head
+    q/k/v RMSNorm + RoPE): the per-op graph (one QKNormRope launch per
+    layer) and the fused one-launch step (folded into its attention items)."""
+    import torch
+    from popcorn_b200.decode import DecodeStack, LayerShape
+    out = {}
+    for fused in (False, True):
+        st = DecodeStack(lib, LayerShape(), n_layers, seed=55, device=device, fused=fused, qk_norm_rope=True)
+        st.set_position(pos)
+        st.x.normal_()
+        enc = st.encoder(stream)
+        st.kernels()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            st.encode_step(enc)
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        out["fused_ms_per_step" if fused else "ms_per_step"] = a.elapsed_time(b) / steps
+        del g, st
+    return out
+
+
 def time_aq_step(pc, lib, stream, n_layers, pos, warmup, steps, device):
     """The decode step over 4-bit affine weights (AqDecodeStack, bf16
     activations, ctx 4096): CUDA events over graph replays."""
@@ -680,6 +710,7 @@ def main():
         # (175 MB > L2) and the LM head (256000 x 2304), each from a graph ----
         aq = time_aq_matvec(pc, enc, stream, shape)
         aq["decode_step"] = time_aq_step(pc, lib, stream, n_layers, pos, args.warmup, min(args.steps, 50), local)
+        qk_rope = time_qk_rope_step(lib, stream, n_layers, pos, args.warmup, min(args.steps, 50), local)
 
         # ---- the same step as one persistent kernel (DecodeStack(fused=True)) ----
         fused = DecodeStack(lib, shape, n_layers, seed=1234 + rank, device=local, fused=True)
@@ -751,6 +782,7 @@ def main():
                            "bytes": tail_bytes, "gbs": tail_bytes / (tail_us * 1e-6) / 1e9,
                            "frac_of_measured_hbm": tail_bytes / (tail_us * 1e-6) / 1e9 / hbm_gbs},
         "aq_matvec": aq,
+        "qk_norm_rope_step": qk_rope,
         "fused_step": {"kernel": "decode_step_f16 (one persistent launch per token, all 26 layers)",
                        "ms_per_step": fused_ms, "tok_s": 1000.0 / fused_ms,
                        "step_hbm_gbs": bytes_step / (fused_ms * 1e-3) / 1e9, "device_error_word": fused_err},
