@@ -151,6 +151,11 @@ def time_cpu_layer(reps_min=1, budget_s=15.0, threads=None):
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the reference's kernels
+    (oracle/) over the whole 26-layer step, every step, on all host cores.
+    Each step runs the oracle decode layer 26 times (one layer's weights and
+    caches reused: on the host they stream from DRAM either way), so
+    ms_per_step is measured, not multiplied."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -158,28 +163,34 @@ def run_reference(args):
     oracle.set_threads(os.cpu_count() or 1)
     cores = oracle.threads()
 
-    def step():
+    def layer():
         oracle.decode_layer(d["x"], "f16", d["w_attn_norm"], d["w_mlp_norm"], d["w_qkv"], d["w_o"], d["w_gate"],
                             d["w_up"], d["w_down"], d["k_cache"], d["v_cache"], 8, 4, 256, CTX - 1)
 
-    for _ in range(args.warmup):
-        step()
+    def step():
+        for _ in range(LAYERS):
+            layer()
+
+    steps = max(1, min(args.steps, args.ref_steps))
+    warmup = max(1, min(args.warmup, 3))
+    for _ in range(warmup):
+        layer()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
-    dt = (time.perf_counter() - t0) / args.steps
-    tok_s = 1.0 / (dt * LAYERS)
-    sample = "each step: one of the %d layers (ctx %d) on the host; tok/s = 1 / (%d x layer time)" % (LAYERS, CTX,
-                                                                                                     LAYERS)
+    dt = (time.perf_counter() - t0) / steps
+    tok_s = 1.0 / dt
+    sample = ("each step: all %d layers (ctx %d) on the host, one layer's weights and caches reused; "
+              "%d timed step(s) after %d warm-up layer(s)" % (LAYERS, CTX, steps, warmup))
     line = {"impl": "reference", "metric": metric_name(), "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * LAYERS * 1000.0,
+            "steps": steps, "warmup": warmup, "ms_per_step": dt * 1000.0,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV cache and input)",
             "config": config_dict("cpu, %d threads" % cores),
             "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference = the C++ restatement of the reference's Metal kernels (oracle/); the Swift/Metal "
-                    "original cannot run on Linux"}
+                    "original cannot run on Linux. steps capped at --ref-steps (%d) to bound the run" % args.ref_steps}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -188,7 +199,7 @@ def run_reference(args):
 # FlashDecoding sweep
 # ---------------------------------------------------------------------------
 
-def run_fd_sweep(args):
+def fd_sweep_points(pc, lib, hbm_gbs):
     """Config 3: batch {1,8,32,64} x ctx {1k,4k,16k,32k}, 16 Q / 8 KV heads,
     head_dim 256, bf16 K/V N(0,1), ragged lengths U[ctx/2, ctx] (seeded),
     split count chosen by the library. Each point: K/V bytes actually read
@@ -197,10 +208,6 @@ def run_fd_sweep(args):
     Points smaller than 2x L2 rotate over several cache copies so every call
     reads from HBM."""
     import torch
-    import popcorn_b200 as pc
-    torch.cuda.set_device(0)
-    hbm_gbs, _, peak_kind = peaks()
-    lib = pc.KernelLibrary(0)
     Nq, Nkv, Hd = 16, 8, 256
     points = []
     gen = torch.Generator(device="cuda").manual_seed(7)
@@ -244,8 +251,60 @@ def run_fd_sweep(args):
             gbs = kv_bytes / (us * 1e-6) / 1e9
             points.append({"batch": B, "ctx": ctx, "us": round(us, 2), "kv_bytes": kv_bytes, "gbs": round(gbs, 1),
                            "frac_of_measured_hbm": round(gbs / hbm_gbs, 3)})
-            del caches, kerns, g
+            del caches, kerns, g, k, v
             torch.cuda.empty_cache()
+    return points
+
+
+def fd_config1(pc, lib, hbm_gbs):
+    """Config 1: one FlashDecoding op (B 1, one query token, 8 Q / 4 KV heads,
+    head_dim 256, KV context 1024, f16 N(0,1) q/k/v, scale 1/16, causal):
+    4 202 496 algorithmic bytes per call (K + V + q + out). One call's data
+    (4.2 MB) fits in L2, so the timed graph rotates over 64 distinct K/V
+    copies (269 MB > L2) and every call reads from HBM. CUDA events over
+    graph replays; the per-call time includes the split combine."""
+    import torch
+    B, Nq, Nkv, S, Hd, copies = 1, 8, 4, 1024, 256, 64
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    kv = [(torch.randn(B, Nkv, S, Hd, device="cuda", generator=gen).half(),
+           torch.randn(B, Nkv, S, Hd, device="cuda", generator=gen).half()) for _ in range(copies)]
+    q = torch.randn(B, Nq, 1, Hd, device="cuda", generator=gen).half()
+    out = torch.empty_like(q)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        enc = pc.KernelCommandEncoder(lib, stream=stream, scratch=pc.FixedScratch(16 << 20))
+        kerns = [pc.Kernels.FlashAttention(q, k, v, into=out, scale=1.0 / 16) for k, v in kv]
+        enc.encode(*kerns)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            enc.encode(*kerns)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1000.0 / (reps * copies)
+    nbytes = 2 * B * Nkv * S * Hd * 2 + 2 * B * Nq * Hd * 2
+    gbs = nbytes / (us * 1e-6) / 1e9
+    names = kerns[0].function_names
+    del kv, kerns, g
+    torch.cuda.empty_cache()
+    return {"kernels": "+".join(names), "us": us, "bytes": nbytes, "gbs": gbs, "frac_of_measured_hbm": gbs / hbm_gbs,
+            "timing": "64 distinct K/V copies (269 MB) per graph replay, CUDA events"}
+
+
+def run_fd_sweep(args):
+    import torch
+    import popcorn_b200 as pc
+    torch.cuda.set_device(0)
+    hbm_gbs, _, peak_kind = peaks()
+    points = fd_sweep_points(pc, pc.KernelLibrary(0), hbm_gbs)
     line = {"metric": "FlashDecoding sweep HBM GB/s (config 3)", "unit": "GB/s", "peak": hbm_gbs,
             "peak_kind": peak_kind, "dtype": "bf16", "data": "synthetic seeded N(0,1) K/V, ragged U[ctx/2, ctx]",
             "config": {"workload": "config3: B {1,8,32,64} x ctx {1k,4k,16k,32k}, 16Q/8KV, hd 256"},
@@ -254,17 +313,13 @@ def run_fd_sweep(args):
     return 0
 
 
-def run_prefill(args):
+def prefill_kernels(pc, lib, steps, warmup, tf_peak):
     """Config 4: the prefill GEMM (M 8192 x K 2304 x N 9216, bf16, transposeB,
     2*M*N*K = 347.9 GFLOP) and causal FlashAttention (B 4, 8 Q / 4 KV heads,
     S 2048, hd 256, bf16: 4*B*Nq*(S(S+1)/2)*hd = 68.75 GFLOP), each on the
     tcgen05 tensor cores, CUDA events over graph replays after warm-up.
     Operands (GEMM 370 MB in+out) exceed L2."""
     import torch
-    import popcorn_b200 as pc
-    torch.cuda.set_device(0)
-    _, tf_peak, peak_kind = peaks()
-    lib = pc.KernelLibrary(0)
     g = torch.Generator(device="cuda").manual_seed(4)
     M, K, N = 8192, 2304, 9216
     a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
@@ -288,12 +343,12 @@ def run_prefill(args):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 enc.encode(kern)
-            for _ in range(max(args.warmup, 3)):
+            for _ in range(max(warmup, 3)):
                 graph.replay()
             torch.cuda.synchronize()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
-            reps = max(args.steps, 5)
+            reps = max(steps, 5)
             e0.record(stream)
             for _ in range(reps):
                 graph.replay()
@@ -303,6 +358,18 @@ def run_prefill(args):
             tf = flops / (us * 1e-6) / 1e12
             res[name] = {"kernel": kern.function_names[0], "us": round(us, 2), "gflop": round(flops / 1e9, 2),
                          "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / tf_peak, 3)}
+            del graph
+    del a, w, c, q, k, v, o, gemm, fa
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_prefill(args):
+    import torch
+    import popcorn_b200 as pc
+    torch.cuda.set_device(0)
+    _, tf_peak, peak_kind = peaks()
+    res = prefill_kernels(pc, pc.KernelLibrary(0), args.steps, args.warmup, tf_peak)
     line = {"metric": "prefill TFLOP/s (config 4)", "unit": "TFLOP/s", "peak": tf_peak, "peak_kind": peak_kind,
             "dtype": "bf16", "data": "synthetic seeded N(0,1) activations / q,k,v, N(0,0.02) weights",
             "config": {"workload": "config4: GEMM 8192x2304x9216 tb; causal FA B4 8Q/4KV S2048 hd256"},
@@ -315,45 +382,117 @@ def run_prefill(args):
 # Tensor-parallel 9B-shape batched decode
 # ---------------------------------------------------------------------------
 
-def run_tp(args):
+TP_ROLES = ("qkv_gemm", "qkv_scatter", "attention", "o_proj_gemm", "allreduce_o_add_norm", "gate_up_gemm",
+            "gated_act", "down_gemm", "allreduce_down_add_norm")
+
+
+def _graph_time(stream, encode, reps, warmup=3):
+    """ms per replay of a graph holding what encode() enqueues."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        encode()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / reps
+
+
+def tp9b_leg(args, world, rank, local):
     """Config 5: Gemma-2-9B-shape decoder (42 layers, vocab 256000), batch 32,
-    KV context 8192, bf16, tensor-parallel over the torchrun ranks with an
-    NCCL all-reduce after o_proj and down_proj. A step = one token for all 32
-    sequences through every layer and the LM head, replayed from one CUDA
-    graph (NCCL captured). Total work is fixed as N grows (strong scaling);
-    value = 32 / step time."""
+    KV context 8192, bf16, tensor-parallel over the torchrun ranks (one
+    process per GPU): Q/KV heads, FFN columns and the vocabulary sharded,
+    an all-reduce after o_proj and after down_proj. A step = one token for
+    all 32 sequences through every layer and the LM head, replayed from one
+    CUDA graph. Total work is fixed as N grows (strong scaling); tok/s =
+    32 / step time (max over ranks).
+
+    Before timing, one step runs on the NCCL path (torch.distributed
+    all-reduce + AddRMSNorm) and one on the peer path (the one-shot
+    all-reduce over NVLink peer memory fused with Add + RMSNorm) from the
+    same input; `parity` is the largest logit difference between them
+    relative to the logits' RMS, and whether the two paths pick the same
+    argmax token for every sequence. The timed step uses the peer path.
+    `breakdown` replays each role's 42 launches from its own graph (all
+    ranks together), so `allreduce_share` = the two all-reduce roles' time
+    / the step time."""
     import torch
     import torch.distributed as dist
     import popcorn_b200 as pc
     from popcorn_b200.tp import TPDecodeModel, TPShape
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     hbm_gbs, _, peak_kind = peaks()
     shape = TPShape(layers=args.tp_layers)
     model = TPDecodeModel(pc.KernelLibrary(local), shape, rank=rank, world=world, seed=5, device=local)
-    if args.allreduce in ("peer", "peer-fused"):
-        def all_gather(blob):
-            if world == 1:
-                return [blob]
-            out = [None] * world
-            dist.all_gather_object(out, blob)
-            return out
-        model.use_peer_allreduce(all_gather, fuse_gemm=args.allreduce == "peer-fused")
     stream = torch.cuda.Stream(device=local)
 
     def all_reduce(t):
         if world > 1:
             dist.all_reduce(t)
 
-    with torch.cuda.stream(stream):
-        model.x.normal_()
-        enc = model.encoder(stream)
-        model.step(enc, all_reduce)  # eager warm-up (NCCL communicator set-up)
+    def all_gather(blob):
+        if world == 1:
+            return [blob]
+        out = [None] * world
+        dist.all_gather_object(out, blob)
+        return out
+
+    def sync_all():
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def parity_of(m):
+        """One step on the NCCL path, then one on the peer path, from the same
+        input; returns the comparison of the two paths' logits."""
+        m.x.normal_(generator=torch.Generator(device=m.x.device).manual_seed(11))
+        x_in = m.x.clone()
+        e = m.encoder(stream)
+        m.step(e, all_reduce)
+        sync_all()
+        ref = m.logits.float()
+        m.x.copy_(x_in)
+        m.use_peer_allreduce(all_gather, fuse_gemm=args.allreduce == "peer-fused")
+        e = m.encoder(stream)
+        m.step(e, all_reduce)
+        sync_all()
+        got = m.logits.float()
+        m.x.copy_(x_in)
+        rms = ref.pow(2).mean().sqrt()
+        d = (got - ref).abs()
+        # the bound of a chain of rounding points (bf16): relative L2 below
+        # 5e-3 and every logit within 8 bf16 ulps at the logits' RMS scale
+        ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(ref.abs(), rms))) - 7)
+        red = torch.stack([d.max() / rms, (d.pow(2).sum().sqrt() / ref.pow(2).sum().sqrt()),
+                           (d > 8 * ulp).any().float(), (got.argmax(1) != ref.argmax(1)).any().float(),
+                           (d == 0).all().logical_not().float()])
+        if world > 1:
+            dist.all_reduce(red, op=dist.ReduceOp.MAX)
+        return {"max_abs_diff_over_rms": float(red[0]), "rel_l2": float(red[1]),
+                "within_chain_tolerance": bool(red[1] < 5e-3 and red[2] == 0), "argmax_equal": bool(red[3] == 0),
+                "bit_identical": bool(red[4] == 0)}
+
+    with torch.cuda.stream(stream):
+        # ---- parity: a 2-layer model of the same shapes and sharding (a
+        # short chain of rounding points), then the full 42-layer model ----
+        short = TPDecodeModel(pc.KernelLibrary(local), TPShape(layers=2), rank=rank, world=world, seed=5,
+                              device=local)
+        parity = {"paths": "NCCL all-reduce + AddRMSNorm vs peer all-reduce fused with Add + RMSNorm",
+                  "argmax": "per rank over its vocabulary slice", "two_layer": parity_of(short)}
+        del short
+        torch.cuda.empty_cache()
+        parity["full_depth"] = parity_of(model)
+        enc = model.encoder(stream)
+        x0 = model.x.clone()
+
+        # ---- the timed step (peer path), graph-captured ----
+        model.x.copy_(x0)
         n0 = enc.dispatch_count
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
@@ -361,11 +500,11 @@ def run_tp(args):
         launches = enc.dispatch_count - n0
         for _ in range(args.warmup):
             graph.replay()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        sync_all()
         clocks = ClockSampler(local)
         clocks.start()
+        time.sleep(0.2)
+        sync_all()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -375,28 +514,69 @@ def run_tp(args):
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / args.steps
         clk = clocks.stop()
+        sync_all()
+        del graph
+
+        # ---- per-role breakdown (peer path; 9 launches per layer) ----
+        ks = model.kernels()
+        body = ks[1:-1]
+        per_layer = len(TP_ROLES)
+        breakdown = {}
+        if len(body) == per_layer * shape.L:
+            for i, role in enumerate(TP_ROLES):
+                sel = body[i::per_layer]
+                breakdown[role] = _graph_time(stream, lambda sel=sel: enc.encode(*sel), reps=5)
+            breakdown["lm_head_gemm"] = _graph_time(stream, lambda: enc.encode(ks[-1]), reps=5)
+            sync_all()
+    vals = [ms] + [breakdown[k] for k in sorted(breakdown)]
     if world > 1:
-        t = torch.tensor([ms], device="cuda")
+        t = torch.tensor(vals, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t[0])
+        vals = [float(x) for x in t]
+    ms = vals[0]
+    breakdown = {k: round(v, 4) for k, v in zip(sorted(breakdown), vals[1:])}
+    err = pc.device_error_check(local)
     per_rank_bytes = model.bytes_per_step()
+    ar_ms = breakdown.get("allreduce_o_add_norm", 0.0) + breakdown.get("allreduce_down_add_norm", 0.0)
+    top = max((k for k in breakdown), key=lambda k: breakdown[k]) if breakdown else None
+    res = {"workload": "config5: Gemma-2-9B-shape decode, %d layers, vocab 256000, batch 32, KV ctx 8192, bf16"
+                       % shape.L,
+           "parallelism": "tp%d" % world, "allreduce": args.allreduce, "scaling": "strong",
+           "tok_s": shape.B * 1000.0 / ms, "ms_per_step": ms,
+           "per_rank_bytes_per_step": per_rank_bytes,
+           "per_rank_hbm_gbs": per_rank_bytes / (ms * 1e-3) / 1e9,
+           "per_rank_frac_of_measured_hbm": per_rank_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, "peak_kind": peak_kind,
+           "allreduce_per_step": 2 * shape.L, "allreduce_bytes": shape.B * shape.H * 2,
+           "breakdown_ms_per_step": breakdown,
+           "breakdown_note": "each role's launches of one step replayed from their own graph, max over ranks",
+           "allreduce_share": ar_ms / ms if ms > 0 else None, "largest_role": top,
+           "gpu_launches_per_step": launches, "parity": parity, "clocks": clk, "device_error_word": err}
+    del model, ks, body
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_tp(args):
+    """bench.py --workload tp9b: the config-5 leg alone, as its own JSON line."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    res = tp9b_leg(args, world, rank, local)
     line = {"metric": "Gemma-2-9B-shape batched decode tok/s (42 layers, batch 32, ctx 8192, TP)",
-            "value": shape.B * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV)",
-            "config": {"workload": "config5: 9B-shape decode, %d layers, vocab 256000, batch 32, KV ctx 8192"
-                                   % shape.L, "global_batch": shape.B, "seq_len": shape.ctx,
-                       "parallelism": "tp%d" % world, "allreduce": args.allreduce,
-                       "l2": "inputs larger than L2"},
-            "per_rank_hbm_gbs": per_rank_bytes / (ms * 1e-3) / 1e9,
-            "per_rank_frac_of_measured_hbm": per_rank_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, "peak_kind": peak_kind,
-            "allreduce_per_step": 2 * shape.L, "allreduce_bytes": shape.B * shape.H * 2,
-            "gpu_launches": launches * args.steps, "clocks": clk}
+            "value": res["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV)",
+            "config": {"workload": res["workload"], "global_batch": 32, "seq_len": 8192,
+                       "parallelism": res["parallelism"], "l2": "inputs larger than L2"},
+            "tp9b": res, "gpu_launches": res["gpu_launches_per_step"] * args.steps, "clocks": res["clocks"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        # Leave without tearing the communicator down: a destroy after a
-        # graph-captured NCCL collective was seen to block for minutes.
         torch.cuda.synchronize()
         dist.barrier()
         sys.stdout.flush()
@@ -544,6 +724,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-steps", type=int, default=20,
+                    help="reference arm: at most this many timed steps (each is 26 oracle layers on the host)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="config-2 line only (skip the config-1/3/4/5 objects)")
     ap.add_argument("--l2-prefetch", action="store_true",
                     help="each kernel of the step pulls the start of the next kernel's operand into L2")
     ap.add_argument("--profile-steps", type=int, default=5)
@@ -792,6 +976,28 @@ def main():
         "launches_per_step": launches_per_step,
         "clocks": clk,
     }
+    if not args.no_extra:
+        # The other BASELINE configs, measured by the same run: config 1 (one
+        # FlashDecoding op), config 3 (the FlashDecoding sweep) and config 4
+        # (prefill GEMM + attention) on one GPU; config 5 (tensor-parallel
+        # 9B-shape decode) on every rank of this run, so a run at N GPUs
+        # reports TP-N. The config-2 stack is freed first (config 5 holds
+        # 108.7 GB / N per rank).
+        del graph, stack, enc, ks
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        if world == 1:
+            line["fd_config1"] = fd_config1(pc, lib, hbm_gbs)
+            line["fd_sweep"] = {"kernels": "flash_decoding_partial_bf16 + flash_decoding_reduce_bf16 (ragged)",
+                                "points": fd_sweep_points(pc, lib, hbm_gbs)}
+            _, tf_peak, tf_kind = peaks()
+            line["prefill"] = prefill_kernels(pc, lib, 10, args.warmup, tf_peak)
+            line["prefill"]["peak_tflops"] = tf_peak
+            line["prefill"]["peak_kind"] = tf_kind
+        line["tp9b"] = tp9b_leg(args, world, rank, local)
+        line["gpu_launches_tp9b"] = line["tp9b"]["gpu_launches_per_step"] * args.steps
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         t_layer, cores, reps = time_cpu_layer()
         line["cpu_baseline"] = {"value": 1.0 / (t_layer * n_layers), "unit": "tok/s", "cores": cores, "kind": "port",

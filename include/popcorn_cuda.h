@@ -211,7 +211,9 @@ PC_API int pc_kernel_flash_attention_dims(const pc_tensor* q, const pc_tensor* k
  * [B,Nkv,Smax,Hd] with per-sequence key counts seq_lens (int32 [B] on the
  * device, 0 <= len <= Smax). Equals FlashDecoding run per sequence on the
  * compact slice [1,Nkv,len,Hd] with the query at position len-1. A
- * sequence with len 0 yields zeros. */
+ * sequence with len 0 yields zeros. The kernels clamp each len to
+ * [0, Smax] on the device, so a value outside the contract never reads
+ * past the cache. */
 PC_API int pc_kernel_flash_decoding_ragged(const pc_tensor* q, const pc_tensor* k_cache,
                                            const pc_tensor* v_cache, const pc_tensor* seq_lens,
                                            const pc_tensor* out, float scale, pc_attention_mask mask,
@@ -539,17 +541,18 @@ PC_API int pc_kernel_decode_stack(const pc_decode_stack_desc* desc, pc_kernel** 
 /* ---- decode attention without allocation ------------------------------- */
 
 /* No counterpart in the reference. For callers that cannot allocate device
- * memory — code enqueuing work while a stream is captured into a CUDA graph,
- * real-time decode loops that must never allocate (an allocation can
- * synchronise the device), hosts whose device memory belongs to another
- * framework's pool — this runs the same decode attention as
+ * memory — real-time decode loops that must never allocate (an allocation
+ * can synchronise the device and stall the loop), hosts whose device memory
+ * belongs to another framework's pool and may not be touched by a library —
+ * this runs the same decode attention as
  * pc_kernel_flash_attention (Sq == 1) / pc_kernel_flash_decoding_ragged
  * (seq_lens != NULL) with the same split plan, so the results are
  * identical, but keeps the partial (m, l, O) buffers in a fixed device array
  * inside this library instead of borrowing them from a scratch allocator.
  * The caller passes q [B,Nq,1,Hd], k/v [B,Nkv,S,Hd], out [B,Nq,1,Hd] and
- * an optional seq_lens (i32 [B] on the device); the work is enqueued on
- * `stream` (cudaStream_t) of the current device.
+ * an optional seq_lens (i32 [B] on the device, each 0 <= len <= S and
+ * clamped to that range on the device; with seq_lens, S may be 0); the work
+ * is enqueued on `stream` (cudaStream_t) of the current device.
  *  - The array holds pc_flash_decoding_noalloc_capacity() bytes (1 MiB) on
  *    every GPU that loads the library, until the process exits. A problem
  *    whose partials need more is rejected with PC_ERR_WORKSPACE_EXHAUSTED

@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "dtype.cuh"
 #include "launch.hpp"
+#include "peer_reduce.cuh"
 #include "popcorn.hpp"
 
 namespace popcorn {
@@ -97,6 +98,30 @@ __global__ void add_rmsnorm_kernel(const AddRMSNorm p) {
     }
 }
 
+// 16-bit rows with H % 8 == 0: the row step of the peer all-reduce with a
+// single "rank" (the partial b), so this kernel and the fused all-reduce
+// accumulate the sum of squares in the same order and round identically —
+// the NCCL path and the peer path of a tensor-parallel model then agree bit
+// for bit wherever the collective's sums agree.
+template <class T>
+__global__ void __launch_bounds__(256) add_rmsnorm_rows_kernel(const AddRMSNorm a) {
+    pdl_wait();
+    __shared__ float red[256 / 32];
+    PeerAllReduce p{};
+    p.partial[0][0] = a.b;
+    p.world = 1;
+    p.buffer = 0;
+    p.residual = a.a;
+    p.sum_out = a.sum_out;
+    p.norm_out = a.norm_out;
+    p.weight = a.weight;
+    p.rows = a.rows;
+    p.H = a.H;
+    p.eps = a.eps;
+    p.add_one = a.add_one;
+    pr_reduce_row<T, 256>(p, blockIdx.x, true, threadIdx.x, red, [] { __syncthreads(); });
+}
+
 }  // namespace
 
 cudaError_t qkv_scatter(const QKVScatter& p, cudaStream_t s) {
@@ -123,6 +148,14 @@ cudaError_t gated_activation(const void* gu, void* out, int dtype, int64_t rows,
 
 cudaError_t add_rmsnorm(const AddRMSNorm& p, cudaStream_t s) {
     if (p.rows == 0) return cudaSuccess;
+    const bool rows16 = (p.dtype == PC_BF16 || p.dtype == PC_F16) && p.H % kPrVec == 0 &&
+                        p.H <= int64_t(256) * kPrVec * kPrMaxChunks && aligned16(p.a) && aligned16(p.b) &&
+                        aligned16(p.sum_out) && aligned16(p.norm_out);
+    if (rows16) {
+        dim3 g(unsigned(p.rows)), b(256);
+        if (p.dtype == PC_BF16) return launch_k(add_rmsnorm_rows_kernel<TBF16>, g, b, 0, s, p);
+        return launch_k(add_rmsnorm_rows_kernel<TF16>, g, b, 0, s, p);
+    }
     const int threads = p.H >= 4096 ? 1024 : (p.H >= 1024 ? 256 : 128);
     dim3 g(unsigned(p.rows)), b(threads);
     switch (p.dtype) {

@@ -116,6 +116,14 @@ struct FDArgs {
     float* pl;
 };
 
+// Keys of sequence b: seq_lens[b] clamped to [0, S] (a larger value would
+// read past the cache's rows), or S without seq_lens.
+__device__ __forceinline__ int64_t seq_len(const FlashDecode& p, int64_t b) {
+    if (!p.seq_lens) return p.S;
+    const int64_t n = int64_t(p.seq_lens[b]);
+    return n < 0 ? 0 : (n > p.S ? p.S : n);
+}
+
 // Key range [jb, je) of this CTA's split for sequence length len.
 __device__ __forceinline__ void split_range(const FDArgs& a, int64_t len, int split, int64_t& jb, int64_t& je) {
     jb = int64_t(split) * a.chunk;
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
 
     pdl_wait();  // q, the cache and seq_lens may come from the previous kernel
 
-    const int64_t len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
+    const int64_t len = seq_len(p, b);
     int64_t jb, je;
     split_range(a, len, split, jb, je);
 
@@ -449,7 +457,7 @@ __global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
     const int64_t b = blockIdx.z;
     const int64_t Hd = p.Hd;
     const int64_t hkv = hq * p.Nkv / p.Nq;
-    const int64_t len = p.seq_lens ? int64_t(p.seq_lens[b]) : p.S;
+    const int64_t len = seq_len(p, b);
     int64_t jb, je;
     split_range(a, len, split, jb, je);
     float q[MAXE], o[MAXE];

@@ -2,11 +2,10 @@
 // cannot allocate device memory.
 //
 // The encoder path borrows the decode attention's partial (m, l, O) buffers
-// from the caller's scratch allocator. Some callers have none to offer: code
-// that enqueues work while a stream is being captured into a CUDA graph
-// (cudaMalloc is not allowed there), real-time decode loops that must never
-// hit an allocation and its implicit device synchronisation, and hosts whose
-// device memory is owned by another framework's pool. For them this file
+// from the caller's scratch allocator. Some callers have none to offer:
+// real-time decode loops that must never hit an allocation and its implicit
+// device synchronisation, and hosts whose device memory is owned by another
+// framework's pool that a library may not draw from. For them this file
 // holds the partials in a fixed, file-scope device array instead; the caller
 // still passes q, K, V and the output.
 //
@@ -96,7 +95,8 @@ int pc_flash_decoding_noalloc(const pc_tensor* q, const pc_tensor* k, const pc_t
     if (B < 1 || Nq < 1 || Nkv < 1 || Nq % Nkv != 0)
         return reject(PC_ERR_TENSOR_SHAPE_MISMATCH, "query heads must be a positive multiple of KV heads.");
     if (Hd < 1 || Hd > 512) return reject(PC_ERR_TENSOR_SHAPE_MISMATCH, "head dim must be in 1..512.");
-    if (S < 1) return reject(PC_ERR_TENSOR_SHAPE_MISMATCH, "K/V need at least one key.");
+    // As the encoder path: S == 0 is only meaningful with per-sequence lengths.
+    if (S < 0 || (!seq_lens && S < 1)) return reject(PC_ERR_TENSOR_SHAPE_MISMATCH, "K/V need at least one key.");
     if (!is_float(q->dtype) || q->dtype != k->dtype || k->dtype != v->dtype || !is_float(out->dtype))
         return reject(PC_ERR_UNSUPPORTED_DATA_TYPE_COMBINATION,
                       "q, k, v must share one of f32/f16/bf16 and out must be f32/f16/bf16.");

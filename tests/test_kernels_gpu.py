@@ -242,6 +242,25 @@ def test_fd_ragged_edges(pc, enc):
         assert_close(got[b:b + 1], ref, "f32", what="ragged b%d" % b)
 
 
+def test_fd_ragged_lengths_clamped(pc, enc):
+    """seq_lens outside [0, Smax] (Smax = 1000, not a multiple of the 32-key
+    tile) are clamped on the device: a length past the cache reads no row
+    beyond it and equals length Smax; a negative length equals 0."""
+    rng = np.random.default_rng(21)
+    B, Nq, Nkv, S, Hd = 3, 8, 4, 1000, 256
+    lens = np.array([S + 4000, S, -5], np.int32)
+    q = rand(rng, (B, Nq, 1, Hd), "bf16")
+    k = rand(rng, (B, Nkv, S, Hd), "bf16")
+    v = rand(rng, (B, Nkv, S, Hd), "bf16")
+    out = empty_dev((B, Nq, 1, Hd), "f32")
+    run(enc, pc.Kernels.FlashDecodingRagged(to_dev(q, "bf16"), to_dev(k, "bf16"), to_dev(v, "bf16"),
+                                            to_dev(lens, "i32"), into=out, scale=1.0 / 16))
+    got = from_dev(out, "f32")
+    exp = oracle.flash_decoding(q[:2], "bf16", k[:2], v[:2], "bf16", "f32", 1.0 / 16)
+    assert_close(got[:2], exp, "f32", what="clamped lengths")
+    assert np.all(got[2] == 0)
+
+
 # ---------------------------------------------------------------------------
 # KV write, RMSNorm, matvec, elementwise
 # ---------------------------------------------------------------------------
