@@ -188,6 +188,18 @@ PC_API const char* pc_kernel_function_names(const pc_kernel* kernel);
  * PC_ERR_KERNEL_FUNCTION_NOT_FOUND. */
 PC_API int pc_kernel_set_l2_prefetch(pc_kernel* kernel, int32_t slot, const void* ptr, uint64_t bytes);
 
+/* Extension (no reference counterpart): scheduling hints. Results never
+ * change.
+ *  - PC_HINT_KV_EARLY (decode FlashAttention, value 0 or 1): the caller
+ *    promises that the kernel enqueued just before this one writes neither
+ *    seq_lens nor any K/V row except the newest of each sequence (the decode
+ *    step's KV write). The attention then copies every K/V tile that holds
+ *    no newest row while the previous kernel drains (before its dependency
+ *    wait); the tile with the newest row is copied after the wait.
+ * Other kernels / hints return PC_ERR_KERNEL_FUNCTION_NOT_FOUND. */
+typedef enum pc_kernel_hint { PC_HINT_KV_EARLY = 2 } pc_kernel_hint;
+PC_API int pc_kernel_set_hint(pc_kernel* kernel, int32_t hint, int64_t value);
+
 /* FlashAttention.Path, FlashAttention.swift:94-98 + route(sq:hd:supportsMPP:)
  * :109-113. On B200 the tensor-core prefill kernel plays the MPP role. */
 typedef enum pc_attention_path { PC_PATH_PLAIN = 0, PC_PATH_TENSOR = 1, PC_PATH_DECODING = 2 } pc_attention_path;

@@ -145,17 +145,21 @@ def matmul(a, adt, b, bdt, odt, transpose_b):
     return out
 
 
-def gelu_tanh(x, dt):
+def gelu_tanh(x, dt, odt=None):
+    """GeluTanh.metal:6-35 (odt f32: the value before the store's rounding)."""
     x = _c(x)
-    out = np.empty(x.shape, dtype=NP[dt])
-    lib().or_gelu_tanh(_p(x), DT[dt], _p(out), DT[dt], x.size)
+    odt = odt or dt
+    out = np.empty(x.shape, dtype=NP[odt])
+    lib().or_gelu_tanh(_p(x), DT[dt], _p(out), DT[odt], x.size)
     return out
 
 
-def silu(x, dt):
+def silu(x, dt, odt=None):
+    """silu(g) = g / (1 + exp(-g)) (odt f32: the value before rounding)."""
     x = _c(x)
-    out = np.empty(x.shape, dtype=NP[dt])
-    lib().or_silu(_p(x), DT[dt], _p(out), DT[dt], x.size)
+    odt = odt or dt
+    out = np.empty(x.shape, dtype=NP[odt])
+    lib().or_silu(_p(x), DT[dt], _p(out), DT[odt], x.size)
     return out
 
 

@@ -111,6 +111,7 @@ def _declare(L):
         "pc_kernel_binding": ([P, I, T, ctypes.POINTER(I)], I),
         "pc_kernel_function_names": ([P], ctypes.c_char_p),
         "pc_kernel_set_l2_prefetch": ([P, I32, P, ctypes.c_uint64], I),
+        "pc_kernel_set_hint": ([P, I32, ctypes.c_int64], I),
         "pc_flash_attention_route": ([I64, I64, I32], I),
         "pc_kernel_flash_attention": ([T, T, T, T, F, M, PP], I),
         "pc_kernel_flash_attention_dims": ([T, T, T, T, I64, I64, I64, I64, I64, I64, F, M, PP], I),

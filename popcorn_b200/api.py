@@ -392,6 +392,16 @@ class Kernel:
         _check(N.lib().pc_kernel_set_l2_prefetch(self._h, int(slot), ptr, n))
         return self
 
+    HINT_KV_EARLY = 2
+
+    def set_hint(self, hint, value=1):
+        """Scheduling hint (pc_kernel_set_hint). HINT_KV_EARLY: decode
+        attention may copy the K/V rows older than each sequence's newest
+        before it waits for the previous kernel (which must write no other
+        rows, nor seq_lens). Results never change."""
+        _check(N.lib().pc_kernel_set_hint(self._h, int(hint), int(value)))
+        return self
+
     def encode(self, encoder):
         encoder.encode(self)
 

@@ -36,10 +36,14 @@
 #include "dtype.cuh"
 #include "launch.hpp"
 #include "popcorn.hpp"
+#include "trace.cuh"
 
 namespace popcorn {
 
 __device__ unsigned int g_fd_error_word;
+namespace launch {
+PC_DT_BUFFER
+}
 
 namespace launch {
 
@@ -101,7 +105,7 @@ template <class KV, int HD, int G>
 constexpr size_t fd_smem_bytes() {
     using S = FDShape<KV, HD>;
     size_t ring = size_t(S::kStages) * S::kStageBytes;
-    size_t merge = size_t(S::kCWarps) * G * (HD + 2) * 4;
+    size_t merge = (size_t(S::kCWarps) * G * (HD + 3) + 2 * G) * 4;
     return ring > merge ? ring : merge;
 }
 
@@ -137,26 +141,38 @@ __device__ __forceinline__ void split_range(const FDArgs& a, int64_t len, int sp
 
 // Merges the NW warp states (mm/ll [NW][G], oo [NW][G][HD]) and writes this
 // CTA's (m, l, O) for heads hq0..hq0+G-1 — or the normalised output when the
-// plan has a single split.
+// plan has a single split. The per-warp weights exp2(m_w - M) and the merged
+// (M, L) of each head are computed once into `fw` (NW*G + 2*G floats of
+// shared memory) before the per-element sums. Every thread of the CTA calls it.
 template <int G, int HD, int NW>
 __device__ __forceinline__ void write_result(const FDArgs& a, int64_t b, int64_t hq0, int split, const float* mm,
-                                             const float* ll, const float* oo, int tid, int nthreads) {
+                                             const float* ll, const float* oo, float* fw, int tid, int nthreads) {
     const FlashDecode& p = a.p;
-    for (int idx = tid; idx < G * HD; idx += nthreads) {
-        int g = idx / HD, d = idx % HD;
+    float* Mg = fw + NW * G;
+    float* Lg = Mg + G;
+    if (tid < G) {
+        const int g = tid;
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NW; ++w) M = fmaxf(M, mm[w * G + g]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
+        float L = 0.f;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                float mw = mm[w * G + g];
-                float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
-                L += f * ll[w * G + g];
-                O += f * oo[(w * G + g) * HD + d];
-            }
+        for (int w = 0; w < NW; ++w) {
+            const float mw = mm[w * G + g];
+            const float f = (M == -INFINITY || mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            fw[w * G + g] = f;
+            L += f * ll[w * G + g];
         }
+        Mg[g] = M;
+        Lg[g] = L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * HD; idx += nthreads) {
+        const int g = idx / HD, d = idx % HD;
+        const float M = Mg[g], L = Lg[g];
+        float O = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) O += fw[w * G + g] * oo[(w * G + g) * HD + d];
         int64_t hq = hq0 + g;
         if (a.splits == 1) {
             float r = L > 0.f ? O * (1.0f / L) : 0.f;
@@ -188,6 +204,7 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     __shared__ volatile int s_abort;
     __shared__ volatile int s_issued;
     __shared__ volatile int s_consumed[kGroups];
+    DT_SHARED
 
     pdl_launch_dependents();
     const FlashDecode& p = a.p;
@@ -200,6 +217,8 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     const int64_t hq0 = hkv * gtot + int64_t(hg) * G;
 
     if (tid == 0) {
+        DT_INIT();
+        DT_MARK(0);
         for (int s = 0; s < NST; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 4);  // the four warps of the group that read it
@@ -214,7 +233,31 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     const int64_t head_off = (b * p.Nkv + hkv) * p.S * HD;  // elements
     const char* kbase = static_cast<const char*>(p.k) + head_off * Elem<KV>::bytes;
     const char* vbase = static_cast<const char*>(p.v) + head_off * Elem<KV>::bytes;
-    if (warp == kCWarps && lane == 0) {
+    int n_early = 0;  // tiles the producer copied before the wait
+    if (warp == kCWarps && lane == 0 && p.kv_early) {
+        // The caller promised that the previous kernel writes neither
+        // seq_lens nor any K/V row but the newest of each sequence: copy
+        // every tile of this split that holds no newest row now, while the
+        // previous kernel drains (the first NST tiles take stages whose
+        // empty barriers have not been armed yet).
+        const int64_t len0 = seq_len(p, b);
+        int64_t jb0, je0;
+        split_range(a, len0, split, jb0, je0);
+        for (int t = 0; t < NST && jb0 + int64_t(t) * kTileKeys < je0; ++t) {
+            const int64_t j0 = jb0 + int64_t(t) * kTileKeys;
+            const int64_t nk = je0 - j0 < kTileKeys ? je0 - j0 : kTileKeys;
+            if (j0 + nk >= len0) break;  // holds key len0 - 1, the newest
+            const uint32_t bytes = uint32_t(nk) * S::kRowBytes;
+            const uint32_t bar = smem_u32(&full[t]);
+            mbar_expect_tx(bar, 2 * bytes);
+            char* st = smem + size_t(t) * S::kStageBytes;
+            bulk_g2s(smem_u32(st), kbase + j0 * S::kRowBytes, bytes, bar);
+            bulk_g2s(smem_u32(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
+            n_early = t + 1;
+            s_issued = n_early;
+            if (t == 0) DT_MARK(4);
+        }
+    } else if (warp == kCWarps && lane == 0) {
         // Before waiting for the previous kernel: warm L2 with this split's
         // keys. A prefetch only fills L2 (which always holds the latest data),
         // so rows the previous kernel is still writing are read correctly
@@ -234,6 +277,7 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     }
 
     pdl_wait();  // q, the cache and seq_lens may come from the previous kernel
+    if (tid == 0) DT_MARK(1);
 
     const int64_t len = seq_len(p, b);
     int64_t jb, je;
@@ -244,13 +288,21 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     float* oo = ll + kCWarps * G;
 
     if (jb >= je) {  // no keys for this split (FlashDecoding.metal:78-87)
+        if (p.kv_early) {
+            // Copies issued before the wait (only if the caller broke the
+            // early-copy promise) land before the ring is reused.
+            __syncthreads();
+            if (tid == 0)
+                for (int t = 0; t < s_issued; ++t) mbar_wait(smem_u32(&full[t]), 0u, &g_fd_error_word);
+            __syncthreads();
+        }
         if (tid < kCWarps * G) {
             mm[tid] = -INFINITY;
             ll[tid] = 0.f;
         }
         for (int i = tid; i < kCWarps * G * HD; i += kFastThreads) oo[i] = 0.f;
         __syncthreads();
-        write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, tid, kFastThreads);
+        write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, oo + kCWarps * G * HD, tid, kFastThreads);
         return;
     }
 
@@ -268,7 +320,7 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     if (warp == kCWarps) {
         // ---- producer ----
         if (lane == 0) {
-            for (int t = 0; t < ntiles; ++t) {
+            for (int t = n_early; t < ntiles; ++t) {
                 const int s = t % NST;
                 const uint32_t ph = uint32_t(t / NST) & 1u;
                 if (s_abort || !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, &g_fd_error_word)) {
@@ -284,6 +336,8 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
                 bulk_g2s(smem_u32(st), kbase + j0 * S::kRowBytes, bytes, bar);
                 bulk_g2s(smem_u32(st + S::kTileBytes), vbase + j0 * S::kRowBytes, bytes, bar);
                 s_issued = t + 1;
+                if (t == 0 && n_early == 0) DT_MARK(4);
+                DT_MARK(7);
             }
             // Own loads issued: warm L2 for the next kernel of the chain.
             const int part = int(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
@@ -307,6 +361,10 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
             if (s_abort || !mbar_wait(smem_u32(&full[s]), parity, &g_fd_error_word)) {
                 s_abort = 1;
                 break;
+            }
+            if (tid == 0) {
+                if (t == 0) DT_MARK(3);
+                DT_MARK(6);
             }
             const int64_t j0 = jb + int64_t(t) * kTileKeys;
             const int nk = int(je - j0 < kTileKeys ? je - j0 : kTileKeys);
@@ -411,6 +469,14 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
     }
 
     __syncthreads();  // every tile consumed (or abandoned); the ring is free
+    if (p.kv_early) {
+        // Early copies past the tile count seen after the wait (a broken
+        // early-copy promise) are drained before the merge reuses the ring.
+        if (tid == 0 && !s_abort)
+            for (int t = ntiles; t < s_issued && t < NST; ++t)
+                mbar_wait(smem_u32(&full[t]), 0u, &g_fd_error_word);
+        __syncthreads();
+    }
     if (s_abort) {
         if (tid == 0) {
             // Drain (bounded) the copies issued for tiles nobody consumed.
@@ -438,7 +504,9 @@ __global__ void __launch_bounds__(FDShape<KV, HD>::kThreads, 1) fd_partial_kerne
             for (int e = 0; e < E; ++e) oo[(warp * G + g) * HD + lane * E + e] = o[g][e];
     }
     __syncthreads();
-    write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, tid, kFastThreads);
+    if (tid == 0) DT_MARK(2);
+    write_result<G, HD, kCWarps>(a, b, hq0, split, mm, ll, oo, oo + kCWarps * G * HD, tid, kFastThreads);
+    DT_COMMIT(200);
 }
 
 // Generic kernel (any Hd <= 512, any alignment, q dtype may differ from
@@ -531,6 +599,7 @@ __global__ void __launch_bounds__(kThreads) fd_generic_kernel(const FDArgs a) {
 // groups-th split with several independent loads in flight, and the group
 // partial sums are added in shared memory.
 constexpr int kCombThreads = 256;
+constexpr int kCombK = 8;  // splits per thread on the one-round-trip path
 
 // blockIdx.z takes head dims [z * dchunk, (z + 1) * dchunk): more CTAs for
 // the few (b, hq) rows of a decode step.
@@ -543,12 +612,83 @@ __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* p
     float* part = sh + ((splits + 3) & ~3);
     __shared__ float red[kCombThreads / 32];
     __shared__ float s_M, s_L;
+    DT_SHARED
+    if (threadIdx.x == 0) {
+        DT_INIT();
+        DT_MARK(0);
+    }
     pdl_launch_dependents();
     pdl_wait();
+    if (threadIdx.x == 0) DT_MARK(1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t bh = int64_t(blockIdx.y) * Nq + blockIdx.x;
     const float* m = pm + bh * splits;
     const float* l = pl + bh * splits;
+    {
+        // Few splits (every decode step): each thread owns one float4
+        // column of the chunk and up to kCombK splits, and issues all of its
+        // loads (m, l and O of those splits) at once, so the whole combine
+        // costs one round trip to L2 and two CTA barriers.
+        const int64_t d0 = int64_t(blockIdx.z) * dchunk;
+        const int64_t dn = Hd - d0 < dchunk ? Hd - d0 : dchunk;
+        const int cols = int(dn / 4);
+        const int groups = cols > 0 ? kCombThreads / cols : 0;
+        if ((Hd & 3) == 0 && (dn & 3) == 0 && cols > 0 && cols <= kCombThreads && splits <= groups * kCombK) {
+            float* red_m = sh;                    // [groups]
+            float* red_l = sh + groups;           // [groups]
+            float4* part = reinterpret_cast<float4*>(sh + 2 * ((groups + 1) & ~1));  // [groups][cols]
+            const int col = tid % cols, grp = tid / cols;
+            const bool act = grp < groups;
+            const float* o = po + bh * splits * Hd + d0;
+            float ms[kCombK], ls[kCombK];
+            float4 ov[kCombK];
+#pragma unroll
+            for (int k = 0; k < kCombK; ++k) {
+                const int s = grp + k * groups;
+                if (act && s < splits) {
+                    ms[k] = m[s];
+                    ls[k] = l[s];
+                    ov[k] = reinterpret_cast<const float4*>(o + int64_t(s) * Hd)[col];
+                } else {
+                    ms[k] = -INFINITY;
+                    ls[k] = 0.f;
+                    ov[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            float mloc = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < kCombK; ++k) mloc = fmaxf(mloc, ms[k]);
+            if (act && col == 0) red_m[grp] = mloc;
+            __syncthreads();
+            float M = -INFINITY;
+            for (int g = 0; g < groups; ++g) M = fmaxf(M, red_m[g]);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            float lsum = 0.f;
+#pragma unroll
+            for (int k = 0; k < kCombK; ++k) {
+                const float f = (M == -INFINITY || ms[k] == -INFINITY) ? 0.f : exp2f(ms[k] - M);
+                lsum = fmaf(f, ls[k], lsum);
+                acc.x = fmaf(f, ov[k].x, acc.x); acc.y = fmaf(f, ov[k].y, acc.y);
+                acc.z = fmaf(f, ov[k].z, acc.z); acc.w = fmaf(f, ov[k].w, acc.w);
+            }
+            if (act) {
+                part[grp * cols + col] = acc;
+                if (col == 0) red_l[grp] = lsum;
+            }
+            __syncthreads();
+            float L = 0.f;
+            for (int g = 0; g < groups; ++g) L += red_l[g];
+            const float inv_l = L > 0.f ? 1.0f / L : 0.f;
+            for (int d = tid; d < dn; d += kCombThreads) {
+                const int c = d >> 2, e = d & 3;
+                float v = 0.f;
+                for (int g = 0; g < groups; ++g) v += reinterpret_cast<const float*>(part + g * cols + c)[e];
+                Elem<OT>::store(out, bh * Hd + d0 + d, v * inv_l);
+            }
+            DT_COMMIT(201);
+            return;
+        }
+    }
     float mx = -INFINITY;
     for (int s = tid; s < splits; s += kCombThreads) mx = fmaxf(mx, m[s]);
     mx = warp_max(mx);
@@ -620,6 +760,7 @@ __global__ void __launch_bounds__(kCombThreads) fd_combine_kernel(const float* p
             Elem<OT>::store(out, bh * Hd + d0 + d, acc * inv_l);
         }
     }
+    DT_COMMIT(201);
 }
 
 bool fast_path(const FlashDecode& p) {
@@ -761,7 +902,7 @@ cudaError_t flash_decode_combine(const FlashDecode& p, const FlashDecodePlan& pl
     const int64_t dchunk = (p.Hd % 64 == 0 && p.Hd > 64 && p.B * p.Nq < 4 * current_sm_count()) ? 64 : p.Hd;
     dim3 grid(unsigned(p.Nq), unsigned(p.B), unsigned(p.Hd / dchunk));
     const int64_t groups = (dchunk % 4 == 0 && dchunk / 4 <= kCombThreads) ? kCombThreads / (dchunk / 4) : 0;
-    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(groups) * dchunk) * 4;
+    size_t smem = (size_t((plan.splits + 3) & ~3) + size_t(groups) * dchunk + 2 * size_t(groups + 2)) * 4;
     switch (p.out_dtype) {
     case PC_F32:
         return launch_k(fd_combine_kernel<TF32>, grid, dim3(kCombThreads), smem, s, po, pm, pl, p.out, p.Nq, p.Hd,
@@ -807,6 +948,23 @@ uint32_t read_and_clear_aq_errors();
 
 }  // namespace launch
 }  // namespace popcorn
+
+#ifdef PC_DECODE_TRACE
+extern "C" __attribute__((visibility("default"))) int pc_debug_fd_trace(unsigned long long* host, int max,
+                                                                        int reset) {
+    unsigned int n = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(&n, popcorn::launch::g_dt_n, sizeof(n));
+    if (n > PC_DT_MAX) n = PC_DT_MAX;
+    if (host && max > 0)
+        cudaMemcpyFromSymbol(host, popcorn::launch::g_dt_buf, size_t(n < unsigned(max) ? n : max) * 9 * 8);
+    if (reset) {
+        unsigned int z = 0;
+        cudaMemcpyToSymbol(popcorn::launch::g_dt_n, &z, sizeof(z));
+    }
+    return int(n);
+}
+#endif
 
 extern "C" int pc_device_error_check(int device, uint32_t* flags) {
     int prev = 0;

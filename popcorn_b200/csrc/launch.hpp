@@ -82,6 +82,7 @@ struct Gemv {
     int64_t q_rows, kv_rows, Hd, Smax, offset;
     const int32_t* pos_dev;
     L2Prefetch pf;
+    int pre_stages = 0;  // stages issued before the activation row is staged (0: the whole ring)
 };
 cudaError_t gemv(const Gemv& p, cudaStream_t stream);
 
@@ -126,6 +127,7 @@ struct FlashDecode {
     int mask_kind;
     int32_t window;
     L2Prefetch pf;
+    int kv_early = 0;  // copy K/V tiles without the newest row before the dependency wait
 };
 struct FlashDecodePlan {
     int splits;

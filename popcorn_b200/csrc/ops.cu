@@ -15,6 +15,10 @@ void Kernel::set_prefetch(int, const void*, uint64_t) {
     fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, std::string(name()) + " takes no L2 prefetch hint.");
 }
 
+void Kernel::set_hint(int hint, int64_t) {
+    fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, std::string(name()) + " takes no hint " + std::to_string(hint) + ".");
+}
+
 namespace {
 
 void put_prefetch(launch::L2Prefetch& pf, int slot, const void* ptr, uint64_t bytes) {
@@ -112,6 +116,11 @@ public:
         put_prefetch(pf_, slot, ptr, bytes);
     }
 
+    void set_hint(int hint, int64_t value) override {
+        if (path_ != PC_PATH_DECODING || hint != PC_HINT_KV_EARLY) Kernel::set_hint(hint, value);
+        kv_early_ = value ? 1 : 0;
+    }
+
     std::vector<Binding> tensors() const override {
         std::vector<Binding> b = {{q_, PC_ACCESS_READ}, {k_, PC_ACCESS_READ}, {v_, PC_ACCESS_READ}, {out_, PC_ACCESS_WRITE}};
         if (has_lens_) b.push_back({lens_, PC_ACCESS_READ});
@@ -132,7 +141,7 @@ public:
         }
         launch::FlashDecode p{q_.data(), q_.dtype(), k_.data(), v_.data(), k_.dtype(), out_.data(), out_.dtype(),
                               B_, Nq_, Nkv_, Sk_, Hd_, has_lens_ ? static_cast<const int32_t*>(lens_.data()) : nullptr,
-                              scale_, mask_.kind, mask_.window, pf_};
+                              scale_, mask_.kind, mask_.window, pf_, kv_early_};
         launch::FlashDecodePlan plan = launch::flash_decode_plan(p, enc.sm_count());
         // FlashDecoding.swift:55-59: partial O [B,Nq,P,Hd], m and l [B,Nq,P], f32.
         std::vector<ScratchSpec> specs = {{{B_, Nq_, plan.splits, Hd_}, PC_F32},
@@ -175,6 +184,7 @@ private:
     pc_attention_mask mask_;
     int path_ = PC_PATH_DECODING;
     launch::L2Prefetch pf_{};
+    int kv_early_ = 0;
 };
 
 // ---------------------------------------------------------------------------
@@ -1522,6 +1532,17 @@ int pc_kernel_set_l2_prefetch(pc_kernel* kernel, int32_t slot, const void* ptr, 
     try {
         if (!kernel) fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, "kernel is null.");
         kernel->impl->set_prefetch(slot, ptr, bytes);
+    } catch (const PopcornError& e) {
+        set_last_error(e.message);
+        return e.code;
+    }
+    return PC_OK;
+}
+
+int pc_kernel_set_hint(pc_kernel* kernel, int32_t hint, int64_t value) {
+    try {
+        if (!kernel) fail(PC_ERR_KERNEL_FUNCTION_NOT_FOUND, "kernel is null.");
+        kernel->impl->set_hint(hint, value);
     } catch (const PopcornError& e) {
         set_last_error(e.message);
         return e.code;

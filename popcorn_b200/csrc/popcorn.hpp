@@ -166,6 +166,8 @@ public:
     // L2 prefetch hint (slot 0 or 1) for kernels that stream from HBM; the
     // default rejects it.
     virtual void set_prefetch(int slot, const void* ptr, uint64_t bytes);
+    // Scheduling hints (pc_kernel_hint); the default rejects them.
+    virtual void set_hint(int hint, int64_t value);
 
 protected:
     std::string function_names_;

@@ -91,7 +91,7 @@ class DecodeStack:
     """
 
     def __init__(self, library, shape, n_layers, seed=0, device=0, l2_prefetch=False, fused=False, vocab=0,
-                 qk_norm_rope=False, rope_theta=10000.0, norm_add_one=True):
+                 qk_norm_rope=False, rope_theta=10000.0, norm_add_one=True, kv_early=None):
         """vocab > 0 adds the step's tail: the final RMSNorm fused into the LM
         head GEMV (tied embedding [vocab, H]) into `logits`, then Argmax into
         `token` (int32) — the greedy next token (Argmax.metal).
@@ -105,7 +105,11 @@ class DecodeStack:
 
         norm_add_one: RMSNorm weights are applied as (1 + w) (Gemma 2 style,
         RMSNorm.swift addOneToWeight) or as w (Gemma 4)."""
+        import os
         import torch
+        if kv_early is None:
+            kv_early = os.environ.get("POPCORN_KV_EARLY", "0") == "1"
+        self.kv_early = kv_early
         self.norm_add_one = norm_add_one
         self.shape = shape
         self.library = library
@@ -179,6 +183,10 @@ class DecodeStack:
                                              norm_v=True))
             ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                                   mask=AttentionMask.causal))
+            if self.kv_early:
+                # the kernel before it (QKV projection, or the q/k/v norm +
+                # RoPE) writes only the newest K/V row
+                ks[-1].set_hint(Kernels.FlashDecodingRagged.HINT_KV_EARLY)
             ks.append(Kernels.MatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
             ks.append(Kernels.GatedMLP(self.h, w.w_gate, w.w_up, into=self.act, norm_weight=w.mlp_norm, eps=s.eps,
                                        add_one_to_weight=self.norm_add_one, activation=s.activation))

@@ -8,7 +8,8 @@ import pytest
 import oracle
 from tests.conftest import approx_equal
 from tests.golden import make_golden
-from tests.gpu_util import assert_close, empty_dev, f32, from_dev, rand, to_dev
+from tests.gpu_util import (assert_close, dot_tolerance, empty_dev, f32, from_dev, gated_candidates, rand,
+                            residual_candidates, to_dev)
 
 pytestmark = pytest.mark.gpu
 
@@ -149,13 +150,15 @@ def _fd_case(pc, enc, B, Nq, Nkv, S, Hd, dt, odt, scale, mask="causal", window=-
     k = rand(rng, (B, Nkv, S, Hd), dt, kv_scale)
     v = rand(rng, (B, Nkv, S, Hd), dt)
     exp = oracle.flash_decoding(q, dt, k, v, dt, odt, scale, mask=mask, window=window)
+    pre = oracle.flash_decoding(q, dt, k, v, dt, "f32", scale, mask=mask, window=window)
     out = empty_dev((B, Nq, 1, Hd), odt)
     m = {"causal": pc.AttentionMask.causal, "bidirectional": pc.AttentionMask.bidirectional}.get(mask)
     if m is None:
         m = pc.AttentionMask.causal_sliding_window(window)
     kern = pc.Kernels.FlashAttention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), into=out, scale=scale, mask=m)
     run(enc, kern)
-    assert_close(from_dev(out, odt), exp, odt, what="FD B%d %d/%d S%d Hd%d %s->%s" % (B, Nq, Nkv, S, Hd, dt, odt))
+    assert_close(from_dev(out, odt), exp, odt, what="FD B%d %d/%d S%d Hd%d %s->%s" % (B, Nq, Nkv, S, Hd, dt, odt),
+                 pre=pre)
     return kern
 
 
@@ -216,10 +219,11 @@ def test_fd_ragged_sweep_shapes(pc, enc, B, ctx):
     k = rand(rng, (B, Nkv, ctx, Hd), "bf16")
     v = rand(rng, (B, Nkv, ctx, Hd), "bf16")
     exp = oracle.flash_decoding(q, "bf16", k, v, "bf16", "bf16", 1.0 / 16, seq_lens=lens)
+    pre = oracle.flash_decoding(q, "bf16", k, v, "bf16", "f32", 1.0 / 16, seq_lens=lens)
     out = empty_dev((B, Nq, 1, Hd), "bf16")
     run(enc, pc.Kernels.FlashDecodingRagged(to_dev(q, "bf16"), to_dev(k, "bf16"), to_dev(v, "bf16"),
                                             to_dev(lens, "i32"), into=out, scale=1.0 / 16))
-    assert_close(from_dev(out, "bf16"), exp, "bf16", what="ragged B%d ctx%d" % (B, ctx))
+    assert_close(from_dev(out, "bf16"), exp, "bf16", what="ragged B%d ctx%d" % (B, ctx), pre=pre)
 
 
 def test_fd_ragged_edges(pc, enc):
@@ -296,10 +300,11 @@ def test_rmsnorm(pc, enc, dt, rows, H, weight, add_one):
     x = rand(rng, (rows, H), dt)
     w = (rng.standard_normal(H) * 0.1).astype(np.float32) if weight else None
     exp = oracle.rmsnorm(x, dt, w, eps=1e-6, add_one=add_one)
+    pre = oracle.rmsnorm(x, dt, w, odt="f32", eps=1e-6, add_one=add_one)
     out = empty_dev((rows, H), dt)
     run(enc, pc.Kernels.RMSNorm(to_dev(x, dt), None if w is None else to_dev(w, "f32"), into=out, eps=1e-6,
                                 add_one_to_weight=add_one))
-    assert_close(from_dev(out, dt), exp, dt, what="rmsnorm")
+    assert_close(from_dev(out, dt), exp, dt, what="rmsnorm", pre=pre)
 
 
 @pytest.mark.parametrize("xdt,wdt,odt", [("f32", "f32", "f32"), ("f32", "bf16", "f32"), ("bf16", "bf16", "f32"),
@@ -311,11 +316,12 @@ def test_matvec(pc, enc, xdt, wdt, odt, K, N):
     x = rand(rng, (1, K), xdt)
     w = rand(rng, (N, K), wdt, 0.02)
     exp = oracle.matvec_nk(x[0], xdt, w, wdt, odt)
+    pre = oracle.matvec_nk(x[0], xdt, w, wdt, "f32")
     out = empty_dev((1, N), odt)
     kern = pc.Kernels.Matmul(to_dev(x, xdt), to_dev(w, wdt), into=out, transpose_b=True)
     assert kern.function_names[0].startswith("matvec_nk_")
     run(enc, kern)
-    assert_close(from_dev(out, odt)[0], exp, odt, what="matvec %s.%s.%s K%d N%d" % (xdt, wdt, odt, K, N))
+    assert_close(from_dev(out, odt)[0], exp, odt, what="matvec %s.%s.%s K%d N%d" % (xdt, wdt, odt, K, N), pre=pre)
 
 
 @pytest.mark.parametrize("adt,bdt,cdt", [("f32", "f32", "f32"), ("bf16", "bf16", "bf16"), ("f16", "f16", "f32"),
@@ -327,9 +333,10 @@ def test_matmul_general(pc, enc, adt, bdt, cdt, M, K, N, tb):
     a = rand(rng, (M, K), adt)
     b = rand(rng, (N, K) if tb else (K, N), bdt)
     exp = oracle.matmul(a, adt, b, bdt, cdt, tb)
+    pre = oracle.matmul(a, adt, b, bdt, "f32", tb)
     out = empty_dev((M, N), cdt)
     run(enc, pc.Kernels.Matmul(to_dev(a, adt), to_dev(b, bdt), into=out, transpose_b=tb))
-    assert_close(from_dev(out, cdt), exp, cdt, what="matmul")
+    assert_close(from_dev(out, cdt), exp, cdt, what="matmul", pre=pre)
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
@@ -341,9 +348,9 @@ def test_elementwise(pc, enc, dt):
     ad, bd = to_dev(a, dt), to_dev(b, dt)
     out = empty_dev((n,), dt)
     run(enc, pc.Kernels.GeluTanh(ad, into=out))
-    assert_close(from_dev(out, dt), oracle.gelu_tanh(a, dt), dt, what="gelu")
+    assert_close(from_dev(out, dt), oracle.gelu_tanh(a, dt), dt, what="gelu", pre=oracle.gelu_tanh(a, dt, "f32"))
     run(enc, pc.Kernels.SiLU(ad, into=out))
-    assert_close(from_dev(out, dt), oracle.silu(a, dt), dt, what="silu")
+    assert_close(from_dev(out, dt), oracle.silu(a, dt), dt, what="silu", pre=oracle.silu(a, dt, "f32"))
     run(enc, pc.Kernels.Mul(ad, bd, into=out))
     assert np.array_equal(from_dev(out, dt).view(np.uint8), oracle.mul(a, b, dt).view(np.uint8))
     run(enc, pc.Kernels.Add(ad, bd, into=out))
@@ -363,10 +370,11 @@ def test_rmsnorm_matmul(pc, enc, dt):
     w = rand(rng, (N, K), dt, 0.02)
     xn = oracle.rmsnorm(x, dt, nw, eps=1e-6, add_one=True)
     exp = oracle.matvec_nk(xn[0], dt, w, dt, dt)
+    pre = oracle.matvec_nk(xn[0], dt, w, dt, "f32")
     out = empty_dev((1, N), dt)
     run(enc, pc.Kernels.RMSNormMatmul(to_dev(x, dt), to_dev(nw, "f32"), to_dev(w, dt), into=out, eps=1e-6,
                                       add_one_to_weight=True))
-    assert_close(from_dev(out, dt)[0], exp, dt, what="rmsnorm+matvec")
+    assert_close(from_dev(out, dt)[0], exp, dt, what="rmsnorm+matvec", pre=pre)
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
@@ -384,11 +392,13 @@ def test_gated_mlp(pc, enc, dt, act, norm):
     u = oracle.matvec_nk(xn[0], dt, wu, dt, dt)
     a = oracle.silu(g, dt) if act == 1 else oracle.gelu_tanh(g, dt)
     exp = oracle.mul(a, u, dt)
+    cands = gated_candidates(oracle.matvec_nk(xn[0], dt, wg, dt, "f32"), oracle.matvec_nk(xn[0], dt, wu, dt, "f32"),
+                             dt, act)
     out = empty_dev((1, F), dt)
     run(enc, pc.Kernels.GatedMLP(to_dev(x, dt), to_dev(wg, dt), to_dev(wu, dt), into=out,
                                  norm_weight=to_dev(nw, "f32") if norm else None, eps=1e-6, add_one_to_weight=True,
                                  activation=act))
-    assert_close(from_dev(out, dt)[0], exp, dt, what="gated mlp")
+    assert_close(from_dev(out, dt)[0], exp, dt, what="gated mlp", candidates=cands)
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
@@ -400,9 +410,10 @@ def test_matmul_residual(pc, enc, dt):
     r = rand(rng, (1, N), dt)
     y = oracle.matvec_nk(a[0], dt, w, dt, dt)
     exp = oracle.add(r[0], y, dt)
+    cands = residual_candidates(oracle.matvec_nk(a[0], dt, w, dt, "f32"), r[0], dt)
     out = empty_dev((1, N), dt)
     run(enc, pc.Kernels.MatmulResidual(to_dev(a, dt), to_dev(w, dt), to_dev(r, dt), into=out))
-    assert_close(from_dev(out, dt)[0], exp, dt, what="matvec+add")
+    assert_close(from_dev(out, dt)[0], exp, dt, what="matvec+add", candidates=cands)
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
@@ -417,16 +428,18 @@ def test_qkv_projection(pc, enc, dt, device_pos):
     vc = rand(rng, (1, Nkv, Smax, Hd), dt)
     xn = oracle.rmsnorm(x, dt, nw, eps=1e-6, add_one=True)
     qkv = oracle.matvec_nk(xn[0], dt, w, dt, dt)
+    qkv_pre = oracle.matvec_nk(xn[0], dt, w, dt, "f32")
     kd, vd = to_dev(kc, dt), to_dev(vc, dt)
     q_out = empty_dev((1, Nq, 1, Hd), dt)
     position = to_dev(np.array([pos], np.int32), "i32") if device_pos else None
     run(enc, pc.Kernels.QKVProjection(to_dev(x, dt), to_dev(nw, "f32"), to_dev(w, dt), q_out, kd, vd,
                                       offset=0 if device_pos else pos, position=position, eps=1e-6,
                                       add_one_to_weight=True))
-    assert_close(from_dev(q_out, dt).ravel(), qkv[:Nq * Hd], dt, what="q")
+    assert_close(from_dev(q_out, dt).ravel(), qkv[:Nq * Hd], dt, what="q", pre=qkv_pre[:Nq * Hd])
     gk, gv = from_dev(kd, dt), from_dev(vd, dt)
-    assert_close(gk[0, :, pos].ravel(), qkv[Nq * Hd:(Nq + Nkv) * Hd], dt, what="k row")
-    assert_close(gv[0, :, pos].ravel(), qkv[(Nq + Nkv) * Hd:], dt, what="v row")
+    assert_close(gk[0, :, pos].ravel(), qkv[Nq * Hd:(Nq + Nkv) * Hd], dt, what="k row",
+                 pre=qkv_pre[Nq * Hd:(Nq + Nkv) * Hd])
+    assert_close(gv[0, :, pos].ravel(), qkv[(Nq + Nkv) * Hd:], dt, what="v row", pre=qkv_pre[(Nq + Nkv) * Hd:])
     # every other cache row is untouched (bit-exact)
     mask = np.ones(Smax, bool)
     mask[pos] = False
@@ -448,12 +461,13 @@ def test_prefill_attention(pc, enc, dt, odt, mask, window, B, Nq, Nkv, Sq, Sk, H
     v = rand(rng, (B, Nkv, Sk, Hd), dt)
     scale = 1.0 / np.sqrt(Hd)
     exp = oracle.flash_attention(q, dt, k, v, dt, odt, scale, mask=mask, window=window)
+    pre = oracle.flash_attention(q, dt, k, v, dt, "f32", scale, mask=mask, window=window)
     out = empty_dev((B, Nq, Sq, Hd), odt)
     m = {"causal": pc.AttentionMask.causal, "bidirectional": pc.AttentionMask.bidirectional}.get(mask)
     if m is None:
         m = pc.AttentionMask.causal_sliding_window(window)
     run(enc, pc.Kernels.FlashAttention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), into=out, scale=scale, mask=m))
-    assert_close(from_dev(out, odt), exp, odt, what="prefill FA")
+    assert_close(from_dev(out, odt), exp, odt, what="prefill FA", pre=pre)
 
 
 @pytest.mark.parametrize("dt,odt", [("bf16", "bf16"), ("bf16", "f32"), ("f16", "f16")])
@@ -469,6 +483,7 @@ def test_prefill_attention_tcgen05(pc, enc, dt, odt, mask, window, B, Nq, Nkv, S
     v = rand(rng, (B, Nkv, Sk, Hd), dt)
     scale = 1.0 / np.sqrt(Hd)
     exp = oracle.flash_attention(q, dt, k, v, dt, odt, scale, mask=mask, window=window)
+    pre = oracle.flash_attention(q, dt, k, v, dt, "f32", scale, mask=mask, window=window)
     out = empty_dev((B, Nq, Sq, Hd), odt)
     m = {"causal": pc.AttentionMask.causal, "bidirectional": pc.AttentionMask.bidirectional}.get(mask)
     if m is None:
@@ -476,7 +491,7 @@ def test_prefill_attention_tcgen05(pc, enc, dt, odt, mask, window, B, Nq, Nkv, S
     kern = pc.Kernels.FlashAttention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt), into=out, scale=scale, mask=m)
     assert kern.function_names == ["flash_attention_tc_bf16"]
     run(enc, kern)
-    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 prefill FA")
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 prefill FA", pre=pre)
     assert pc.device_error_check(0) == 0
 
 
@@ -497,8 +512,9 @@ def test_prefill_attention_tcgen05_config4(pc, enc):
         ks = from_dev(k[b:b + 1, hkv:hkv + 1].contiguous(), "bf16")
         vs = from_dev(v[b:b + 1, hkv:hkv + 1].contiguous(), "bf16")
         exp = oracle.flash_attention(qs, "bf16", ks, vs, "bf16", "bf16", 1.0 / 16, mask="causal")
+        pre = oracle.flash_attention(qs, "bf16", ks, vs, "bf16", "f32", 1.0 / 16, mask="causal")
         assert_close(from_dev(out[b:b + 1, hq:hq + 1].contiguous(), "bf16"), exp, "bf16",
-                     what="config-4 FA b%d h%d" % (b, hq))
+                     what="config-4 FA b%d h%d" % (b, hq), pre=pre)
 
 
 def test_no_device_errors_recorded(pc):
@@ -522,7 +538,9 @@ def test_matmul_tcgen05(pc, enc, M, K, N, dt, odt):
     assert kern.function_names == ["matmul_tc_bf16_tb"]
     run(enc, kern)
     exp = oracle.matmul(a, dt, b, dt, odt, True)
-    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul %dx%dx%d" % (M, K, N))
+    terms = np.abs(f32(a, dt).astype(np.float64)) @ np.abs(f32(b, dt).astype(np.float64)).T
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul %dx%dx%d" % (M, K, N),
+                 pre=oracle.matmul(a, dt, b, dt, "f32", True), pre_tol=dot_tolerance(terms))
 
 
 @pytest.mark.parametrize("M,K,N,dt,odt", [(128, 64, 256, "bf16", "f32"), (256, 2304, 512, "bf16", "bf16"),
@@ -538,7 +556,9 @@ def test_matmul_tcgen05_b_not_transposed(pc, enc, M, K, N, dt, odt):
     assert kern.function_names == ["matmul_tc_bf16_nn"]
     run(enc, kern)
     exp = oracle.matmul(a, dt, b, dt, odt, False)
-    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul (B [K,N]) %dx%dx%d" % (M, K, N))
+    terms = np.abs(f32(a, dt).astype(np.float64)) @ np.abs(f32(b, dt).astype(np.float64))
+    assert_close(from_dev(out, odt), exp, odt, what="tcgen05 matmul (B [K,N]) %dx%dx%d" % (M, K, N),
+                 pre=oracle.matmul(a, dt, b, dt, "f32", False), pre_tol=dot_tolerance(terms))
 
 
 def test_matmul_tcgen05_config4_rows(pc, enc):
@@ -553,9 +573,12 @@ def test_matmul_tcgen05_config4_rows(pc, enc):
     rows = np.random.default_rng(0).choice(M, 24, replace=False)
     rows.sort()
     a_np = from_dev(a[torch.from_numpy(rows).cuda()].contiguous(), "bf16")
-    exp = oracle.matmul(a_np, "bf16", from_dev(b, "bf16"), "bf16", "bf16", True)
+    b_np = from_dev(b, "bf16")
+    exp = oracle.matmul(a_np, "bf16", b_np, "bf16", "bf16", True)
     got = from_dev(out, "bf16")[rows]
-    assert_close(got, exp, "bf16", what="config-4 GEMM rows")
+    terms = np.abs(f32(a_np, "bf16").astype(np.float64)) @ np.abs(f32(b_np, "bf16").astype(np.float64)).T
+    assert_close(got, exp, "bf16", what="config-4 GEMM rows", pre=oracle.matmul(a_np, "bf16", b_np, "bf16", "f32", True),
+                 pre_tol=dot_tolerance(terms))
 
 
 def test_scalar_mul_kat(kats):

@@ -73,5 +73,7 @@ def test_allreduce_wait_gives_up_then_recovers():
     o = (p0 + p1).bfloat16().float()
     exp_sum = (res.float() + o).bfloat16()
     assert torch.equal(s_out, exp_sum)
-    exp_norm = oracle.rmsnorm(from_dev(exp_sum, "bf16"), "bf16", w.cpu().numpy(), eps=1e-6, add_one=True)
-    assert_close(from_dev(n_out, "bf16"), exp_norm, "bf16", what="norm after recovery")
+    s_host = from_dev(exp_sum, "bf16")
+    exp_norm = oracle.rmsnorm(s_host, "bf16", w.cpu().numpy(), eps=1e-6, add_one=True)
+    assert_close(from_dev(n_out, "bf16"), exp_norm, "bf16", what="norm after recovery",
+                 pre=oracle.rmsnorm(s_host, "bf16", w.cpu().numpy(), odt="f32", eps=1e-6, add_one=True))
