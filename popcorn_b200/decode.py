@@ -104,11 +104,16 @@ class DecodeStack:
         projection; the fused step folds it into the attention items.
 
         norm_add_one: RMSNorm weights are applied as (1 + w) (Gemma 2 style,
-        RMSNorm.swift addOneToWeight) or as w (Gemma 4)."""
+        RMSNorm.swift addOneToWeight) or as w (Gemma 4).
+
+        kv_early: each layer's decode attention gets PC_HINT_KV_EARLY (the
+        kernel before it writes only the newest K/V row), so it copies the
+        older K/V tiles while that kernel drains (default on;
+        POPCORN_KV_EARLY=0 turns it off for comparisons)."""
         import os
         import torch
         if kv_early is None:
-            kv_early = os.environ.get("POPCORN_KV_EARLY", "0") == "1"
+            kv_early = os.environ.get("POPCORN_KV_EARLY", "1") == "1"
         self.kv_early = kv_early
         self.norm_add_one = norm_add_one
         self.shape = shape
