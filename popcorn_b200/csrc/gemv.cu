@@ -93,7 +93,6 @@ __device__ __forceinline__ void gemv_store(const Gemv& p, int64_t n, float a, fl
 // stride 16-byte chunks (conflict-free shared loads), and the k-chunks of a
 // row accumulate in registers until the warp reduction and the epilogue.
 struct GemvPlan {
-    int l2ahead;      // stages pulled into L2 ahead of the ring's bulk copies (0: none)
     int kc;           // columns per stage (multiple of 8)
     int nkc;          // stages per tile
     int ntiles;       // tiles of 8 outputs
@@ -140,37 +139,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
     if (warp == kConsumers) {
         // ---- producer ----
         if (lane == 0) {
-            // L2 cursor: g.l2ahead stages past the ring, pulled into L2 so the
-            // bulk copy of that stage later finds its rows there.
-            int pt = blockIdx.x, pk = 0, pm = 0;
-            auto l2_advance = [&]() {
-                if (++pm == R) {
-                    pm = 0;
-                    if (++pk == g.nkc) {
-                        pk = 0;
-                        pt += gridDim.x;
-                    }
-                }
-            };
-            auto l2_issue = [&]() {
-                if (pt >= g.ntiles) return;
-                const int64_t k0 = int64_t(pk) * g.kc;
-                const int kcols = int(K - k0 < g.kc ? K - k0 : g.kc);
-                const int64_t n0 = int64_t(pt) * 8;
-                const int nvalid = int(p.N - n0 < 8 ? p.N - n0 : 8);
-                const char* base = static_cast<const char*>(pm == 0 ? p.w : p.w2);
-                if (kcols == K) {
-                    bulk_prefetch_l2(base + n0 * K * es, uint32_t(kcols) * es * nvalid);
-                } else {
-                    for (int r = 0; r < nvalid; ++r)
-                        bulk_prefetch_l2(base + ((n0 + r) * K + k0) * es, uint32_t(kcols) * es);
-                }
-            };
-            if (g.l2ahead > 0)
-                for (int i = 0; i < g.stages + g.l2ahead; ++i) {
-                    if (i >= g.stages) l2_issue();
-                    l2_advance();
-                }
             int it = 0;
             for (int tile = blockIdx.x; tile < g.ntiles; tile += gridDim.x) {
                 for (int kci = 0; kci < g.nkc && !s_abort; ++kci) {
@@ -198,10 +166,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
                                          row_bytes, bar);
                         }
                         s_issued = it + 1;
-                        if (g.l2ahead > 0) {
-                            l2_issue();
-                            l2_advance();
-                        }
                     }
                 }
                 if (s_abort) break;
@@ -499,11 +463,6 @@ bool make_plan(const Gemv& p, GemvPlan& g) {
     if (xbytes + 2 * size_t(g.stage_bytes) > budget) return false;
     g.stages = int((budget - xbytes) / g.stage_bytes);
     if (g.stages > 8) g.stages = 8;
-    static const int env_l2 = [] {
-        const char* e = getenv("POPCORN_GEMV_L2AHEAD");
-        return e ? atoi(e) : 0;
-    }();
-    g.l2ahead = env_l2;
     return g.stages >= 2;
 }
 

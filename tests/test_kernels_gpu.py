@@ -226,6 +226,33 @@ def test_fd_ragged_sweep_shapes(pc, enc, B, ctx):
     assert_close(from_dev(out, "bf16"), exp, "bf16", what="ragged B%d ctx%d" % (B, ctx), pre=pre)
 
 
+@pytest.mark.parametrize("B,ctx", [(32, 32768), (64, 16384)])
+def test_fd_ragged_sweep_large(pc, enc, B, ctx):
+    """The largest BASELINE config-3 points (16 Q / 8 KV heads, hd 256, bf16,
+    ragged lengths U[ctx/2, ctx]), where the ragged split planner does its
+    real work: the whole batch on the GPU (8.6 GB of K/V, generated there),
+    four sampled sequences against the oracle run per sequence."""
+    Nq, Nkv, Hd = 16, 8, 256
+    gen = torch.Generator(device="cuda").manual_seed(B + ctx)
+    lens = np.random.default_rng(B * 7 + ctx).integers(ctx // 2, ctx + 1, size=B).astype(np.int32)
+    q = torch.randn(B, Nq, 1, Hd, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Nkv, ctx, Hd, device="cuda", generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, Nkv, ctx, Hd, device="cuda", generator=gen).to(torch.bfloat16)
+    out = empty_dev((B, Nq, 1, Hd), "bf16")
+    run(enc, pc.Kernels.FlashDecodingRagged(q, k, v, to_dev(lens, "i32"), into=out, scale=1.0 / 16))
+    got = from_dev(out, "bf16")
+    for b in (0, 1, B // 2, B - 1):
+        L = int(lens[b])
+        qs = from_dev(q[b:b + 1].contiguous(), "bf16")
+        ks = from_dev(k[b:b + 1, :, :L].contiguous(), "bf16")
+        vs = from_dev(v[b:b + 1, :, :L].contiguous(), "bf16")
+        exp = oracle.flash_decoding(qs, "bf16", ks, vs, "bf16", "bf16", 1.0 / 16)
+        pre = oracle.flash_decoding(qs, "bf16", ks, vs, "bf16", "f32", 1.0 / 16)
+        assert_close(got[b:b + 1], exp, "bf16", what="ragged B%d ctx%d seq %d (len %d)" % (B, ctx, b, L), pre=pre)
+    del k, v
+    torch.cuda.empty_cache()
+
+
 def test_fd_ragged_edges(pc, enc):
     """Lengths 0 (zeros out), 1 and Smax in one batch."""
     rng = np.random.default_rng(9)
