@@ -124,6 +124,28 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
     unsigned char* ring = smem;
     float4* xs = reinterpret_cast<float4*>(smem + size_t(g.stages) * g.stage_bytes);
 
+    // The norm weights depend on nothing: the consumers request them before
+    // the producer issues the ring's bulk copies, so they do not queue
+    // behind ~190 KB of weight traffic on this SM.
+    constexpr bool kX16 = Elem<XT>::bytes == 2 && VEC == 8;
+    constexpr int kXC = 8;  // chunks per thread: rows up to 8 * 8 * 256 elements
+    const bool chunked = kX16 && K <= int64_t(kXC) * 8 * kConsumers * 32 &&
+                         (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    float4 nwv[NORM ? kXC : 1][2];
+    const bool nw_chunked = NORM && chunked && p.norm_weight && (reinterpret_cast<uintptr_t>(p.norm_weight) & 15) == 0;
+    if constexpr (NORM) {
+        if (nw_chunked && warp < kConsumers) {
+#pragma unroll
+            for (int j = 0; j < kXC; ++j) {
+                const int c = tid + j * kConsumers * 32;
+                if (c < nx) {
+                    nwv[j][0] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c);
+                    nwv[j][1] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c + 1);
+                }
+            }
+        }
+    }
+
     if (tid == 0) {
         for (int s = 0; s < g.stages; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
@@ -178,24 +200,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
         // 16-bit x in 16-byte chunks (one load per 8 elements, all in flight
         // at once); the norm weights depend on nothing and load before the
         // wait for the previous kernel.
-        constexpr bool kX16 = Elem<XT>::bytes == 2 && VEC == 8;
-        constexpr int kXC = 8;  // chunks per thread: rows up to 8 * 8 * 256 elements
-        const bool chunked = kX16 && K <= int64_t(kXC) * 8 * kConsumers * 32 &&
-                             (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
-        float4 nwv[NORM ? kXC : 1][2];
-        const bool nw_chunked = NORM && chunked && p.norm_weight && (reinterpret_cast<uintptr_t>(p.norm_weight) & 15) == 0;
-        if constexpr (NORM) {
-            if (nw_chunked) {
-#pragma unroll
-                for (int j = 0; j < kXC; ++j) {
-                    const int c = tid + j * kConsumers * 32;
-                    if (c < nx) {
-                        nwv[j][0] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c);
-                        nwv[j][1] = __ldg(reinterpret_cast<const float4*>(p.norm_weight) + 2 * c + 1);
-                    }
-                }
-            }
-        }
         pdl_wait();
         float ss = 0.f;
         auto stage_scalar = [&]() {
