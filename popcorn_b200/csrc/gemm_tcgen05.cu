@@ -448,8 +448,8 @@ bool tcgen05_supports(const Matmul& p) {
 
 // Split-K for skinny (swapped) problems: a batched-decode GEMM has few
 // 128-row weight tiles (e.g. 8 for N = 1024), so whole-K tiles would stream
-// the weights from a handful of SMs. Partitions of >= 4 K tiles are added
-// until the (tile, partition) units cover the SMs. Returns the partition
+// the weights from a handful of SMs. The partition count (each >= 4 K tiles)
+// is chosen by the cost of its unit rounds (below). Returns the partition
 // count (1: no split) and the output-tile count and width.
 static int ksplit_plan(const Matmul& p, int64_t* tiles_out, int* bn_out) {
     if (p.M > 64) return 1;
@@ -459,12 +459,29 @@ static int ksplit_plan(const Matmul& p, int64_t* tiles_out, int* bn_out) {
     const int sms = current_sm_count();
     if (tiles_out) *tiles_out = tiles;
     if (bn_out) *bn_out = bn;
+    // Tiles that already cover half the SMs stream whole K (measured: a
+    // split of the 224-tile gate/up GEMM at TP1 was slower).
     if (tiles * 2 > sms || ktiles < 8) return 1;
-    int64_t ks = (sms + tiles - 1) / tiles;
-    if (ks > ktiles / 4) ks = ktiles / 4;
-    if (ks <= 1) return 1;
-    const int64_t kps = (ktiles + ks - 1) / ks;
-    return int((ktiles + kps - 1) / kps);  // no empty partition
+    // The partition count whose units finish soonest, in units of one K tile
+    // of streaming: rounds of SM-sized unit batches times (the unit's K
+    // tiles + its fp32 partial, about one K tile of bytes), plus the last
+    // partition's read of all the partials. A count that leaves a partial
+    // extra round costs a whole unit on the busiest SMs. Ties: fewer
+    // partitions.
+    int64_t best_ks = 1;
+    double best = 1e30;
+    for (int64_t ks = 1; ks <= ktiles / 4 && ks <= 64; ++ks) {
+        const int64_t kps = (ktiles + ks - 1) / ks;
+        const int64_t parts = (ktiles + kps - 1) / kps;  // no empty partition
+        const int64_t rounds = (tiles * parts + sms - 1) / sms;
+        const double t = parts == 1 ? double(rounds) * double(kps)
+                                    : double(rounds) * double(kps + 1) + double(parts);
+        if (t < best - 1e-9) {
+            best = t;
+            best_ks = parts;
+        }
+    }
+    return int(best_ks);
 }
 
 size_t matmul_tcgen05_workspace(const Matmul& p) {
