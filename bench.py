@@ -15,7 +15,12 @@ so every step streams them from HBM.
 At N > 1 (torchrun, one process per GPU) every rank runs its own replica
 (the config-2 decode path at batch 1 does not shard: replicas only);
 `value` is the tokens/s of all ranks together, timed as the max over ranks.
-Rank 0 prints one JSON line.
+The same line then carries the other BASELINE configs: at N = 1 the single
+FlashDecoding op (`fd_config1`), the 16-point FlashDecoding sweep
+(`fd_sweep`) and the prefill GEMM and attention (`prefill`); at every N the
+tensor-parallel 9B-shape decode at TP = N (`tp9b`: tok/s, per-role
+breakdown, all-reduce share, clocks and a peer-vs-NCCL parity check) — the
+scaling curve. Rank 0 prints one JSON line.
 """
 import argparse
 import json
