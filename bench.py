@@ -438,8 +438,14 @@ def tp9b_leg(args, world, rank, local):
     stream = torch.cuda.Stream(device=local)
 
     def all_reduce(t):
+        # the reference path of the parity check: NCCL sums the partials in
+        # fp32 and the sum is rounded once, as the peer kernel does (a bf16
+        # NCCL reduction rounds every partial sum of its ring, which differs
+        # from any single-rounding sum from 4 ranks on)
         if world > 1:
-            dist.all_reduce(t)
+            t32 = t.float()
+            dist.all_reduce(t32)
+            t.copy_(t32)
 
     def all_gather(blob):
         if world == 1:
@@ -488,7 +494,8 @@ def tp9b_leg(args, world, rank, local):
         # short chain of rounding points), then the full 42-layer model ----
         short = TPDecodeModel(pc.KernelLibrary(local), TPShape(layers=2), rank=rank, world=world, seed=5,
                               device=local)
-        parity = {"paths": "NCCL all-reduce + AddRMSNorm vs peer all-reduce fused with Add + RMSNorm",
+        parity = {"paths": "NCCL all-reduce (fp32 sum, one rounding) + AddRMSNorm vs peer all-reduce fused with "
+                           "Add + RMSNorm",
                   "argmax": "per rank over its vocabulary slice", "two_layer": parity_of(short)}
         del short
         torch.cuda.empty_cache()
