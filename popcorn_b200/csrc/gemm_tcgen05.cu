@@ -30,6 +30,8 @@
 
 #include <mutex>
 
+#include <atomic>
+
 #include "async.cuh"
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -512,6 +514,45 @@ cudaError_t matmul_tcgen05_allreduce(const Matmul& p, const PeerAllReduce& ar, c
     return matmul_tcgen05_impl(p, &ar, s);
 }
 
+// Split-K arrival counters of Matmul objects: each object owns a range
+// (gemm_reserve_counters). The last partition of a tile sets its counter
+// back to zero, and the array starts zeroed, so launches need no memset in
+// front of them (which would also end the programmatic overlap with the
+// previous kernel). Launches of ONE object that overlap on the GPU (two
+// streams, no ordering) would race on its range; a launch whose bounded
+// wait gave up (device error word set) may leave its counters non-zero.
+constexpr int kGemmCounters = 1 << 16;
+__device__ unsigned int g_gemm_counters[kGemmCounters];
+
+int gemm_reserve_counters(int64_t n) {
+    static std::atomic<int64_t> next{0};
+    if (n < 1 || n > kGemmCounters / 8) return -1;
+    int64_t start = next.fetch_add(n) % kGemmCounters;
+    if (start + n > kGemmCounters) start = 0;  // no range straddles the end
+    return int(start);
+}
+
+// Device address of g_gemm_counters on the current device (looked up once).
+static unsigned int* gemm_counters_here() {
+    static std::mutex lock;
+    static unsigned int* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> guard(lock);
+    if (!addr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_gemm_counters) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        addr[dev] = static_cast<unsigned int*>(ptr);
+    }
+    return addr[dev];
+}
+
 static cudaError_t matmul_tcgen05_impl(const Matmul& p, const PeerAllReduce* ar, cudaStream_t s) {
     // Skinny M: swap so the weight rows fill the 128-row MMA side.
     const bool swap = p.M <= 64;
@@ -545,10 +586,15 @@ static cudaError_t matmul_tcgen05_impl(const Matmul& p, const PeerAllReduce* ar,
         if (ks > 1) {
             g.ksplit = ks;
             g.ws = static_cast<float*>(p.workspace);
-            g.cnt = reinterpret_cast<unsigned int*>(static_cast<char*>(p.workspace) +
-                                                    size_t(tiles) * ks * bn * kBM * 4);
-            cudaError_t e = cudaMemsetAsync(g.cnt, 0, size_t(tiles) * 4, s);
-            if (e != cudaSuccess) return e;
+            unsigned int* own = p.ctr_base >= 0 && p.ctr_base + tiles <= kGemmCounters ? gemm_counters_here() : nullptr;
+            if (own) {
+                g.cnt = own + p.ctr_base;  // zero between launches
+            } else {
+                g.cnt = reinterpret_cast<unsigned int*>(static_cast<char*>(p.workspace) +
+                                                        size_t(tiles) * ks * bn * kBM * 4);
+                cudaError_t e = cudaMemsetAsync(g.cnt, 0, size_t(tiles) * 4, s);
+                if (e != cudaSuccess) return e;
+            }
         }
     }
     switch (p.c_dtype) {

@@ -97,7 +97,10 @@ struct Matmul {
     int64_t M, K, N;
     int transpose_b;
     void* workspace = nullptr;  // tcgen05 split-K partials (matmul_tcgen05_workspace bytes) or null
+    int ctr_base = -1;          // split-K arrival counters reserved by gemm_reserve_counters (-1: zeroed per launch)
 };
+// Reserves `n` split-K arrival counters for one Matmul object; -1 when none.
+int gemm_reserve_counters(int64_t n);
 cudaError_t matmul(const Matmul& p, cudaStream_t stream);
 // True when the tcgen05 tensor-core GEMM serves this problem.
 bool matmul_uses_tensor_cores(const Matmul& p);

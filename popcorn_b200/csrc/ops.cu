@@ -305,12 +305,16 @@ public:
                                                                dtype_name(ad) + ", " + dtype_name(bd) + ", " +
                                                                dtype_name(cd) + ".");
         launch::Matmul p = params();
+        if (m <= 64 && launch::matmul_uses_tensor_cores(p))
+            ctr_base_ = launch::gemm_reserve_counters(2 * ((n + 127) / 128));  // >= the split-K tile count
         function_names_ = !launch::matmul_uses_tensor_cores(p) ? "matmul"
                           : p.transpose_b                       ? "matmul_tc_bf16_tb"
                                                                 : "matmul_tc_bf16_nn";
     }
     launch::Matmul params() const {
-        return launch::Matmul{a_.data(), a_.dtype(), b_.data(), b_.dtype(), c_.data(), c_.dtype(), m_, k_, n_, tb_ ? 1 : 0};
+        launch::Matmul p{a_.data(), a_.dtype(), b_.data(), b_.dtype(), c_.data(), c_.dtype(), m_, k_, n_, tb_ ? 1 : 0};
+        p.ctr_base = ctr_base_;
+        return p;
     }
     const char* name() const override { return "Matmul"; }
     void set_prefetch(int slot, const void* ptr, uint64_t bytes) override {
@@ -356,6 +360,7 @@ private:
     bool tb_;
     bool gemv_ = false;
     launch::L2Prefetch pf_{};
+    int ctr_base_ = -1;
 };
 
 // ---------------------------------------------------------------------------
