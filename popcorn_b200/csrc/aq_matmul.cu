@@ -110,86 +110,97 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) { return float_to_bf16_bi
 // x of tokens [m0, m0 + mt) and groups [c0, c0 + cg) into shared memory, as
 // the B pairs of x_pairs: per (group j, token n, part, plane, thread t) one
 // 16-byte vector (plane 0: b0-b3, plane 1: b4-b7; part 1: the lo half of an
-// f32 x), and the groups' sums sum(x) (fp32, in k order) per (j, n). All
-// `nthreads` threads from `tid` take part; the caller synchronises.
+// f32 x), and the groups' sums sum(x) (fp32) per (j, n). One unit is a
+// quarter group (16 values, thread slot t) so that four threads share a
+// group and all its loads are in flight at once; the quarters' sums meet by
+// shuffles within the four lanes (the same order on each lane). All
+// `nthreads` threads (a multiple of 4) from `tid` take part; the caller
+// synchronises.
 //
 // nscale (optional, fused RMSNorm): token n's value k is staged as
-// round((x * nscale[n]) * w[k]) in x's type — what RMSNorm would have stored
-// (RMSNorm.metal:7-42) — and the group sums are of those values.
+// round((x * nscale[n]) * nw[k]) in x's type, nw[k] the norm weight (plus
+// one when the form asks for it, no weight: 1) as RMSNorm applies it — what
+// RMSNorm would have stored (RMSNorm.metal:7-42) — and the group sums are of
+// those values.
 template <class XT>
-__device__ __forceinline__ float norm_value(const AqMatmul& p, float v, float scale, int64_t k) {
+__device__ __forceinline__ float norm_value(float v, float scale, const float* nw, int64_t k) {
     v *= scale;
-    if (p.norm_weight) v *= p.add_one ? 1.0f + p.norm_weight[k] : p.norm_weight[k];
+    if (nw) v *= nw[k];
     return Elem<XT>::round(v);
 }
 
 template <class XT>
 __device__ __forceinline__ void stage_x(const AqMatmul& p, int64_t m0, int mt, int64_t c0, int cg, uint4* xs,
-                                        float* sxs, int tid, int nthreads, const float* nscale = nullptr) {
+                                        float* sxs, int tid, int nthreads, const float* nscale = nullptr,
+                                        const float* nw = nullptr) {
     constexpr bool XF32 = std::is_same<XT, TF32>::value;
     constexpr int NP = XF32 ? 2 : 1;
     auto at = [&](int j, int n, int part, int plane, int tt) -> uint4& {
         return xs[((((size_t(j) * mt + n) * NP + part) * 2 + plane) * 4) + tt];
     };
-    for (int u = tid; u < cg * mt; u += nthreads) {
-        const int j = u / mt, n = u % mt;
-        const char* src = static_cast<const char*>(p.x) + ((m0 + n) * p.K + (c0 + j) * 64) * Elem<XT>::bytes;
+    // the unit count is a multiple of 4 and so is nthreads: a quad of lanes
+    // runs the same iterations
+    const unsigned quad = 0xFu << (threadIdx.x & 28);
+    for (int u = tid; u < 4 * cg * mt; u += nthreads) {
+        const int tt = u & 3, jn = u >> 2;
+        const int j = jn / mt, n = jn % mt;
+        const int64_t k0 = (c0 + j) * 64 + tt * 16;
+        const char* src = static_cast<const char*>(p.x) + ((m0 + n) * p.K + k0) * Elem<XT>::bytes;
         float sx = 0.f;
+        uint32_t b[8];
+        if constexpr (!XF32) {
+            const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(src));
+            const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(src) + 1);
+            uint32_t q[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
-        for (int tt = 0; tt < 4; ++tt) {
-            uint32_t b[8];
-            if constexpr (!XF32) {
-                const uint4 l0 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * tt);
-                const uint4 l1 = __ldg(reinterpret_cast<const uint4*>(src) + 2 * tt + 1);
-                uint32_t q[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float2 f = unpack2<XT>(q[i]);
-                    if (nscale) {
-                        const int64_t k = (c0 + j) * 64 + tt * 16 + 2 * i;
-                        f.x = norm_value<XT>(p, f.x, nscale[n], k);
-                        f.y = norm_value<XT>(p, f.y, nscale[n], k + 1);
-                        q[i] = pack2<XT>(f.x, f.y);
-                    }
-                    sx += f.x;
-                    sx += f.y;
+            for (int i = 0; i < 8; ++i) {
+                float2 f = unpack2<XT>(q[i]);
+                if (nscale) {
+                    f.x = norm_value<XT>(f.x, nscale[n], nw, k0 + 2 * i);
+                    f.y = norm_value<XT>(f.y, nscale[n], nw, k0 + 2 * i + 1);
+                    q[i] = pack2<XT>(f.x, f.y);
                 }
-                x_pairs(q, b);
-                at(j, n, 0, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
-                at(j, n, 0, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
-            } else {
-                uint32_t qh[8], ql[8];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 f = __ldg(reinterpret_cast<const float4*>(src) + 4 * tt + i);
-                    float e[4] = {f.x, f.y, f.z, f.w};
-                    if (nscale)
-#pragma unroll
-                        for (int h = 0; h < 4; ++h)
-                            e[h] = norm_value<XT>(p, e[h], nscale[n], (c0 + j) * 64 + tt * 16 + 4 * i + h);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const float e0 = e[2 * h], e1 = e[2 * h + 1];
-                        const uint32_t h0 = bf16_bits(e0), h1 = bf16_bits(e1);
-                        const uint32_t l0 = bf16_bits(e0 - __uint_as_float(h0 << 16));
-                        const uint32_t l1 = bf16_bits(e1 - __uint_as_float(h1 << 16));
-                        qh[2 * i + h] = h0 | (h1 << 16);
-                        ql[2 * i + h] = l0 | (l1 << 16);
-                        // the sum of what the MMAs multiply (hi + lo), so the
-                        // offset term cancels exactly
-                        sx += __uint_as_float(h0 << 16) + __uint_as_float(l0 << 16);
-                        sx += __uint_as_float(h1 << 16) + __uint_as_float(l1 << 16);
-                    }
-                }
-                x_pairs(qh, b);
-                at(j, n, 0, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
-                at(j, n, 0, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
-                x_pairs(ql, b);
-                at(j, n, NP - 1, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
-                at(j, n, NP - 1, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
+                sx += f.x;
+                sx += f.y;
             }
+            x_pairs(q, b);
+            at(j, n, 0, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
+            at(j, n, 0, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
+        } else {
+            uint32_t qh[8], ql[8];
+            float4 f4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) f4[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float e[4] = {f4[i].x, f4[i].y, f4[i].z, f4[i].w};
+                if (nscale)
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) e[h] = norm_value<XT>(e[h], nscale[n], nw, k0 + 4 * i + h);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float e0 = e[2 * h], e1 = e[2 * h + 1];
+                    const uint32_t h0 = bf16_bits(e0), h1 = bf16_bits(e1);
+                    const uint32_t l0 = bf16_bits(e0 - __uint_as_float(h0 << 16));
+                    const uint32_t l1 = bf16_bits(e1 - __uint_as_float(h1 << 16));
+                    qh[2 * i + h] = h0 | (h1 << 16);
+                    ql[2 * i + h] = l0 | (l1 << 16);
+                    // the sum of what the MMAs multiply (hi + lo), so the
+                    // offset term cancels exactly
+                    sx += __uint_as_float(h0 << 16) + __uint_as_float(l0 << 16);
+                    sx += __uint_as_float(h1 << 16) + __uint_as_float(l1 << 16);
+                }
+            }
+            x_pairs(qh, b);
+            at(j, n, 0, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
+            at(j, n, 0, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
+            x_pairs(ql, b);
+            at(j, n, NP - 1, 0, tt) = make_uint4(b[0], b[1], b[2], b[3]);
+            at(j, n, NP - 1, 1, tt) = make_uint4(b[4], b[5], b[6], b[7]);
         }
-        sxs[j * mt + n] = sx;
+        sx += __shfl_xor_sync(quad, sx, 1);
+        sx += __shfl_xor_sync(quad, sx, 2);
+        if (tt == 0) sxs[j * mt + n] = sx;
     }
 }
 
@@ -465,6 +476,10 @@ __global__ void __launch_bounds__(kQThreads, 1)
     float* parts = reinterpret_cast<float*>(q_smem + size_t(kQWarps) * kQSlots * (kQSegBytes + 256));
     uint4* xs = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(parts) + size_t(ts_count) * q.ks * 512);
     float* sxs = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + size_t(G) * q.mt * NP * 128);
+    // fused RMSNorm: the norm weights [K] and the quarter-group sums of
+    // squares [mt][G][4]
+    float* nws = sxs + size_t(G) * q.mt;
+    float* nsq = nws + (p.norm_weight ? p.K : 0);
     const int64_t m0 = int64_t(blockIdx.z) * q.mt;
     const int mt = ONE ? 1 : int(p.M - m0 < q.mt ? p.M - m0 : q.mt);
 
@@ -513,46 +528,57 @@ __global__ void __launch_bounds__(kQThreads, 1)
     if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
     __syncwarp();
     for (int i = 0; i < kQAhead; ++i) issue();
+    // the norm weights are parameters, never written by the previous kernel:
+    // loaded before the wait on it (made visible by the barrier after the
+    // sums of squares)
+    if (p.norm && p.norm_weight)
+        for (int k = tid; k < int(p.K); k += kQThreads) nws[k] = p.add_one ? 1.0f + p.norm_weight[k] : p.norm_weight[k];
 
     pdl_wait();
     if (p.norm) {
-        // fused RMSNorm: token n's scale rsqrt(mean(x^2) + eps). Each (group,
-        // token) unit's sum of squares goes to the sums area first (one
-        // 16-byte load per 8 values, all in flight at once), then summed in
-        // group order; the staging pass below re-reads x from L1.
-        for (int u = tid; u < int(G) * mt; u += kQThreads) {
-            const int j = u / mt, n = u % mt;
-            const char* src = static_cast<const char*>(p.x) + ((m0 + n) * p.K + int64_t(j) * 64) * Elem<XT>::bytes;
+        // fused RMSNorm: token n's scale rsqrt(mean(x^2) + eps). The sums of
+        // squares of quarter groups (16 values, two 16-byte loads, all in
+        // flight) go to the sums area, then one warp per token adds its
+        // quarters (lane-strided, then a butterfly: every lane the same
+        // value); the staging pass below re-reads x from L1.
+        float* sq = nsq;
+        for (int u = tid; u < 4 * int(G) * mt; u += kQThreads) {
+            const int tt = u & 3, jn = u >> 2;
+            const int j = jn / mt, n = jn % mt;
+            const char* src =
+                static_cast<const char*>(p.x) + ((m0 + n) * p.K + int64_t(j) * 64 + tt * 16) * Elem<XT>::bytes;
             float ss = 0.f;
             if constexpr (!XF32) {
-                uint4 c[8];
+                const uint4 c0 = __ldg(reinterpret_cast<const uint4*>(src));
+                const uint4 c1 = __ldg(reinterpret_cast<const uint4*>(src) + 1);
+                float f[8];
+                unpack8<XT>(c0, f);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) c[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+                for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+                unpack8<XT>(c1, f);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float f[8];
-                    unpack8<XT>(c[i], f);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
-                }
+                for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
             } else {
-                float4 c[16];
+                float4 c[4];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) c[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
+                for (int i = 0; i < 4; ++i) c[i] = __ldg(reinterpret_cast<const float4*>(src) + i);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) ss += c[i].x * c[i].x + c[i].y * c[i].y + c[i].z * c[i].z + c[i].w * c[i].w;
+                for (int i = 0; i < 4; ++i) ss += c[i].x * c[i].x + c[i].y * c[i].y + c[i].z * c[i].z + c[i].w * c[i].w;
             }
-            sxs[j * mt + n] = ss;
+            sq[(n * int(G) + j) * 4 + tt] = ss;
         }
         __syncthreads();
-        if (tid < mt) {
+        if (warp < mt) {
             float ss = 0.f;
-            for (int j = 0; j < int(G); ++j) ss += sxs[j * mt + tid];
-            nscale[tid] = rsqrtf(ss / float(p.K) + p.eps);
+            for (int i = lane; i < 4 * int(G); i += 32) ss += sq[warp * 4 * int(G) + i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) nscale[warp] = rsqrtf(ss / float(p.K) + p.eps);
         }
         __syncthreads();
     }
-    stage_x<XT>(p, m0, mt, 0, int(G), xs, sxs, tid, kQThreads, p.norm ? nscale : nullptr);
+    stage_x<XT>(p, m0, mt, 0, int(G), xs, sxs, tid, kQThreads, p.norm ? nscale : nullptr,
+                p.norm && p.norm_weight ? nws : nullptr);
     __syncthreads();  // x staged, barriers and partial slots initialised
     // per-thread shared offsets: the weights' swizzled 8-byte word pair of
     // group jl of a segment (row g; row g + 8 is 1 KB further), and x
@@ -765,15 +791,17 @@ bool aq_tma_plan(const AqMatmul& p, AqTmaPlan& q) {
     while (q.ks < kQWarps && tiles * q.ks < int64_t(sms) * kQWarps && 2 * q.ks <= nseg) q.ks *= 2;
     const size_t fixed =
         size_t(kQWarps) * kQSlots * (kQSegBytes + 256) + size_t(2 * (kQWarps / q.ks)) * q.ks * 512;
-    const size_t budget = 220 * 1024 - fixed;
-    const size_t per_token = size_t(G) * ((p.x_dtype == PC_F32 ? 2 : 1) * 128 + 4);
+    const size_t norm_fixed = p.norm && p.norm_weight ? size_t(p.K) * 4 : 0;  // norm weights
+    if (fixed + norm_fixed >= 220 * 1024) return false;
+    const size_t budget = 220 * 1024 - fixed - norm_fixed;
+    const size_t per_token = size_t(G) * ((p.x_dtype == PC_F32 ? 2 : 1) * 128 + 4 + (p.norm ? 16 : 0));
     int64_t mt = int64_t(budget / per_token);
     if (mt > 8) mt = 8;
     if (mt > p.M) mt = p.M;
     if (mt < 1) return false;
     q.mt = int(mt);
     q.mtiles = int((p.M + mt - 1) / mt);
-    q.smem = fixed + size_t(G) * q.mt * ((p.x_dtype == PC_F32 ? 2 : 1) * 128 + 4);
+    q.smem = fixed + norm_fixed + size_t(q.mt) * per_token;
     return true;
 }
 

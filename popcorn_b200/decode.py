@@ -453,6 +453,9 @@ class AqDecodeStack(DecodeStack):
                                          add_one_to_weight=self.norm_add_one, norm_v=True))
         ks.append(Kernels.FlashDecodingRagged(self.q, w.k_cache, w.v_cache, lens, into=self.attn, scale=s.scale,
                                               mask=AttentionMask.causal))
+        if self.kv_early:
+            # the kernel before it writes only the newest K/V row
+            ks[-1].set_hint(Kernels.FlashDecodingRagged.HINT_KV_EARLY)
         ks.append(Kernels.AqMatmulResidual(self.attn.view(1, s.Nq * s.Hd), w.w_o, cur, into=self.h))
         ks.append(Kernels.AqGatedMLP(self.h, w.mlp_norm, w.w_gate_up, into=self.act, eps=s.eps,
                                      add_one_to_weight=self.norm_add_one, activation=s.activation))
