@@ -413,7 +413,7 @@ __device__ __forceinline__ void aq_epilogue(const AqMatmul& p, int tile, int g, 
 // One CTA per SM, sixteen warps, each an independent stream: a warp takes
 // units (16-row tile, K slice) in turn and feeds itself with 3-D TMA copies
 // (no multicast) of one 256-value segment of its 16 rows (2 KB) into a
-// private four-slot ring, three segments ahead of the one it multiplies. The
+// private two-slot ring, one segment ahead of the one it multiplies. The
 // packed matrix is viewed as [32 words][N rows][K/256 segments]; the 128-byte
 // swizzle makes the 8-byte loads of eight different rows conflict-free. The
 // four scales (and biases) of a row's segment are 8 contiguous bytes: the
@@ -424,7 +424,11 @@ __device__ __forceinline__ void aq_epilogue(const AqMatmul& p, int tile, int g, 
 // once per CTA (its token tile).
 constexpr int kQWarps = 16;
 constexpr int kQThreads = kQWarps * 32;
-constexpr int kQSlots = 4;       // ring slots per warp
+// Two slots: 16 warps x 2 copies of 2 KB in flight per SM. More copies in
+// flight stream SLOWER on B200 (a per-warp TMA ring with no arithmetic:
+// 2 x 2 KB and 3 x 2 KB per warp 6.35-6.5 TB/s, 4 x 2 KB 4.7 TB/s, 6 x 2 KB
+// 3.4 TB/s), and this kernel's warps are busy issuing their arithmetic.
+constexpr int kQSlots = 2;       // ring slots per warp
 constexpr int kQAhead = kQSlots - 1;
 constexpr int kQSegBytes = 2048;  // 16 rows x 128 B
 
@@ -599,7 +603,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int tile = cc.tile, k = cc.k, v = cc.v;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         while (cc.valid && cc.v == v) {
-            issue();  // keep three segments in flight
+            issue();  // keep kQAhead segments in flight
             const int slot = consumed % kQSlots;
             if (!mbar_wait(smem_u32(&full[warp][slot]), uint32_t(consumed / kQSlots) & 1u, &g_aq_error_word)) {
                 ok = false;
