@@ -12,7 +12,7 @@
 // per 2 FLOPs. One persistent CTA per SM: a producer warp streams 8-row x
 // kc-column weight tiles HBM -> shared memory with 1-D bulk copies
 // (cp.async.bulk, no multicast) into a 2-8 stage mbarrier ring of up to
-// ~190 KB, starting before griddepcontrol.wait (weights never depend on the
+// ~150 KB (short matvecs) or ~190 KB (long ones), starting before griddepcontrol.wait (weights never depend on the
 // previous kernel, so under programmatic dependent launch the stream starts
 // while that kernel drains). Eight consumer warps own one weight row each
 // per stage; the activation row is converted to fp32 once per CTA into
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const Gemv p, 
 
     // The norm weights depend on nothing: the consumers request them before
     // the producer issues the ring's bulk copies, so they do not queue
-    // behind ~190 KB of weight traffic on this SM.
+    // behind the ring's weight traffic on this SM.
     constexpr bool kX16 = Elem<XT>::bytes == 2 && VEC == 8;
     constexpr int kXC = 8;  // chunks per thread: rows up to 8 * 8 * 256 elements
     const bool chunked = kX16 && K <= int64_t(kXC) * 8 * kConsumers * 32 &&
