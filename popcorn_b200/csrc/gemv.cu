@@ -457,6 +457,14 @@ size_t gemv_smem_override() {
 // GEMV keeps the deeper ring (203 vs 206 us).
 constexpr int kShortTilesPerCta = 32;
 constexpr size_t kShortBudget = 150 * 1024;
+// POPCORN_GEMV_SHORT_TILES overrides kShortTilesPerCta (tuning).
+int short_tiles_per_cta() {
+    static const int v = [] {
+        const char* e = getenv("POPCORN_GEMV_SHORT_TILES");
+        return e ? atoi(e) : kShortTilesPerCta;
+    }();
+    return v;
+}
 
 bool make_plan(const Gemv& p, GemvPlan& g) {
     const int es = dtype_stride(p.w_dtype);
@@ -474,7 +482,7 @@ bool make_plan(const Gemv& p, GemvPlan& g) {
     size_t xbytes = size_t(K) * 4;
     const int sms = current_sm_count();
     size_t budget = gemv_smem_override();
-    if (budget == 0) budget = (g.ntiles + sms - 1) / sms <= kShortTilesPerCta ? kShortBudget : kTmaSmemBudget;
+    if (budget == 0) budget = (g.ntiles + sms - 1) / sms <= short_tiles_per_cta() ? kShortBudget : kTmaSmemBudget;
     if (xbytes + 2 * size_t(g.stage_bytes) > budget) return false;
     g.stages = int((budget - xbytes) / g.stage_bytes);
     if (g.stages > 8) g.stages = 8;
