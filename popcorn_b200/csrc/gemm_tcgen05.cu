@@ -52,7 +52,14 @@ using namespace tc;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle atom of 16-bit elements
-constexpr int kStages = 4;
+// Operand ring depth: 4 stages; the skinny (decode-batch) tiles, whose
+// stages are mostly weight bytes, stream with a deeper ring (6 stages of
+// 16 + 4 KB: config-5 TP1 step 21.095 -> 21.04 ms; 8 stages 21.03).
+constexpr int kSkinnyStages = 6;
+template <int BN>
+constexpr int gemm_stages() {
+    return BN <= 64 ? kSkinnyStages : 4;
+}
 
 struct GemmArgs {
     void* c;
@@ -88,6 +95,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
     constexpr int ES = int(sizeof(typename CT::storage));
     constexpr int BOX = 32 * 32 * ES;
+    constexpr int kStages = gemm_stages<BN>();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tfull[2], tempty[2];
     __shared__ uint32_t s_tmem;
@@ -408,6 +416,7 @@ template <int BN, class CT>
 cudaError_t launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& g,
                       cudaStream_t s) {
     auto kern = gemm_tcgen05_kernel<BN, CT>;
+    constexpr int kStages = gemm_stages<BN>();
     constexpr size_t smem = size_t(kStages) * (kBM * kBK * 2 + BN * kBK * 2) +
                             size_t(kEpiWarps) * 32 * 32 * sizeof(typename CT::storage) + 1024;
     static bool configured = false;
