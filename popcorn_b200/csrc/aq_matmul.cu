@@ -631,13 +631,17 @@ __global__ void __launch_bounds__(kQThreads, 1)
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 group_mma<F16, NP>(wa.x, wa.y, wb.x, wb.y, xl, xl + 4, true, d);
                 // D = sum x (kOff + q): acc += scale * D + (bias - kOff * scale) * sum(x)
-                const float k0 = fmaf(-kOff, sc0[jl], bi0[jl]), k1 = fmaf(-kOff, sc1[jl], bi1[jl]);
                 if constexpr (ONE) {
-                    // accumulator columns 2t, 2t + 1: only t == 0, column 0 is a token
+                    // accumulator columns 2t, 2t + 1: only t == 0, column 0 is
+                    // a token. The offset leaves D inside one fma (D - kOff *
+                    // sum(x) = sum x q, the only rounding that of the small
+                    // result), then acc += scale * that + bias * sum(x).
                     const float sxa = jl == 0 ? sx4.x : jl == 1 ? sx4.y : jl == 2 ? sx4.z : sx4.w;
-                    acc[0] += fmaf(sc0[jl], d[0], k0 * sxa);
-                    acc[2] += fmaf(sc1[jl], d[2], k1 * sxa);
+                    const float e0 = fmaf(-kOff, sxa, d[0]), e2 = fmaf(-kOff, sxa, d[2]);
+                    acc[0] = fmaf(sc0[jl], e0, fmaf(bi0[jl], sxa, acc[0]));
+                    acc[2] = fmaf(sc1[jl], e2, fmaf(bi1[jl], sxa, acc[2]));
                 } else {
+                    const float k0 = fmaf(-kOff, sc0[jl], bi0[jl]), k1 = fmaf(-kOff, sc1[jl], bi1[jl]);
                     const float sxa = 2 * t < mt ? sxs[j * mt + 2 * t] : 0.f;
                     const float sxb = 2 * t + 1 < mt ? sxs[j * mt + 2 * t + 1] : 0.f;
                     acc[0] += fmaf(sc0[jl], d[0], k0 * sxa);
